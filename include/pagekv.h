@@ -1,0 +1,203 @@
+/*
+ * pagekv.h - C ABI of libpagekv, a B200 (sm_100a) implementation of pagellm's paged
+ * KV-cache hot path (pagellm: src/pagellm/cache/paged.py).
+ *
+ * Conventions
+ *   - Every entry point returns an int status (PK_OK = 0). On failure a message is
+ *     available from pk_last_error() (thread-local, valid until the next failing call).
+ *   - "dev" pointers are CUDA device pointers on the pool's device; "host" pointers are
+ *     ordinary host memory (pinned memory makes the copies asynchronous).
+ *   - stream is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Calls are asynchronous with respect to the host unless stated otherwise.
+ *   - Query / key / value / output rows are float32, row-major:
+ *       q, out: [rows][n_heads][head_dim]     k, v: [rows][n_kv_heads][head_dim]
+ *   - The pool stores K and V as [layers][num_blocks][block_size][n_kv_heads][head_dim]
+ *     in float32 or bfloat16; a token's slot is block * block_size + offset.
+ *   - The library keeps no global state besides the thread-local error message and
+ *     needs no locking for the single-engine-thread use pagellm makes of its cache.
+ */
+#ifndef PAGEKV_H
+#define PAGEKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(PK_BUILD)
+#define PK_API __attribute__((visibility("default")))
+#else
+#define PK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum pk_status {
+    PK_OK = 0,
+    PK_ERR_INVALID_ARG = 1,   /* bad shape / dtype / pointer: pagellm raises ValueError   */
+    PK_ERR_OUT_OF_RANGE = 2,  /* block id, slot or position outside the pool or table     */
+    PK_ERR_CUDA = 3,          /* a CUDA runtime call failed                                 */
+    PK_ERR_OUT_OF_BLOCKS = 4, /* free list and evictable set empty: pagellm's OutOfBlocks   */
+    PK_ERR_DOUBLE_FREE = 5,   /* decref of a block whose ref count is 0                     */
+    PK_ERR_TIMEOUT = 6,       /* a bounded device-side wait gave up (kernel returned early) */
+    PK_ERR_DUPLICATE = 7,     /* sequence id already has a table                            */
+    PK_ERR_NOT_FOUND = 8,     /* unknown sequence id                                        */
+    PK_ERR_UNSUPPORTED = 9    /* configuration this build does not handle                   */
+};
+
+enum pk_dtype { PK_F32 = 0, PK_BF16 = 1 };
+
+typedef struct pk_pool pk_pool;
+typedef struct pk_batch pk_batch;
+typedef struct pk_block_manager pk_block_manager;
+
+/* Message of the last failing call on this thread ("" if none). */
+PK_API const char* pk_last_error(void);
+/* ABI version: bumped on any incompatible change. */
+PK_API int pk_abi_version(void);
+
+/* ---------------------------------------------------------------- pool
+ * Replaces PagedKVPool (cache/paged.py:282-300). K and V are allocated on `device`
+ * and zero-filled, as pagellm's np.zeros pool is. */
+PK_API int pk_pool_create(int n_layers, int64_t num_blocks, int block_size, int n_kv_heads,
+                   int head_dim, int dtype, int device, pk_pool** out);
+PK_API int pk_pool_destroy(pk_pool* pool);
+/* Device base pointers of K and V and the total bytes (PagedKVPool.nbytes, :298-300). */
+PK_API int pk_pool_buffers(const pk_pool* pool, void** k_dev, void** v_dev, int64_t* nbytes);
+/* Whether the tensor-core attention kernel serves this pool (bf16, head_dim 64/128/256,
+ * block_size a multiple of 16, <= 8 KV heads), its shared-memory layout and pipeline depth,
+ * and why not when it does not. */
+PK_API int pk_pool_tc_info(const pk_pool* pool, int* enabled, int* per_head_layout, int* stages,
+                    const char** why);
+/* Copy-on-write block copies over all layers (PagedKVPool.copy_block, :294-296, driven by
+ * engine/llm_engine.py:205-206). pairs_host: npairs (src, dst) int64 pairs, applied as if
+ * in list order. Ids are checked on the host before anything is launched. */
+PK_API int pk_pool_copy_blocks(pk_pool* pool, const int64_t* pairs_host, int64_t npairs, void* stream);
+/* Same, with the pairs already on the device (no validation beyond npairs >= 0;
+ * every id must be in [0, num_blocks) and no dst may also be a src). */
+PK_API int pk_pool_copy_blocks_dev(pk_pool* pool, const int64_t* pairs_dev, int64_t npairs,
+                            void* stream);
+/* Scatter rows into one layer at the given slots (PagedBatch.write_and_attend,
+ * :443-444): pool.k_flat[layer, slots] = k. k_dev/v_dev float32 [n][n_kv_heads][head_dim];
+ * slots_dev int64. Slots are not range-checked here (pk_batch_plan checks its own). */
+PK_API int pk_pool_append(pk_pool* pool, int layer, const float* k_dev, const float* v_dev,
+                   const int64_t* slots_dev, int64_t n, void* stream);
+
+/* slot_mapping (cache/paged.py:303-306): slots[i] = table[p / bs] * bs + p % bs for
+ * p = positions[i]. Device arrays. A position outside [0, table_len * bs) yields slot
+ * -1 and, if err_dev is not NULL, sets *err_dev to 1. */
+PK_API int pk_slot_mapping(const int32_t* table_dev, int64_t table_len, const int64_t* positions_dev,
+                    int64_t n, int block_size, int64_t* slots_dev, int32_t* err_dev,
+                    void* stream);
+
+/* ---------------------------------------------------------------- batch
+ * Replaces PagedBatch (cache/paged.py:383-464): the per-step view of a set of sequences.
+ * A batch object is reusable across steps; its device buffers only grow. */
+PK_API int pk_batch_create(pk_pool* pool, pk_batch** out);
+PK_API int pk_batch_destroy(pk_batch* batch);
+/* PagedBatch.__init__ (:397-439). Host arrays: block tables in CSR form
+ * (table_indptr[nseq+1] int64, table_ids int32), starts[nseq], n_new[nseq] (int64).
+ * Sequence i owns rows offsets[i] .. offsets[i]+n_new[i]-1 at positions starts[i]...
+ * Validates every table (ids in range, long enough for starts[i]+n_new[i] tokens), uploads
+ * it, computes positions and slots on the device and plans the attention kernels.
+ * Returns the number of rows in *n_rows. */
+PK_API int pk_batch_plan(pk_batch* batch, int nseq, const int64_t* table_indptr,
+                  const int32_t* table_ids, const int64_t* starts, const int64_t* n_new,
+                  int64_t* n_rows, void* stream);
+/* Device pointers of the step's int64 positions and slots (valid until the next plan). */
+PK_API int pk_batch_rows(const pk_batch* batch, const int64_t** positions_dev, const int64_t** slots_dev);
+/* PagedBatch.write_and_attend (:441-464) for one layer: append k/v at the step's slots,
+ * then causal GQA attention of every row over its sequence's cached prefix plus the
+ * step's own rows. q_dev/out_dev [rows][n_heads][head_dim], k_dev/v_dev
+ * [rows][n_kv_heads][head_dim], float32, device. */
+PK_API int pk_batch_write_and_attend(pk_batch* batch, int layer, int n_heads, const float* q_dev,
+                              const float* k_dev, const float* v_dev, float* out_dev,
+                              void* stream);
+/* Attention only (no append): the read half of write_and_attend. */
+PK_API int pk_batch_attend(pk_batch* batch, int layer, int n_heads, const float* q_dev, float* out_dev,
+                    void* stream);
+/* write_and_attend from HOST buffers: uploads q/k/v, runs the layer and downloads out,
+ * all on `stream`; returns after `out_host` is filled (synchronous). */
+PK_API int pk_batch_write_and_attend_host(pk_batch* batch, int layer, int n_heads, const float* q_host,
+                                   const float* k_host, const float* v_host, float* out_host,
+                                   void* stream);
+/* Reads (and clears) the device error word that bounded waits set on timeout.
+ * Synchronises `stream`. Returns PK_ERR_TIMEOUT if any kernel of this batch gave up. */
+PK_API int pk_batch_check(pk_batch* batch, void* stream);
+/* Planning statistics of the last plan: [0] rows, [1] sequences on the tensor-core split-KV
+ * kernel, [2] its CTAs, [3] its total K/V blocks, [4] split sequences needing the merge
+ * kernel, [5] rows on the CUDA-core kernel, [6] kernels launched per write_and_attend. */
+PK_API int pk_batch_stats(const pk_batch* batch, int64_t* stats7);
+
+/* Host-only dry run of the split-KV planner (no device needed): given per-unit block
+ * counts, returns for each CTA its first block [ncta+1] (ncta = min(total, max_ctas)). */
+PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,
+                      int64_t* cta_first_block, int* ncta);
+
+
+/* ---------------------------------------------------------------- block bookkeeping
+ * Host-side replacement of BlockAllocator and BlockManager (cache/paged.py:47-274): FIFO
+ * free list, int64 ref counts, LRU set of evictable cached blocks, hash -> block map and
+ * per-sequence tables, in C++. Hashing (block_hash chains, paged.py:120-131) stays with the
+ * caller, which passes digests as (bytes, length). No CUDA involved; messages of failing
+ * calls come from pk_bm_last_error(). */
+PK_API const char* pk_bm_last_error(void);
+PK_API int pk_bm_create(int64_t num_blocks, int block_size, int enable_prefix_caching,
+                        pk_block_manager** out);
+PK_API int pk_bm_destroy(pk_block_manager* m);
+/* BlockAllocator.allocate / incref / decref / lookup / register (paged.py:73-117).
+ * allocate -> PK_ERR_OUT_OF_BLOCKS when nothing is free or evictable; decref of a block with
+ * ref 0 -> PK_ERR_DOUBLE_FREE; incref of an unreferenced block that is not cached ->
+ * PK_ERR_NOT_FOUND; lookup writes -1 when the hash is unknown or caching is off. */
+PK_API int pk_bm_allocate_block(pk_block_manager* m, int32_t* block);
+PK_API int pk_bm_incref(pk_block_manager* m, int32_t block);
+PK_API int pk_bm_decref(pk_block_manager* m, int32_t block);
+PK_API int pk_bm_lookup(pk_block_manager* m, const uint8_t* hash, int64_t len, int32_t* block);
+PK_API int pk_bm_register(pk_block_manager* m, int32_t block, const uint8_t* hash, int64_t len);
+/* [0] num_free (paged.py:63-66), [1] free-list length, [2] evictable, [3] cached hashes,
+ * [4] prefix_hits, [5] prefix_queries, [6] sequences with a table. */
+PK_API int pk_bm_counts(const pk_block_manager* m, int64_t* counts7);
+/* Live pointer to the int64 ref counts (BlockAllocator.ref, paged.py:54). */
+PK_API int pk_bm_refcounts(pk_block_manager* m, int64_t** ref);
+/* Free list in FIFO order (paged.py:53) / evictable blocks oldest first (paged.py:57). */
+PK_API int pk_bm_free_list(const pk_block_manager* m, int32_t* out, int64_t cap, int64_t* n);
+PK_API int pk_bm_evictable_list(const pk_block_manager* m, int32_t* out, int64_t cap, int64_t* n);
+/* Hash a block is published under (BlockAllocator.block_hash, paged.py:55); *len = -1 if none. */
+PK_API int pk_bm_block_hash(const pk_block_manager* m, int32_t block, uint8_t* out, int64_t cap,
+                            int64_t* len);
+PK_API int pk_bm_add_prefix_stats(pk_block_manager* m, int64_t hits, int64_t queries);
+/* BlockManager.allocate (paged.py:187-203) given the caller's plan_prefix result. */
+PK_API int pk_bm_seq_allocate(pk_block_manager* m, int64_t seq, int64_t n_tokens,
+                              const int32_t* hits, int64_t n_hits, const uint8_t* hashes,
+                              int64_t hash_len, int64_t* cached_tokens);
+/* BlockManager.can_append (paged.py:206-213). */
+PK_API int pk_bm_can_append(pk_block_manager* m, int64_t seq, int64_t n_tokens, int* ok);
+/* BlockManager.ensure_capacity (paged.py:215-239): (src, dst) copy pairs into pairs_out. */
+PK_API int pk_bm_ensure_capacity(pk_block_manager* m, int64_t seq, int64_t n_tokens,
+                                 int64_t write_from, int64_t* pairs_out, int64_t cap,
+                                 int64_t* npairs);
+/* A sequence's hash chain (BlockTable.hashes, paged.py:142-144): length and last digest,
+ * or the digest at position i. */
+PK_API int pk_bm_seq_hashes(pk_block_manager* m, int64_t seq, int64_t* n, uint8_t* last,
+                            int64_t cap, int64_t* last_len);
+PK_API int pk_bm_seq_hash_at(pk_block_manager* m, int64_t seq, int64_t i, uint8_t* out,
+                             int64_t cap, int64_t* len);
+/* BlockManager.mark_computed's bookkeeping (paged.py:251-254): append digests, register. */
+PK_API int pk_bm_seq_push_hashes(pk_block_manager* m, int64_t seq, const uint8_t* hashes,
+                                 int64_t hash_len, int64_t count);
+/* BlockManager.fork (paged.py:257-263) and free (paged.py:265-271). */
+PK_API int pk_bm_fork(pk_block_manager* m, int64_t parent, int64_t child);
+PK_API int pk_bm_free_seq(pk_block_manager* m, int64_t seq);
+/* BlockManager.block_table (paged.py:273-274); sequence ids with a table. */
+PK_API int pk_bm_table(const pk_block_manager* m, int64_t seq, int32_t* out, int64_t cap,
+                       int64_t* n);
+PK_API int pk_bm_seq_ids(const pk_block_manager* m, int64_t* out, int64_t cap, int64_t* n);
+/* Tables of `nseq` sequences as CSR (the input of pk_batch_plan), without a detour through
+ * Python lists. ids = NULL sizes the call (*total). */
+PK_API int pk_bm_tables_csr(const pk_block_manager* m, const int64_t* seqs, int64_t nseq,
+                            int64_t* indptr, int32_t* ids, int64_t cap, int64_t* total);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PAGEKV_H */

@@ -1,0 +1,823 @@
+// libpagekv C ABI: pool, per-step batch planning and kernel orchestration.
+// The entry points mirror pagellm's cache/paged.py (PagedKVPool, slot_mapping, PagedBatch);
+// the declarations and their reference citations are in include/pagekv.h.
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "pagekv.h"
+#include "pk_internal.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define PK_CUDA(call)                                                                      \
+    do {                                                                                   \
+        cudaError_t e_ = (call);                                                           \
+        if (e_ != cudaSuccess)                                                             \
+            return fail(PK_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));      \
+    } while (0)
+
+// Makes `dev` current for the scope, restoring the caller's device afterwards.
+struct DeviceScope {
+    int prev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceScope(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) err = cudaSetDevice(dev);
+    }
+    ~DeviceScope() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// Grow-only device allocation.
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t cap = 0;
+    cudaError_t reserve(size_t bytes) {
+        if (bytes <= cap) return cudaSuccess;
+        if (ptr) {
+            cudaError_t e = cudaFree(ptr);
+            if (e != cudaSuccess) return e;
+            ptr = nullptr;
+            cap = 0;
+        }
+        size_t want = std::max<size_t>(bytes, 4096);
+        want = want + want / 4;
+        cudaError_t e = cudaMalloc(&ptr, want);
+        if (e == cudaSuccess) cap = want;
+        return e;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+    }
+};
+
+// Packs several host arrays into one pinned buffer and ships them with a single copy.
+// The pinned buffer is reused only after the previous copy out of it has finished.
+struct Uploader {
+    void* host = nullptr;
+    size_t host_cap = 0;
+    DevBuf dev;
+    cudaEvent_t done = nullptr;
+    bool pending = false;
+    std::vector<std::pair<const void*, size_t>> parts;
+    std::vector<size_t> offs;
+
+    static size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+    void begin() {
+        parts.clear();
+        offs.clear();
+    }
+    size_t add(const void* src, size_t bytes) {
+        size_t off = parts.empty() ? 0 : up256(offs.back() + parts.back().second);
+        parts.emplace_back(src, bytes);
+        offs.push_back(off);
+        return off;
+    }
+    int commit(cudaStream_t st) {
+        size_t total = parts.empty() ? 0 : offs.back() + parts.back().second;
+        if (total == 0) return PK_OK;
+        if (!done) PK_CUDA(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+        if (pending) {
+            PK_CUDA(cudaEventSynchronize(done));
+            pending = false;
+        }
+        if (total > host_cap) {
+            if (host) PK_CUDA(cudaFreeHost(host));
+            host = nullptr;
+            host_cap = 0;
+            size_t want = std::max<size_t>(total + total / 4, 4096);
+            PK_CUDA(cudaMallocHost(&host, want));
+            host_cap = want;
+        }
+        PK_CUDA(dev.reserve(total));
+        for (size_t i = 0; i < parts.size(); ++i)
+            if (parts[i].second) std::memcpy(static_cast<char*>(host) + offs[i], parts[i].first, parts[i].second);
+        PK_CUDA(cudaMemcpyAsync(dev.ptr, host, total, cudaMemcpyHostToDevice, st));
+        PK_CUDA(cudaEventRecord(done, st));
+        pending = true;
+        return PK_OK;
+    }
+    template <typename T>
+    T* at(size_t i) const {
+        return reinterpret_cast<T*>(static_cast<char*>(dev.ptr) + offs[i]);
+    }
+    void release() {
+        if (pending && done) cudaEventSynchronize(done);
+        if (host) cudaFreeHost(host);
+        host = nullptr;
+        host_cap = 0;
+        dev.release();
+        if (done) cudaEventDestroy(done);
+        done = nullptr;
+    }
+};
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+}  // namespace
+
+struct pk_pool {
+    int device = 0;
+    int n_layers = 0;
+    int64_t num_blocks = 0;
+    int block_size = 0;
+    int kvh = 0;
+    int d = 0;
+    int dtype = 0;
+    int esize = 0;
+    void* k = nullptr;
+    void* v = nullptr;
+    int64_t layer_elems = 0;
+    int num_sms = 0;
+    // tensor-core path
+    bool tc_ok = false;
+    int tc_per_head = 0;
+    int tc_stages = 0;
+    size_t tc_smem = 0;
+    std::string tc_why;
+    CUtensorMap tmk{};
+    CUtensorMap tmv{};
+    Uploader pairs_up;
+
+    size_t layer_bytes() const { return static_cast<size_t>(layer_elems) * esize; }
+    size_t block_bytes() const { return static_cast<size_t>(block_size) * kvh * d * esize; }
+    char* k_layer(int layer) const { return static_cast<char*>(k) + layer * layer_bytes(); }
+    char* v_layer(int layer) const { return static_cast<char*>(v) + layer * layer_bytes(); }
+};
+
+struct pk_batch {
+    pk_pool* pool = nullptr;
+    int nseq = 0;
+    int64_t nrows = 0;
+    std::vector<int32_t> indptr, ids, starts, nnew, offsets, row_seq;
+    Uploader meta;  // 0 indptr, 1 ids, 2 starts, 3 offsets, 4 row_seq
+    DevBuf rows;    // positions [nrows] then slots [nrows]
+    DevBuf err;     // one int
+    // attention plan for plan_H query heads
+    int plan_H = -1;
+    bool use_tc = false;
+    int nu = 0, total_blocks = 0, ncta = 0, nt = 1, nsplit = 0;
+    int ngeneric = 0;
+    std::vector<int32_t> u_seq, u_t0, u_n, u_blk, sp_u, sp_c0, sp_c1, gen_rows;
+    Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows
+    DevBuf ws;
+    size_t ws_part_o_floats = 0;
+    DevBuf io;  // q | k | v | out for the host-buffer entry point
+    int launches = 0;
+
+    const int64_t* positions() const { return static_cast<const int64_t*>(rows.ptr); }
+    const int64_t* slots() const { return static_cast<const int64_t*>(rows.ptr) + nrows; }
+};
+
+namespace {
+
+// Encode the two tensor maps of the tensor-core kernel. Layout 0 views a layer-stacked
+// pool as [chunk of 64 dims][kv head][slot][64 dims] so that one box = one whole K (or V)
+// block with each (head, chunk) slice's tokens on consecutive 128-byte rows; layout 1
+// is the natural order, one box per (block, head).
+bool encode_pool_maps(pk_pool* P, int layout, std::string* why) {
+    auto enc = tensor_map_encoder();
+    if (!enc) {
+        *why = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    const cuuint64_t slots = static_cast<cuuint64_t>(P->n_layers) * P->num_blocks * P->block_size;
+    const int chunks = P->d / 64;
+    cuuint64_t dims[4];
+    cuuint64_t strides[3];
+    cuuint32_t box[4];
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (layout == 0) {
+        dims[0] = 64; dims[1] = slots; dims[2] = P->kvh; dims[3] = chunks;
+        strides[0] = static_cast<cuuint64_t>(P->kvh) * P->d * 2;
+        strides[1] = static_cast<cuuint64_t>(P->d) * 2;
+        strides[2] = 128;
+        box[0] = 64; box[1] = P->block_size; box[2] = P->kvh; box[3] = chunks;
+    } else {
+        dims[0] = 64; dims[1] = chunks; dims[2] = P->kvh; dims[3] = slots;
+        strides[0] = 128;
+        strides[1] = static_cast<cuuint64_t>(P->d) * 2;
+        strides[2] = static_cast<cuuint64_t>(P->kvh) * P->d * 2;
+        box[0] = 64; box[1] = chunks; box[2] = 1; box[3] = P->block_size;
+    }
+    for (int t = 0; t < 2; ++t) {
+        CUresult r = enc(t == 0 ? &P->tmk : &P->tmv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                         t == 0 ? P->k : P->v, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            char b[96];
+            snprintf(b, sizeof(b), "cuTensorMapEncodeTiled(layout %d) returned %d", layout, (int)r);
+            *why = b;
+            return false;
+        }
+    }
+    return true;
+}
+
+void setup_tc(pk_pool* P) {
+    P->tc_ok = false;
+    auto no = [&](const char* w) { P->tc_why = w; };
+    if (P->dtype != PK_BF16) return no("pool is not bf16");
+    if (P->d % 64 != 0 || P->d > 256) return no("head_dim not in {64,128,256}");
+    if (P->block_size % 16 != 0 || P->block_size > 256) return no("block_size not a multiple of 16 (<=256)");
+    if (P->kvh > pk::kTcMaxKvHeads) return no("more than 8 KV heads");
+    const int64_t slots = static_cast<int64_t>(P->n_layers) * P->num_blocks * P->block_size;
+    if (slots >= (int64_t(1) << 31)) return no("pool has 2^31 slots or more");
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, P->device);
+    const size_t stage = static_cast<size_t>(2) * P->block_size * P->kvh * P->d * 2;
+    int stages = 4;
+    while (stages >= 2 && pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages) > static_cast<size_t>(optin))
+        --stages;
+    (void)stage;
+    if (stages < 2) return no("K/V block too large for two shared-memory stages");
+    std::string why;
+    if (encode_pool_maps(P, 0, &why)) {
+        P->tc_per_head = 0;
+    } else if (encode_pool_maps(P, 1, &why)) {
+        P->tc_per_head = 1;
+    } else {
+        P->tc_why = why;
+        return;
+    }
+    P->tc_stages = stages;
+    P->tc_smem = pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages);
+    P->tc_ok = true;
+    P->tc_why.clear();
+}
+
+int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+// CTA c of n owns blocks [c*T/n, (c+1)*T/n).
+inline int64_t cta_lo(int64_t c, int64_t T, int64_t n) { return c * T / n; }
+
+int cta_of_block(int64_t j, int64_t T, int64_t n) {
+    int64_t c = j * n / T;
+    while (c + 1 < n && cta_lo(c + 1, T, n) <= j) ++c;
+    while (c > 0 && cta_lo(c, T, n) > j) --c;
+    return static_cast<int>(c);
+}
+
+int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
+    pk_pool* P = B->pool;
+    const int g = H / P->kvh;
+    B->plan_H = -1;
+    B->u_seq.clear(); B->u_t0.clear(); B->u_n.clear(); B->u_blk.assign(1, 0);
+    B->sp_u.clear(); B->sp_c0.clear(); B->sp_c1.clear(); B->gen_rows.clear();
+    B->use_tc = false;
+    B->nu = B->total_blocks = B->ncta = B->nsplit = B->ngeneric = 0;
+    B->nt = 1;
+    int qmax = 0;
+    if (P->tc_ok && g <= pk::kMaxCols) {
+        qmax = std::max(1, pk::kMaxCols / g);
+        if (P->d == 256) qmax = g <= 8 ? std::max(1, 8 / g) : 0;  // one n8 tile only at D=256
+    }
+    int64_t T = 0;
+    for (int i = 0; i < B->nseq; ++i) {
+        const int n = B->nnew[i];
+        if (n <= 0) continue;
+        if (qmax == 0) {
+            for (int r = 0; r < n; ++r) B->gen_rows.push_back(B->offsets[i] + r);
+            continue;
+        }
+        for (int t0 = 0; t0 < n; t0 += qmax) {
+            const int nu = std::min(qmax, n - t0);
+            const int64_t ctx = static_cast<int64_t>(B->starts[i]) + t0 + nu;
+            T += ceil_div(ctx, P->block_size);
+            B->u_seq.push_back(i);
+            B->u_t0.push_back(t0);
+            B->u_n.push_back(nu);
+            B->u_blk.push_back(static_cast<int32_t>(T));
+            B->nt = std::max(B->nt, ceil_div(static_cast<int64_t>(nu) * g, 8));
+        }
+    }
+    if (T >= (int64_t(1) << 31)) return fail(PK_ERR_UNSUPPORTED, "step reads 2^31 blocks or more");
+    B->nu = static_cast<int>(B->u_seq.size());
+    B->ngeneric = static_cast<int>(B->gen_rows.size());
+    if (B->nu > 0) {
+        B->use_tc = true;
+        B->total_blocks = static_cast<int>(T);
+        B->ncta = static_cast<int>(std::min<int64_t>(T, P->num_sms));
+        for (int u = 0; u < B->nu; ++u) {
+            const int c0 = cta_of_block(B->u_blk[u], T, B->ncta);
+            const int c1 = cta_of_block(B->u_blk[u + 1] - 1, T, B->ncta);
+            if (c0 != c1) {
+                B->sp_u.push_back(u);
+                B->sp_c0.push_back(c0);
+                B->sp_c1.push_back(c1);
+            }
+        }
+        B->nsplit = static_cast<int>(B->sp_u.size());
+        const size_t segs = static_cast<size_t>(B->nu) + B->ncta;
+        B->ws_part_o_floats = segs * P->kvh * pk::kMaxCols * P->d;
+        const size_t ws_bytes = (B->ws_part_o_floats + segs * P->kvh * pk::kMaxCols * 2) * sizeof(float);
+        if (B->nsplit > 0 || true) PK_CUDA(B->ws.reserve(ws_bytes));
+    }
+    B->plan.begin();
+    B->plan.add(B->u_seq.data(), B->u_seq.size() * 4);
+    B->plan.add(B->u_t0.data(), B->u_t0.size() * 4);
+    B->plan.add(B->u_n.data(), B->u_n.size() * 4);
+    B->plan.add(B->u_blk.data(), B->u_blk.size() * 4);
+    B->plan.add(B->sp_u.data(), B->sp_u.size() * 4);
+    B->plan.add(B->sp_c0.data(), B->sp_c0.size() * 4);
+    B->plan.add(B->sp_c1.data(), B->sp_c1.size() * 4);
+    B->plan.add(B->gen_rows.data(), B->gen_rows.size() * 4);
+    int rc = B->plan.commit(st);
+    if (rc != PK_OK) return rc;
+    B->plan_H = H;
+    return PK_OK;
+}
+
+int check_heads(const pk_batch* B, int H) {
+    if (H <= 0 || H % B->pool->kvh != 0)
+        return fail(PK_ERR_INVALID_ARG, "n_heads=%d is not a positive multiple of n_kv_heads=%d", H,
+                    B->pool->kvh);
+    return PK_OK;
+}
+
+int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaStream_t st) {
+    pk_pool* P = B->pool;
+    if (B->plan_H != H) {
+        int rc = build_attention_plan(B, H, st);
+        if (rc != PK_OK) return rc;
+    }
+    if (B->nrows == 0) return PK_OK;
+    const int g = H / P->kvh;
+    if (B->use_tc) {
+        pk::TcParams p{};
+        p.q = q;
+        p.out = out;
+        p.part_o = static_cast<float*>(B->ws.ptr);
+        p.part_ml = static_cast<float*>(B->ws.ptr) + B->ws_part_o_floats;
+        p.err = static_cast<int*>(B->err.ptr);
+        p.indptr = B->meta.at<int32_t>(0);
+        p.ids = B->meta.at<int32_t>(1);
+        p.starts = B->meta.at<int32_t>(2);
+        p.offsets = B->meta.at<int32_t>(3);
+        p.u_seq = B->plan.at<int32_t>(0);
+        p.u_t0 = B->plan.at<int32_t>(1);
+        p.u_n = B->plan.at<int32_t>(2);
+        p.u_blk = B->plan.at<int32_t>(3);
+        p.nu = B->nu;
+        p.total_blocks = B->total_blocks;
+        p.ncta = B->ncta;
+        p.kvh = P->kvh;
+        p.g = g;
+        p.H = H;
+        p.bs = P->block_size;
+        p.stages = P->tc_stages;
+        p.per_head_layout = P->tc_per_head;
+        p.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
+        p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
+        PK_CUDA(pk::launch_tc_attention(P->d, B->nt, &P->tmk, &P->tmv, p, P->tc_smem, st));
+        B->launches++;
+        if (B->nsplit > 0) {
+            pk::MergeParams m{};
+            m.out = out;
+            m.part_o = p.part_o;
+            m.part_ml = p.part_ml;
+            m.offsets = p.offsets;
+            m.u_seq = p.u_seq;
+            m.u_t0 = p.u_t0;
+            m.u_n = p.u_n;
+            m.split_u = B->plan.at<int32_t>(4);
+            m.split_c0 = B->plan.at<int32_t>(5);
+            m.split_c1 = B->plan.at<int32_t>(6);
+            m.kvh = P->kvh;
+            m.g = g;
+            m.H = H;
+            m.D = P->d;
+            PK_CUDA(pk::launch_merge(m, B->nsplit, st));
+            B->launches++;
+        }
+    }
+    if (B->ngeneric > 0) {
+        if (P->d > 512) return fail(PK_ERR_UNSUPPORTED, "head_dim %d > 512", P->d);
+        pk::GenericParams p{};
+        p.q = q;
+        p.out = out;
+        p.pool_k = P->k_layer(layer);
+        p.pool_v = P->v_layer(layer);
+        p.row_seq = B->meta.at<int32_t>(4);
+        p.indptr = B->meta.at<int32_t>(0);
+        p.ids = B->meta.at<int32_t>(1);
+        p.starts = B->meta.at<int32_t>(2);
+        p.offsets = B->meta.at<int32_t>(3);
+        p.rows = B->plan.at<int32_t>(7);
+        p.nrows = B->ngeneric;
+        p.H = H;
+        p.kvh = P->kvh;
+        p.D = P->d;
+        p.bs = P->block_size;
+        p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(P->d)));
+        PK_CUDA(pk::launch_generic_attention(P->dtype, p, st));
+        B->launches++;
+    }
+    return PK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pk_last_error(void) { return g_err.c_str(); }
+
+int pk_abi_version(void) { return 1; }
+
+int pk_pool_create(int n_layers, int64_t num_blocks, int block_size, int n_kv_heads, int head_dim,
+                   int dtype, int device, pk_pool** out) {
+    if (!out) return fail(PK_ERR_INVALID_ARG, "out is NULL");
+    *out = nullptr;
+    if (n_layers <= 0 || num_blocks <= 0 || block_size <= 0 || n_kv_heads <= 0 || head_dim <= 0)
+        return fail(PK_ERR_INVALID_ARG, "pool dimensions must be positive");
+    if (dtype != PK_F32 && dtype != PK_BF16) return fail(PK_ERR_INVALID_ARG, "unknown dtype %d", dtype);
+    if (num_blocks >= (int64_t(1) << 31)) return fail(PK_ERR_INVALID_ARG, "num_blocks must be < 2^31");
+    DeviceScope ds(device);
+    if (ds.err != cudaSuccess) return fail(PK_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(ds.err));
+    auto* P = new pk_pool();
+    P->device = device;
+    P->n_layers = n_layers;
+    P->num_blocks = num_blocks;
+    P->block_size = block_size;
+    P->kvh = n_kv_heads;
+    P->d = head_dim;
+    P->dtype = dtype;
+    P->esize = dtype == PK_F32 ? 4 : 2;
+    P->layer_elems = num_blocks * block_size * static_cast<int64_t>(n_kv_heads) * head_dim;
+    const size_t bytes = static_cast<size_t>(n_layers) * P->layer_bytes();
+    cudaError_t e = cudaMalloc(&P->k, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&P->v, bytes);
+    if (e == cudaSuccess) e = cudaMemset(P->k, 0, bytes);
+    if (e == cudaSuccess) e = cudaMemset(P->v, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&P->num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) {
+        if (P->k) cudaFree(P->k);
+        if (P->v) cudaFree(P->v);
+        delete P;
+        return fail(PK_ERR_CUDA, "pool allocation of 2 x %zu bytes: %s", bytes, cudaGetErrorString(e));
+    }
+    setup_tc(P);
+    *out = P;
+    return PK_OK;
+}
+
+int pk_pool_destroy(pk_pool* pool) {
+    if (!pool) return PK_OK;
+    DeviceScope ds(pool->device);
+    pool->pairs_up.release();
+    if (pool->k) cudaFree(pool->k);
+    if (pool->v) cudaFree(pool->v);
+    delete pool;
+    return PK_OK;
+}
+
+int pk_pool_buffers(const pk_pool* pool, void** k_dev, void** v_dev, int64_t* nbytes) {
+    if (!pool) return fail(PK_ERR_INVALID_ARG, "pool is NULL");
+    if (k_dev) *k_dev = pool->k;
+    if (v_dev) *v_dev = pool->v;
+    if (nbytes) *nbytes = 2 * static_cast<int64_t>(pool->n_layers) * pool->layer_bytes();
+    return PK_OK;
+}
+
+int pk_pool_tc_info(const pk_pool* pool, int* enabled, int* per_head_layout, int* stages,
+                    const char** why) {
+    if (!pool) return fail(PK_ERR_INVALID_ARG, "pool is NULL");
+    if (enabled) *enabled = pool->tc_ok ? 1 : 0;
+    if (per_head_layout) *per_head_layout = pool->tc_per_head;
+    if (stages) *stages = pool->tc_stages;
+    if (why) *why = pool->tc_why.c_str();
+    return PK_OK;
+}
+
+int pk_pool_copy_blocks_dev(pk_pool* pool, const int64_t* pairs_dev, int64_t npairs, void* stream) {
+    if (!pool) return fail(PK_ERR_INVALID_ARG, "pool is NULL");
+    if (npairs < 0) return fail(PK_ERR_INVALID_ARG, "npairs < 0");
+    if (npairs == 0) return PK_OK;
+    if (!pairs_dev) return fail(PK_ERR_INVALID_ARG, "pairs is NULL");
+    DeviceScope ds(pool->device);
+    PK_CUDA(pk::launch_copy_blocks(pool->k, pool->v, pairs_dev, npairs, pool->n_layers,
+                                   static_cast<int64_t>(pool->layer_bytes()),
+                                   static_cast<int64_t>(pool->block_bytes()),
+                                   static_cast<cudaStream_t>(stream)));
+    return PK_OK;
+}
+
+int pk_pool_copy_blocks(pk_pool* pool, const int64_t* pairs_host, int64_t npairs, void* stream) {
+    if (!pool) return fail(PK_ERR_INVALID_ARG, "pool is NULL");
+    if (npairs < 0) return fail(PK_ERR_INVALID_ARG, "npairs < 0");
+    if (npairs == 0) return PK_OK;
+    if (!pairs_host) return fail(PK_ERR_INVALID_ARG, "pairs is NULL");
+    for (int64_t i = 0; i < 2 * npairs; ++i)
+        if (pairs_host[i] < 0 || pairs_host[i] >= pool->num_blocks)
+            return fail(PK_ERR_OUT_OF_RANGE, "copy pair %lld: block id %lld outside [0, %lld)",
+                        (long long)(i / 2), (long long)pairs_host[i], (long long)pool->num_blocks);
+    DeviceScope ds(pool->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Pairs run as one launch when no copy reads or overwrites another's destination;
+    // otherwise they are cut into consecutive groups that keep list order.
+    std::vector<int64_t> group_start{0};
+    {
+        std::vector<char> is_dst(static_cast<size_t>(pool->num_blocks), 0);
+        std::vector<char> is_src(static_cast<size_t>(pool->num_blocks), 0);
+        std::vector<int64_t> touched;
+        for (int64_t i = 0; i < npairs; ++i) {
+            const int64_t s = pairs_host[2 * i], d = pairs_host[2 * i + 1];
+            if (is_dst[s] || is_dst[d] || is_src[d]) {
+                for (int64_t b : touched) is_dst[b] = is_src[b] = 0;
+                touched.clear();
+                group_start.push_back(i);
+            }
+            is_src[s] = 1;
+            is_dst[d] = 1;
+            touched.push_back(s);
+            touched.push_back(d);
+        }
+    }
+    group_start.push_back(npairs);
+    Uploader& up = pool->pairs_up;
+    up.begin();
+    up.add(pairs_host, static_cast<size_t>(npairs) * 16);
+    int rc = up.commit(st);
+    if (rc != PK_OK) return rc;
+    const int64_t* dev = up.at<int64_t>(0);
+    for (size_t gi = 0; gi + 1 < group_start.size(); ++gi) {
+        const int64_t a = group_start[gi], b = group_start[gi + 1];
+        PK_CUDA(pk::launch_copy_blocks(pool->k, pool->v, dev + 2 * a, b - a, pool->n_layers,
+                                       static_cast<int64_t>(pool->layer_bytes()),
+                                       static_cast<int64_t>(pool->block_bytes()), st));
+    }
+    return PK_OK;
+}
+
+int pk_pool_append(pk_pool* pool, int layer, const float* k_dev, const float* v_dev,
+                   const int64_t* slots_dev, int64_t n, void* stream) {
+    if (!pool) return fail(PK_ERR_INVALID_ARG, "pool is NULL");
+    if (layer < 0 || layer >= pool->n_layers) return fail(PK_ERR_OUT_OF_RANGE, "layer %d", layer);
+    if (n < 0) return fail(PK_ERR_INVALID_ARG, "n < 0");
+    if (n == 0) return PK_OK;
+    if (!k_dev || !v_dev || !slots_dev) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    DeviceScope ds(pool->device);
+    PK_CUDA(pk::launch_append(pool->dtype, pool->k_layer(layer), pool->v_layer(layer), k_dev, v_dev,
+                              slots_dev, n, pool->kvh * pool->d, static_cast<cudaStream_t>(stream)));
+    return PK_OK;
+}
+
+int pk_slot_mapping(const int32_t* table_dev, int64_t table_len, const int64_t* positions_dev,
+                    int64_t n, int block_size, int64_t* slots_dev, int32_t* err_dev, void* stream) {
+    if (n < 0 || table_len < 0 || block_size <= 0) return fail(PK_ERR_INVALID_ARG, "bad sizes");
+    if (n == 0) return PK_OK;
+    if (!positions_dev || !slots_dev || (!table_dev && table_len > 0))
+        return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    PK_CUDA(pk::launch_slot_mapping(table_dev, table_len, positions_dev, n, block_size, slots_dev,
+                                    err_dev, static_cast<cudaStream_t>(stream)));
+    return PK_OK;
+}
+
+int pk_batch_create(pk_pool* pool, pk_batch** out) {
+    if (!pool || !out) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    DeviceScope ds(pool->device);
+    auto* B = new pk_batch();
+    B->pool = pool;
+    cudaError_t e = B->err.reserve(sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(B->err.ptr, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        delete B;
+        return fail(PK_ERR_CUDA, "batch error word: %s", cudaGetErrorString(e));
+    }
+    *out = B;
+    return PK_OK;
+}
+
+int pk_batch_destroy(pk_batch* B) {
+    if (!B) return PK_OK;
+    DeviceScope ds(B->pool->device);
+    B->meta.release();
+    B->plan.release();
+    B->rows.release();
+    B->err.release();
+    B->ws.release();
+    B->io.release();
+    delete B;
+    return PK_OK;
+}
+
+int pk_batch_plan(pk_batch* B, int nseq, const int64_t* table_indptr, const int32_t* table_ids,
+                  const int64_t* starts, const int64_t* n_new, int64_t* n_rows, void* stream) {
+    if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
+    if (nseq < 0) return fail(PK_ERR_INVALID_ARG, "nseq < 0");
+    if (nseq > 0 && (!table_indptr || !starts || !n_new))
+        return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    pk_pool* P = B->pool;
+    const int bs = P->block_size;
+    B->plan_H = -1;
+    B->nseq = 0;
+    B->nrows = 0;
+    B->indptr.assign(1, 0);
+    B->ids.clear();
+    B->starts.clear();
+    B->nnew.clear();
+    B->offsets.assign(1, 0);
+    B->row_seq.clear();
+    if (nseq > 0 && table_indptr[0] != 0) return fail(PK_ERR_INVALID_ARG, "table_indptr[0] != 0");
+    int64_t rows = 0;
+    for (int i = 0; i < nseq; ++i) {
+        const int64_t s = starts[i], n = n_new[i];
+        const int64_t tb = table_indptr[i], te = table_indptr[i + 1];
+        if (s < 0 || n < 0) return fail(PK_ERR_INVALID_ARG, "seq %d: start %lld / n_new %lld negative", i, (long long)s, (long long)n);
+        if (te < tb) return fail(PK_ERR_INVALID_ARG, "table_indptr not non-decreasing at seq %d", i);
+        const int64_t ctx = s + n;
+        if (ctx >= (int64_t(1) << 31)) return fail(PK_ERR_UNSUPPORTED, "seq %d: context %lld too long", i, (long long)ctx);
+        const int64_t need = (ctx + bs - 1) / bs;
+        if (need > te - tb)
+            return fail(PK_ERR_OUT_OF_RANGE, "seq %d: positions up to %lld need %lld blocks, table has %lld",
+                        i, (long long)(ctx - 1), (long long)need, (long long)(te - tb));
+        if (need > 0 && !table_ids) return fail(PK_ERR_INVALID_ARG, "table_ids is NULL");
+        for (int64_t j = tb; j < tb + need; ++j) {
+            const int32_t b = table_ids[j];
+            if (b < 0 || b >= P->num_blocks)
+                return fail(PK_ERR_OUT_OF_RANGE, "seq %d: block id %d outside [0, %lld)", i, b,
+                            (long long)P->num_blocks);
+        }
+        // Only the referenced prefix of each table is uploaded.
+        B->ids.insert(B->ids.end(), table_ids + tb, table_ids + tb + need);
+        if (B->ids.size() >= (size_t(1) << 31)) return fail(PK_ERR_UNSUPPORTED, "too many table entries");
+        B->indptr.push_back(static_cast<int32_t>(B->ids.size()));
+        B->starts.push_back(static_cast<int32_t>(s));
+        B->nnew.push_back(static_cast<int32_t>(n));
+        rows += n;
+        if (rows >= (int64_t(1) << 31)) return fail(PK_ERR_UNSUPPORTED, "too many rows");
+        B->offsets.push_back(static_cast<int32_t>(rows));
+        for (int64_t r = 0; r < n; ++r) B->row_seq.push_back(i);
+    }
+    B->nseq = nseq;
+    B->nrows = rows;
+    if (n_rows) *n_rows = rows;
+    DeviceScope ds(P->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    B->meta.begin();
+    B->meta.add(B->indptr.data(), B->indptr.size() * 4);
+    B->meta.add(B->ids.data(), B->ids.size() * 4);
+    B->meta.add(B->starts.data(), B->starts.size() * 4);
+    B->meta.add(B->offsets.data(), B->offsets.size() * 4);
+    B->meta.add(B->row_seq.data(), B->row_seq.size() * 4);
+    int rc = B->meta.commit(st);
+    if (rc != PK_OK) return rc;
+    PK_CUDA(B->rows.reserve(static_cast<size_t>(std::max<int64_t>(rows, 1)) * 16));
+    PK_CUDA(pk::launch_plan_rows(B->meta.at<int32_t>(4), B->meta.at<int32_t>(3), B->meta.at<int32_t>(2),
+                                 B->meta.at<int32_t>(0), B->meta.at<int32_t>(1), bs, rows,
+                                 static_cast<int64_t*>(B->rows.ptr),
+                                 static_cast<int64_t*>(B->rows.ptr) + rows, st));
+    return PK_OK;
+}
+
+int pk_batch_rows(const pk_batch* B, const int64_t** positions_dev, const int64_t** slots_dev) {
+    if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
+    if (positions_dev) *positions_dev = B->positions();
+    if (slots_dev) *slots_dev = B->slots();
+    return PK_OK;
+}
+
+int pk_batch_attend(pk_batch* B, int layer, int n_heads, const float* q_dev, float* out_dev,
+                    void* stream) {
+    if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
+    int rc = check_heads(B, n_heads);
+    if (rc != PK_OK) return rc;
+    if (layer < 0 || layer >= B->pool->n_layers) return fail(PK_ERR_OUT_OF_RANGE, "layer %d", layer);
+    if (B->nrows > 0 && (!q_dev || !out_dev)) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    DeviceScope ds(B->pool->device);
+    B->launches = 0;
+    return attend_impl(B, layer, n_heads, q_dev, out_dev, static_cast<cudaStream_t>(stream));
+}
+
+int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* q_dev,
+                              const float* k_dev, const float* v_dev, float* out_dev, void* stream) {
+    if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
+    int rc = check_heads(B, n_heads);
+    if (rc != PK_OK) return rc;
+    pk_pool* P = B->pool;
+    if (layer < 0 || layer >= P->n_layers) return fail(PK_ERR_OUT_OF_RANGE, "layer %d", layer);
+    if (B->nrows > 0 && (!q_dev || !k_dev || !v_dev || !out_dev))
+        return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    DeviceScope ds(P->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    B->launches = 0;
+    if (B->nrows > 0) {
+        PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_dev, v_dev,
+                                  B->slots(), B->nrows, P->kvh * P->d, st));
+        B->launches++;
+    }
+    return attend_impl(B, layer, n_heads, q_dev, out_dev, st);
+}
+
+int pk_batch_write_and_attend_host(pk_batch* B, int layer, int n_heads, const float* q_host,
+                                   const float* k_host, const float* v_host, float* out_host,
+                                   void* stream) {
+    if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
+    int rc = check_heads(B, n_heads);
+    if (rc != PK_OK) return rc;
+    pk_pool* P = B->pool;
+    if (B->nrows > 0 && (!q_host || !k_host || !v_host || !out_host))
+        return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    DeviceScope ds(P->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t qn = static_cast<size_t>(B->nrows) * n_heads * P->d;
+    const size_t kn = static_cast<size_t>(B->nrows) * P->kvh * P->d;
+    PK_CUDA(B->io.reserve((2 * qn + 2 * kn) * sizeof(float) + 1024));
+    float* qd = static_cast<float*>(B->io.ptr);
+    float* kd = qd + qn;
+    float* vd = kd + kn;
+    float* od = vd + kn;
+    if (B->nrows > 0) {
+        PK_CUDA(cudaMemcpyAsync(qd, q_host, qn * sizeof(float), cudaMemcpyHostToDevice, st));
+        PK_CUDA(cudaMemcpyAsync(kd, k_host, kn * sizeof(float), cudaMemcpyHostToDevice, st));
+        PK_CUDA(cudaMemcpyAsync(vd, v_host, kn * sizeof(float), cudaMemcpyHostToDevice, st));
+    }
+    rc = pk_batch_write_and_attend(B, layer, n_heads, qd, kd, vd, od, stream);
+    if (rc != PK_OK) return rc;
+    if (B->nrows > 0)
+        PK_CUDA(cudaMemcpyAsync(out_host, od, qn * sizeof(float), cudaMemcpyDeviceToHost, st));
+    PK_CUDA(cudaStreamSynchronize(st));
+    return PK_OK;
+}
+
+int pk_batch_check(pk_batch* B, void* stream) {
+    if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
+    DeviceScope ds(B->pool->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    PK_CUDA(cudaStreamSynchronize(st));
+    int word = 0;
+    PK_CUDA(cudaMemcpy(&word, B->err.ptr, sizeof(int), cudaMemcpyDeviceToHost));
+    if (word != 0) {
+        PK_CUDA(cudaMemset(B->err.ptr, 0, sizeof(int)));
+        return fail(PK_ERR_TIMEOUT, "a bounded device wait timed out (error word %d)", word);
+    }
+    return PK_OK;
+}
+
+int pk_batch_stats(const pk_batch* B, int64_t* s) {
+    if (!B || !s) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    s[0] = B->nrows;
+    s[1] = B->nu;
+    s[2] = B->ncta;
+    s[3] = B->total_blocks;
+    s[4] = B->nsplit;
+    s[5] = B->ngeneric;
+    s[6] = B->launches;
+    return PK_OK;
+}
+
+int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,
+                      int64_t* cta_first_block, int* ncta) {
+    if (n_units < 0 || max_ctas <= 0 || !ncta) return fail(PK_ERR_INVALID_ARG, "bad arguments");
+    int64_t T = 0;
+    for (int64_t i = 0; i < n_units; ++i) {
+        if (unit_blocks[i] <= 0) return fail(PK_ERR_INVALID_ARG, "unit %lld has no blocks", (long long)i);
+        T += unit_blocks[i];
+    }
+    const int64_t n = std::min<int64_t>(T, max_ctas);
+    *ncta = static_cast<int>(n);
+    if (cta_first_block)
+        for (int64_t c = 0; c <= n; ++c) cta_first_block[c] = n ? cta_lo(c, T, n) : 0;
+    return PK_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,419 @@
+// Split-KV paged attention on the tensor cores for bf16 pools (decode rows, speculative
+// verify windows, and prefill chunks cut into windows).
+//
+// Semantics: pagellm cache/paged.py:441-464 (write_and_attend's read half) with the
+// causal rule of model/transformer.py:116-146 - the query at absolute position p sees
+// keys 0..p of its sequence, read through the block table (cache/paged.py:309-352 is the
+// block-at-a-time structure followed here).
+//
+// Work split. Every sequence's query rows are cut into "units" of at most 16/g query
+// tokens (g = query heads per KV head), so one unit's (token, head) columns fit one or two
+// n8 MMA tiles. A unit reads the blocks that hold positions 0..unit_ctx-1. All units'
+// blocks are laid end to end and the total is cut into `ncta` equal ranges: CTA c owns
+// blocks [c*T/ncta, (c+1)*T/ncta). A unit that falls inside one CTA is finished there;
+// a unit cut by CTA boundaries leaves one partial (max, sum, un-normalised output) per
+// CTA, merged by merge_kernel.
+//
+// CTA = 1 producer warp + one consumer warp per KV head. The producer streams each K/V
+// block of the layer into a ring of shared-memory stages with TMA bulk tensor loads (no
+// multicast) signalling mbarriers; consumers wait, compute, and release the stage.
+//
+// Per consumer warp and 16-token tile, with the transposed formulation (tokens as MMA rows):
+//   S^T[16 x 8*NT] = K[16 x D] . Q^T[D x 8*NT]     (Q split as bf16 hi + lo for accuracy)
+//   online softmax down the columns (exp2 domain, scale folded into Q)
+//   P^T -> bf16, transposed in registers with movmatrix into the B operand
+//   O^T[D x 8*NT] += V^T[D x 16] . P^T[16 x 8*NT]  (V^T read with ldmatrix.trans)
+// Shared-memory tiles use the TMA 128-byte swizzle, so the eight 16-byte rows of every
+// ldmatrix phase land in distinct bank groups.
+
+#include "pk_device.cuh"
+#include "pk_internal.h"
+
+namespace pk {
+
+namespace {
+
+__device__ __forceinline__ int upper_bound_i32(const int32_t* a, int n, int x) {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        int mid = (lo + hi) >> 1;
+        if (a[mid] <= x) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+template <int D>
+struct TileGeom {
+    static constexpr int kChunks = D / 64;  // 128-byte swizzle rows per token and head
+};
+
+// Byte offset inside a swizzled K/V stage tile of the 16-byte unit holding
+// dims [8*u, 8*u+8) of (head h, token t).
+__device__ __forceinline__ uint32_t tile_off(int chunk, int h, int t, int u16, int kvh, int bs,
+                                             int chunks, int per_head) {
+    const int row = per_head ? ((h * bs + t) * chunks + chunk) : ((chunk * kvh + h) * bs + t);
+    return static_cast<uint32_t>(row * 128 + ((u16 ^ (row & 7)) << 4));
+}
+
+template <int D, int NT>
+__global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
+    tc_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                   const TcParams p) {
+    constexpr int KS = D / 16;  // k-steps over the head dim / m-tiles of O^T
+    constexpr int CH = TileGeom<D>::kChunks;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    const int tile_bytes = p.bs * p.kvh * D * 2;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * 2 * tile_bytes);
+    uint64_t* empty = full + p.stages;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nwc = p.kvh;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], nwc);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    const int c = blockIdx.x;
+    const int lo = static_cast<int>(static_cast<int64_t>(c) * p.total_blocks / p.ncta);
+    const int hi = static_cast<int>(static_cast<int64_t>(c + 1) * p.total_blocks / p.ncta);
+    const int u_first = upper_bound_i32(p.u_blk, p.nu + 1, lo) - 1;
+
+    if (warp == nwc) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            prefetch_tensormap(&tmk);
+            prefetch_tensormap(&tmv);
+            int it = 0;
+            bool ok = true;
+            for (int j = lo, u = u_first; j < hi && ok; ++u) {
+                const int uend = min(hi, p.u_blk[u + 1]);
+                const int seq = p.u_seq[u];
+                const int tbase = p.indptr[seq] - p.u_blk[u];
+                for (; j < uend; ++j, ++it) {
+                    const int s = it % p.stages;
+                    const uint32_t k = static_cast<uint32_t>(it / p.stages);
+                    if (!mbar_wait_bounded(&empty[s], (k & 1u) ^ 1u)) {
+                        atomicExch(p.err, kErrTimeout);
+                        ok = false;
+                        break;
+                    }
+                    const int phys = p.ids[tbase + j];
+                    const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(phys) * p.bs);
+                    uint8_t* kd = smem + s * 2 * tile_bytes;
+                    uint8_t* vd = kd + tile_bytes;
+                    mbar_arrive_expect_tx(&full[s], 2u * tile_bytes);
+                    if (!p.per_head_layout) {
+                        tma_load_4d(kd, &tmk, 0, slot0, 0, 0, &full[s]);
+                        tma_load_4d(vd, &tmv, 0, slot0, 0, 0, &full[s]);
+                    } else {
+                        const int hb = p.bs * CH * 128;
+                        for (int h = 0; h < p.kvh; ++h) {
+                            tma_load_4d(kd + h * hb, &tmk, 0, 0, h, slot0, &full[s]);
+                            tma_load_4d(vd + h * hb, &tmv, 0, 0, h, slot0, &full[s]);
+                        }
+                    }
+                }
+            }
+            // Never leave the CTA with copies still landing in its shared memory.
+            for (int t = max(0, it - p.stages); t < it; ++t) {
+                mbar_wait_bounded(&full[t % p.stages], static_cast<uint32_t>(t / p.stages) & 1u);
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    const int h = warp;
+    const int g = p.g;
+    const int quad = lane & 3;   // column pair within an n8 tile
+    const int grp = lane >> 2;   // row within an 8-row group
+    int it = 0;
+    for (int j = lo, u = u_first; j < hi; ++u) {
+        const int uend = min(hi, p.u_blk[u + 1]);
+        const int ublk0 = p.u_blk[u];
+        const int seq = p.u_seq[u];
+        const int t0 = p.u_t0[u];
+        const int nq = p.u_n[u];
+        const int qpos0 = p.starts[seq] + t0;  // absolute position of the unit's first query
+        const int uctx = qpos0 + nq;           // keys 0..uctx-1 are read
+        const int row0 = p.offsets[seq] + t0;
+
+        // Q^T as the B operand: column n = lane/4 of each n8 tile, dims 2*quad(+1), +8.
+        uint32_t qh[KS][NT][2], ql[KS][NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int col = nt * 8 + grp;
+            const int tq = col / g;
+            const bool live = tq < nq;
+            const float* qp = p.q + (static_cast<size_t>(row0 + (live ? tq : 0)) * p.H + h * g +
+                                     col % g) * D;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    float2 x = make_float2(0.f, 0.f);
+                    if (live) x = *reinterpret_cast<const float2*>(qp + ks * 16 + half * 8 + 2 * quad);
+                    x.x *= p.qscale;
+                    x.y *= p.qscale;
+                    const uint32_t hb = pack_bf16(x.x, x.y);
+                    qh[ks][nt][half] = hb;
+                    ql[ks][nt][half] = pack_bf16(x.x - bf16_lo_f(hb), x.y - bf16_hi_f(hb));
+                }
+            }
+        }
+        // Causal limit of the C-fragment columns this lane holds (2*quad, 2*quad+1).
+        int lim[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int tq = (nt * 8 + 2 * quad + e) / g;
+                lim[nt][e] = tq < nq ? qpos0 + tq : -1;
+            }
+
+        float m[NT][2], l[NT][2];
+        float acc[KS][NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            m[nt][0] = m[nt][1] = -INFINITY;
+            l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.f;
+        }
+
+        bool alive = true;
+        for (; j < uend; ++j, ++it) {
+            const int s = it % p.stages;
+            // Every lane waits; the verdict is made warp-uniform (and the warp reconverged)
+            // before the .sync.aligned matrix instructions below.
+            const bool got = mbar_wait_bounded(&full[s], static_cast<uint32_t>(it / p.stages) & 1u);
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0) atomicExch(p.err, kErrTimeout);
+                alive = false;
+                break;
+            }
+            const uint32_t kst = smem_u32(smem + s * 2 * tile_bytes);
+            const uint32_t vst = kst + tile_bytes;
+            const int kpos0 = (j - ublk0) * p.bs;
+            const int nvalid = min(p.bs, uctx - kpos0);
+            if (nvalid < p.bs) {
+                // Slots past the context may hold anything; zero this head's V rows there so
+                // that 0 * V stays 0 in the P.V product.
+                uint8_t* vgen = smem + s * 2 * tile_bytes + tile_bytes;
+                const int units = (p.bs - nvalid) * CH * 8;
+                for (int x = lane; x < units; x += 32) {
+                    const int t = nvalid + x / (CH * 8);
+                    const int ch = (x / 8) % CH;
+                    const int u16 = x % 8;
+                    *reinterpret_cast<uint4*>(vgen + tile_off(ch, h, t, u16, p.kvh, p.bs, CH,
+                                                              p.per_head_layout)) =
+                        make_uint4(0, 0, 0, 0);
+                }
+                __syncwarp();
+            }
+            for (int mtile = 0; mtile < p.bs / 16; ++mtile) {
+                // ---- S^T = K . Q^T
+                float sacc[NT][4];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) sacc[nt][i] = 0.f;
+                {
+                    const int tk = mtile * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+                    for (int ks = 0; ks < KS; ++ks) {
+                        const int u16 = (ks & 3) * 2 + (lane >> 4);
+                        uint32_t a[4];
+                        ldmatrix_x4(a, kst + tile_off(ks >> 2, h, tk, u16, p.kvh, p.bs, CH,
+                                                      p.per_head_layout));
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) {
+                            mma_bf16_16816(sacc[nt], a, qh[ks][nt][0], qh[ks][nt][1]);
+                            mma_bf16_16816(sacc[nt], a, ql[ks][nt][0], ql[ks][nt][1]);
+                        }
+                    }
+                }
+                // ---- mask + online softmax down each column
+                const int kp_a = kpos0 + mtile * 16 + grp;  // rows held: grp and grp + 8
+                const int kp_b = kp_a + 8;
+                uint32_t pb[NT][2];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    float pr[4];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const float xa = (kp_a <= lim[nt][e] && kp_a < uctx) ? sacc[nt][e] : -INFINITY;
+                        const float xb = (kp_b <= lim[nt][e] && kp_b < uctx) ? sacc[nt][2 + e] : -INFINITY;
+                        float mx = fmaxf(xa, xb);
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                        const float mnew = fmaxf(m[nt][e], mx);
+                        const float base = (mnew == -INFINITY) ? 0.f : mnew;
+                        const float corr = exp2f(m[nt][e] - base);
+                        const float pa = exp2f(xa - base);
+                        const float pbv = exp2f(xb - base);
+                        l[nt][e] = l[nt][e] * corr + pa + pbv;
+                        m[nt][e] = mnew;
+#pragma unroll
+                        for (int mt = 0; mt < KS; ++mt) {
+                            acc[mt][nt][e] *= corr;
+                            acc[mt][nt][2 + e] *= corr;
+                        }
+                        pr[e] = pa;
+                        pr[2 + e] = pbv;
+                    }
+                    // P^T C-fragment rows grp / grp+8 -> B operand (k = token, n = column)
+                    pb[nt][0] = movmatrix_trans(pack_bf16(pr[0], pr[1]));
+                    pb[nt][1] = movmatrix_trans(pack_bf16(pr[2], pr[3]));
+                }
+                // ---- O^T += V^T . P^T
+                {
+                    const int tv = mtile * 16 + (lane & 7) + (lane >> 4) * 8;
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        const int u16 = (mt & 3) * 2 + ((lane >> 3) & 1);
+                        uint32_t a[4];
+                        ldmatrix_x4_trans(a, vst + tile_off(mt >> 2, h, tv, u16, p.kvh, p.bs, CH,
+                                                            p.per_head_layout));
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) mma_bf16_16816(acc[mt][nt], a, pb[nt][0], pb[nt][1]);
+                    }
+                }
+            }
+            if (nvalid < p.bs) fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (!alive) break;
+
+        // ---- finish the unit's segment
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float t = l[nt][e];
+                t += __shfl_xor_sync(0xffffffffu, t, 4);
+                t += __shfl_xor_sync(0xffffffffu, t, 8);
+                t += __shfl_xor_sync(0xffffffffu, t, 16);
+                l[nt][e] = t;
+            }
+        const bool whole = ublk0 >= lo && p.u_blk[u + 1] <= hi;
+        if (whole) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int col = nt * 8 + 2 * quad + e;
+                    const int tq = col / g;
+                    if (tq >= nq) continue;
+                    const float inv = 1.f / l[nt][e];
+                    float* op = p.out + (static_cast<size_t>(row0 + tq) * p.H + h * g + col % g) * D;
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        op[mt * 16 + grp] = acc[mt][nt][e] * inv;
+                        op[mt * 16 + grp + 8] = acc[mt][nt][2 + e] * inv;
+                    }
+                }
+        } else {
+            const size_t seg = static_cast<size_t>(u) + c;
+            const size_t base = (seg * p.kvh + h) * kMaxCols;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int col = nt * 8 + 2 * quad + e;
+                    if (col / g >= nq) continue;
+                    float* po = p.part_o + (base + col) * D;
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        po[mt * 16 + grp] = acc[mt][nt][e];
+                        po[mt * 16 + grp + 8] = acc[mt][nt][2 + e];
+                    }
+                    if (grp == 0) {
+                        p.part_ml[(base + col) * 2] = m[nt][e];
+                        p.part_ml[(base + col) * 2 + 1] = l[nt][e];
+                    }
+                }
+        }
+    }
+}
+
+// One CTA per (split unit, KV head): combine the partials of every CTA that worked on it.
+__global__ void merge_kernel(const MergeParams p) {
+    const int e = blockIdx.x;
+    const int h = blockIdx.y;
+    const int u = p.split_u[e];
+    const int c0 = p.split_c0[e];
+    const int c1 = p.split_c1[e];
+    const int seq = p.u_seq[u];
+    const int row0 = p.offsets[seq] + p.u_t0[u];
+    const int ncols = p.u_n[u] * p.g;
+    for (int col = 0; col < ncols; ++col) {
+        float mmax = -INFINITY;
+        for (int c = c0; c <= c1; ++c) {
+            const size_t idx = ((static_cast<size_t>(u) + c) * p.kvh + h) * kMaxCols + col;
+            mmax = fmaxf(mmax, p.part_ml[idx * 2]);
+        }
+        float den = 0.f;
+        for (int c = c0; c <= c1; ++c) {
+            const size_t idx = ((static_cast<size_t>(u) + c) * p.kvh + h) * kMaxCols + col;
+            den += exp2f(p.part_ml[idx * 2] - mmax) * p.part_ml[idx * 2 + 1];
+        }
+        const float inv = 1.f / den;
+        float* op = p.out + (static_cast<size_t>(row0 + col / p.g) * p.H + h * p.g + col % p.g) * p.D;
+        for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+            float num = 0.f;
+            for (int c = c0; c <= c1; ++c) {
+                const size_t idx = ((static_cast<size_t>(u) + c) * p.kvh + h) * kMaxCols + col;
+                num += exp2f(p.part_ml[idx * 2] - mmax) * p.part_o[idx * p.D + d];
+            }
+            op[d] = num * inv;
+        }
+    }
+}
+
+template <int D, int NT>
+cudaError_t launch_tc_t(const CUtensorMap* tmk, const CUtensorMap* tmv, const TcParams& p,
+                        size_t smem, cudaStream_t st) {
+    auto kern = tc_attn_kernel<D, NT>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    kern<<<p.ncta, (p.kvh + 1) * 32, smem, st>>>(*tmk, *tmv, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t tc_smem_bytes(int D, int bs, int kvh, int stages) {
+    return static_cast<size_t>(stages) * 2 * bs * kvh * D * 2 + 2 * stages * sizeof(uint64_t) + 1024;
+}
+
+cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUtensorMap* tmv,
+                                const TcParams& p, size_t smem, cudaStream_t st) {
+    if (D == 64 && NT == 1) return launch_tc_t<64, 1>(tmk, tmv, p, smem, st);
+    if (D == 64 && NT == 2) return launch_tc_t<64, 2>(tmk, tmv, p, smem, st);
+    if (D == 128 && NT == 1) return launch_tc_t<128, 1>(tmk, tmv, p, smem, st);
+    if (D == 128 && NT == 2) return launch_tc_t<128, 2>(tmk, tmv, p, smem, st);
+    if (D == 256 && NT == 1) return launch_tc_t<256, 1>(tmk, tmv, p, smem, st);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st) {
+    if (nsplit <= 0) return cudaSuccess;
+    merge_kernel<<<dim3(nsplit, p.kvh), 128, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace pk

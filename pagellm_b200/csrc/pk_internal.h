@@ -1,0 +1,99 @@
+// Internal declarations shared by the libpagekv translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pk {
+
+// Most query columns (query token x head-in-group) one tensor-core warp carries.
+constexpr int kMaxCols = 16;
+// Largest number of KV heads the tensor-core kernel maps to warps of one CTA.
+constexpr int kTcMaxKvHeads = 8;
+
+// Parameters of the split-KV tensor-core attention kernel (bf16 pool).
+// A "unit" is a window of at most kMaxCols / g query tokens of one sequence; every unit
+// reads the blocks holding positions 0 .. unit_ctx-1 of its sequence. Units' blocks are
+// laid end to end and cut into ncta equal ranges, one per CTA.
+struct TcParams {
+    const float* q;        // [rows][H][D]
+    float* out;            // [rows][H][D]
+    float* part_o;         // [segments][kvh][kMaxCols][D]  un-normalised partial sums
+    float* part_ml;        // [segments][kvh][kMaxCols][2]  (running max, sum), log2 domain
+    int* err;              // device error word
+    const int32_t* indptr;  // [nseq+1] block-table CSR
+    const int32_t* ids;     // block ids
+    const int32_t* starts;  // [nseq]
+    const int32_t* offsets; // [nseq+1] first row of each sequence
+    const int32_t* u_seq;   // [nu] sequence of each unit
+    const int32_t* u_t0;    // [nu] first query token of the unit within its sequence
+    const int32_t* u_n;     // [nu] query tokens in the unit
+    const int32_t* u_blk;   // [nu+1] prefix sum of the units' block counts
+    int nu;
+    int total_blocks;
+    int ncta;
+    int kvh;
+    int g;
+    int H;
+    int bs;
+    int stages;
+    int per_head_layout;   // 0: one TMA box per K/V block, 1: one box per (block, head)
+    int64_t layer_slot0;   // first slot of the layer in the flat [layers*num_blocks*bs] axis
+    float qscale;          // log2(e) / sqrt(D)
+};
+
+struct MergeParams {
+    float* out;
+    const float* part_o;
+    const float* part_ml;
+    const int32_t* offsets;
+    const int32_t* u_seq;
+    const int32_t* u_t0;
+    const int32_t* u_n;
+    const int32_t* split_u;   // [nsplit] unit of each split entry
+    const int32_t* split_c0;  // first CTA that worked on it
+    const int32_t* split_c1;  // last CTA that worked on it
+    int kvh;
+    int g;
+    int H;
+    int D;
+};
+
+// CUDA-core attention for any pool dtype / head_dim (float32 pools, odd shapes).
+struct GenericParams {
+    const float* q;
+    float* out;
+    const void* pool_k;  // layer base
+    const void* pool_v;
+    const int32_t* row_seq;
+    const int32_t* indptr;
+    const int32_t* ids;
+    const int32_t* starts;
+    const int32_t* offsets;
+    const int32_t* rows;  // rows to process (indices into q/out)
+    int nrows;
+    int H;
+    int kvh;
+    int D;
+    int bs;
+    float scale;  // 1/sqrt(D)
+};
+
+cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUtensorMap* tmv,
+                                const TcParams& p, size_t smem, cudaStream_t st);
+size_t tc_smem_bytes(int D, int bs, int kvh, int stages);
+cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st);
+cudaError_t launch_generic_attention(int dtype, const GenericParams& p, cudaStream_t st);
+cudaError_t launch_plan_rows(const int32_t* row_seq, const int32_t* offsets, const int32_t* starts,
+                             const int32_t* indptr, const int32_t* ids, int bs, int64_t nrows,
+                             int64_t* positions, int64_t* slots, cudaStream_t st);
+cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k,
+                          const float* v, const int64_t* slots, int64_t n, int rowlen,
+                          cudaStream_t st);
+cudaError_t launch_copy_blocks(void* k, void* v, const int64_t* pairs, int64_t npairs, int layers,
+                               int64_t layer_bytes, int64_t block_bytes, cudaStream_t st);
+cudaError_t launch_slot_mapping(const int32_t* table, int64_t table_len, const int64_t* positions,
+                                int64_t n, int bs, int64_t* slots, int32_t* err, cudaStream_t st);
+
+}  // namespace pk

@@ -1,0 +1,273 @@
+// CUDA-core kernels of libpagekv: per-step row planning (positions + slot mapping),
+// K/V append through the slot mapping, copy-on-write block copies, and the generic
+// attention kernel used for float32 pools and for shapes the tensor-core kernel does not
+// take.
+
+#include <cuda_bf16.h>
+
+#include "pk_device.cuh"
+#include "pk_internal.h"
+
+namespace pk {
+
+namespace {
+
+// ------------------------------------------------------------------ rows of a step
+// PagedBatch.__init__ (pagellm cache/paged.py:410-420): position and slot of every row.
+__global__ void plan_rows_kernel(const int32_t* __restrict__ row_seq,
+                                 const int32_t* __restrict__ offsets,
+                                 const int32_t* __restrict__ starts,
+                                 const int32_t* __restrict__ indptr,
+                                 const int32_t* __restrict__ ids, int bs, int64_t nrows,
+                                 int64_t* __restrict__ positions, int64_t* __restrict__ slots) {
+    for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < nrows;
+         r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int s = row_seq[r];
+        const int64_t pos = static_cast<int64_t>(starts[s]) + (r - offsets[s]);
+        const int64_t blk = pos / bs;
+        positions[r] = pos;
+        slots[r] = static_cast<int64_t>(ids[indptr[s] + blk]) * bs + (pos - blk * bs);
+    }
+}
+
+// slot_mapping (cache/paged.py:303-306) over device arrays, with a range check.
+__global__ void slot_mapping_kernel(const int32_t* __restrict__ table, int64_t table_len,
+                                    const int64_t* __restrict__ positions, int64_t n, int bs,
+                                    int64_t* __restrict__ slots, int32_t* err) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t pos = positions[i];
+        const int64_t blk = pos >= 0 ? pos / bs : -1;
+        if (blk < 0 || blk >= table_len) {
+            slots[i] = -1;
+            if (err) atomicExch(err, 1);
+        } else {
+            slots[i] = static_cast<int64_t>(table[blk]) * bs + (pos - blk * bs);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ append
+// pool_flat[layer, slots[r]] = rows[r] (cache/paged.py:443-444). One thread per 4 values.
+__device__ __forceinline__ void store4(float* dst, float4 x) { *reinterpret_cast<float4*>(dst) = x; }
+__device__ __forceinline__ void store4(__nv_bfloat16* dst, float4 x) {
+    uint2 w;
+    w.x = pack_bf16(x.x, x.y);
+    w.y = pack_bf16(x.z, x.w);
+    *reinterpret_cast<uint2*>(dst) = w;
+}
+__device__ __forceinline__ void store1(float* dst, float x) { *dst = x; }
+__device__ __forceinline__ void store1(__nv_bfloat16* dst, float x) { *dst = __float2bfloat16_rn(x); }
+
+template <typename T>
+__global__ void append_vec4_kernel(T* __restrict__ pk_, T* __restrict__ pv_,
+                                   const float* __restrict__ k, const float* __restrict__ v,
+                                   const int64_t* __restrict__ slots, int64_t n, int rowlen) {
+    const int per_row = rowlen / 4;
+    const int64_t total = n * per_row;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / per_row;
+        const int c = static_cast<int>(i - r * per_row) * 4;
+        const int64_t dst = slots[r] * rowlen + c;
+        store4(pk_ + dst, *reinterpret_cast<const float4*>(k + r * rowlen + c));
+        store4(pv_ + dst, *reinterpret_cast<const float4*>(v + r * rowlen + c));
+    }
+}
+
+template <typename T>
+__global__ void append_scalar_kernel(T* __restrict__ pk_, T* __restrict__ pv_,
+                                     const float* __restrict__ k, const float* __restrict__ v,
+                                     const int64_t* __restrict__ slots, int64_t n, int rowlen) {
+    const int64_t total = n * rowlen;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / rowlen;
+        const int c = static_cast<int>(i - r * rowlen);
+        store1(pk_ + slots[r] * rowlen + c, k[i]);
+        store1(pv_ + slots[r] * rowlen + c, v[i]);
+    }
+}
+
+// ------------------------------------------------------------------ copy-on-write
+// k[:, dst] = k[:, src]; v[:, dst] = v[:, src] (cache/paged.py:294-296).
+// grid = (pairs, layers, 2 tensors); W = widest word dividing the block size.
+template <typename W>
+__global__ void copy_blocks_kernel(uint8_t* __restrict__ k, uint8_t* __restrict__ v,
+                                   const int64_t* __restrict__ pairs, int64_t layer_bytes,
+                                   int64_t block_bytes) {
+    const int64_t src = pairs[2 * blockIdx.x];
+    const int64_t dst = pairs[2 * blockIdx.x + 1];
+    uint8_t* base = (blockIdx.z == 0 ? k : v) + blockIdx.y * layer_bytes;
+    const W* s = reinterpret_cast<const W*>(base + src * block_bytes);
+    W* d = reinterpret_cast<W*>(base + dst * block_bytes);
+    const int64_t words = block_bytes / static_cast<int64_t>(sizeof(W));
+    for (int64_t i = threadIdx.x; i < words; i += blockDim.x) d[i] = s[i];
+}
+
+// ------------------------------------------------------------------ generic attention
+// One CTA (4 warps) per (row, query head). Keys are dealt to warps one at a time; each
+// warp keeps a running max / sum / output (the online softmax of cache/paged.py:309-352),
+// and the four warps are merged at the end. Lanes hold DPL dims of the head each.
+__device__ __forceinline__ float load_f(const float* p) { return *p; }
+__device__ __forceinline__ float load_f(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+template <typename T, int DPL>
+__global__ void __launch_bounds__(128) generic_attn_kernel(const GenericParams p) {
+    constexpr int NW = 4;
+    __shared__ float sm_m[NW], sm_l[NW];
+    extern __shared__ float sm_acc[];  // [NW][D]
+    const int r = p.rows[blockIdx.x];
+    const int head = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int seq = p.row_seq[r];
+    const int pos = p.starts[seq] + (r - p.offsets[seq]);  // sees keys 0..pos
+    const int g = p.H / p.kvh;
+    const int kh = head / g;
+    const T* kpool = static_cast<const T*>(p.pool_k);
+    const T* vpool = static_cast<const T*>(p.pool_v);
+    const int32_t* tbl = p.ids + p.indptr[seq];
+
+    float qv[DPL], acc[DPL];
+    const float* qp = p.q + (static_cast<size_t>(r) * p.H + head) * p.D;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+        const int d = lane + 32 * i;
+        qv[i] = d < p.D ? qp[d] : 0.f;
+        acc[i] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int j = warp; j <= pos; j += NW) {
+        const int64_t slot = static_cast<int64_t>(tbl[j / p.bs]) * p.bs + (j % p.bs);
+        const size_t off = (static_cast<size_t>(slot) * p.kvh + kh) * p.D;
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+            const int d = lane + 32 * i;
+            if (d < p.D) dot = fmaf(qv[i], load_f(kpool + off + d), dot);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        const float s = dot * p.scale;
+        const float mnew = fmaxf(m, s);
+        const float corr = expf(m - mnew);
+        const float w = expf(s - mnew);
+        l = l * corr + w;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+            const int d = lane + 32 * i;
+            const float vv = d < p.D ? load_f(vpool + off + d) : 0.f;
+            acc[i] = fmaf(w, vv, acc[i] * corr);
+        }
+        m = mnew;
+    }
+    if (lane == 0) {
+        sm_m[warp] = m;
+        sm_l[warp] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+        const int d = lane + 32 * i;
+        if (d < p.D) sm_acc[warp * p.D + d] = acc[i];
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, sm_m[w]);
+    float den = 0.f;
+    float wt[NW];
+    for (int w = 0; w < NW; ++w) {
+        wt[w] = sm_m[w] == -INFINITY ? 0.f : expf(sm_m[w] - mx);
+        den += wt[w] * sm_l[w];
+    }
+    float* op = p.out + (static_cast<size_t>(r) * p.H + head) * p.D;
+    for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+        float num = 0.f;
+        for (int w = 0; w < NW; ++w) num += wt[w] * sm_acc[w * p.D + d];
+        op[d] = num / den;
+    }
+}
+
+template <typename T>
+cudaError_t launch_generic_t(const GenericParams& p, cudaStream_t st) {
+    const int dpl = (p.D + 31) / 32;
+    const dim3 grid(p.nrows, p.H);
+    const size_t smem = 4 * p.D * sizeof(float);
+    if (dpl <= 1) generic_attn_kernel<T, 1><<<grid, 128, smem, st>>>(p);
+    else if (dpl <= 2) generic_attn_kernel<T, 2><<<grid, 128, smem, st>>>(p);
+    else if (dpl <= 4) generic_attn_kernel<T, 4><<<grid, 128, smem, st>>>(p);
+    else if (dpl <= 8) generic_attn_kernel<T, 8><<<grid, 128, smem, st>>>(p);
+    else if (dpl <= 16) generic_attn_kernel<T, 16><<<grid, 128, smem, st>>>(p);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+int grid_for(int64_t work, int threads) {
+    int64_t b = (work + threads - 1) / threads;
+    if (b < 1) b = 1;
+    if (b > 148 * 16) b = 148 * 16;
+    return static_cast<int>(b);
+}
+
+}  // namespace
+
+cudaError_t launch_plan_rows(const int32_t* row_seq, const int32_t* offsets, const int32_t* starts,
+                             const int32_t* indptr, const int32_t* ids, int bs, int64_t nrows,
+                             int64_t* positions, int64_t* slots, cudaStream_t st) {
+    if (nrows <= 0) return cudaSuccess;
+    plan_rows_kernel<<<grid_for(nrows, 256), 256, 0, st>>>(row_seq, offsets, starts, indptr, ids,
+                                                           bs, nrows, positions, slots);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_slot_mapping(const int32_t* table, int64_t table_len, const int64_t* positions,
+                                int64_t n, int bs, int64_t* slots, int32_t* err, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    slot_mapping_kernel<<<grid_for(n, 256), 256, 0, st>>>(table, table_len, positions, n, bs, slots,
+                                                          err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k,
+                          const float* v, const int64_t* slots, int64_t n, int rowlen,
+                          cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const bool vec = rowlen % 4 == 0;
+    const int64_t work = vec ? n * (rowlen / 4) : n * rowlen;
+    const int grid = grid_for(work, 256);
+    if (dtype == 0) {
+        float* pk_ = static_cast<float*>(pool_k_layer);
+        float* pv_ = static_cast<float*>(pool_v_layer);
+        if (vec) append_vec4_kernel<float><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, n, rowlen);
+        else append_scalar_kernel<float><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, n, rowlen);
+    } else {
+        auto* pk_ = static_cast<__nv_bfloat16*>(pool_k_layer);
+        auto* pv_ = static_cast<__nv_bfloat16*>(pool_v_layer);
+        if (vec) append_vec4_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, n, rowlen);
+        else append_scalar_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, n, rowlen);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_copy_blocks(void* k, void* v, const int64_t* pairs, int64_t npairs, int layers,
+                               int64_t layer_bytes, int64_t block_bytes, cudaStream_t st) {
+    if (npairs <= 0) return cudaSuccess;
+    const dim3 grid(static_cast<unsigned>(npairs), layers, 2);
+    auto* kb = static_cast<uint8_t*>(k);
+    auto* vb = static_cast<uint8_t*>(v);
+    if (block_bytes % 16 == 0)
+        copy_blocks_kernel<uint4><<<grid, 256, 0, st>>>(kb, vb, pairs, layer_bytes, block_bytes);
+    else if (block_bytes % 8 == 0)
+        copy_blocks_kernel<uint2><<<grid, 256, 0, st>>>(kb, vb, pairs, layer_bytes, block_bytes);
+    else if (block_bytes % 4 == 0)
+        copy_blocks_kernel<uint32_t><<<grid, 256, 0, st>>>(kb, vb, pairs, layer_bytes, block_bytes);
+    else
+        copy_blocks_kernel<uint16_t><<<grid, 256, 0, st>>>(kb, vb, pairs, layer_bytes, block_bytes);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_generic_attention(int dtype, const GenericParams& p, cudaStream_t st) {
+    if (p.nrows <= 0) return cudaSuccess;
+    return dtype == 0 ? launch_generic_t<float>(p, st) : launch_generic_t<__nv_bfloat16>(p, st);
+}
+
+}  // namespace pk
