@@ -129,6 +129,12 @@ PK_API int pk_batch_check(pk_batch* batch, void* stream);
  * kernel, [5] rows on the CUDA-core kernel, [6] kernels launched per write_and_attend. */
 PK_API int pk_batch_stats(const pk_batch* batch, int64_t* stats7);
 
+/* Per-kernel timing of this batch's own launches: with profiling on, CUDA events are
+ * recorded on the launching stream around every kernel. pk_batch_profile_read synchronises
+ * them and returns, per kind [0 append, 1 tensor-core attention, 2 partial merge,
+ * 3 CUDA-core attention], the summed milliseconds and launch counts, then resets. */
+PK_API int pk_batch_profile(pk_batch* batch, int enable);
+PK_API int pk_batch_profile_read(pk_batch* batch, double* ms4, int64_t* count4);
 /* Host-only dry run of the split-KV planner (no device needed): given per-unit block
  * counts, returns for each CTA its first block [ncta+1] (ncta = min(total, max_ctas)). */
 PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,

@@ -202,6 +202,11 @@ class PagedKVPool:
             pass
 
 
+def _aligned(t):
+    """``t`` itself when its data starts on a 16-byte boundary, else an aligned copy."""
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def _csr(block_tables):
     """(indptr int64, ids int32) from a list of per-sequence block lists / arrays."""
     if isinstance(block_tables, tuple) and len(block_tables) == 2 and isinstance(block_tables[0], np.ndarray) \
@@ -309,11 +314,11 @@ class PagedBatch:
         st = _stream(P.device)
         if hasattr(q, "is_cuda"):
             torch = _torch()
-            qd = q.to(P.device, torch.float32).contiguous()
+            qd = _aligned(q.to(P.device, torch.float32).contiguous())
             out = torch.empty_like(qd)
             if append:
-                kd = k.to(P.device, torch.float32).contiguous()
-                vd = v.to(P.device, torch.float32).contiguous()
+                kd = _aligned(k.to(P.device, torch.float32).contiguous())
+                vd = _aligned(v.to(P.device, torch.float32).contiguous())
                 rc = self._lib.pk_batch_write_and_attend(self._b, layer, H, qd.data_ptr(),
                                                          kd.data_ptr(), vd.data_ptr(),
                                                          out.data_ptr(), st)

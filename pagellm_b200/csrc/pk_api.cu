@@ -202,6 +202,12 @@ struct pk_batch {
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
     int launches = 0;
+    // Optional per-kernel timing: events recorded on the launching stream around each
+    // launch, resolved by pk_batch_profile_read.
+    bool profiling = false;
+    std::vector<cudaEvent_t> ev_pool;
+    size_t ev_used = 0;
+    std::vector<int> ev_kind;  // kind of each recorded (start, end) pair
 
     const int64_t* positions() const { return static_cast<const int64_t*>(rows.ptr); }
     const int64_t* slots() const { return static_cast<const int64_t*>(rows.ptr) + nrows; }
@@ -367,6 +373,35 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     return PK_OK;
 }
 
+// Kinds reported by pk_batch_profile_read.
+enum ProfKind { kProfAppend = 0, kProfTc = 1, kProfMerge = 2, kProfGeneric = 3, kProfKinds = 4 };
+
+cudaError_t prof_mark(pk_batch* B, cudaStream_t st) {
+    if (!B->profiling) return cudaSuccess;
+    if (B->ev_used == B->ev_pool.size()) {
+        cudaEvent_t e;
+        cudaError_t r = cudaEventCreate(&e);
+        if (r != cudaSuccess) return r;
+        B->ev_pool.push_back(e);
+    }
+    return cudaEventRecord(B->ev_pool[B->ev_used++], st);
+}
+
+cudaError_t prof_begin(pk_batch* B, cudaStream_t st) { return prof_mark(B, st); }
+
+cudaError_t prof_end(pk_batch* B, int kind, cudaStream_t st) {
+    if (!B->profiling) return cudaSuccess;
+    B->ev_kind.push_back(kind);
+    return prof_mark(B, st);
+}
+
+// Row buffers must be 16-byte aligned: the kernels read them with 8- and 16-byte loads.
+int check_aligned(const void* p, const char* what) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0)
+        return fail(PK_ERR_INVALID_ARG, "%s is not 16-byte aligned", what);
+    return PK_OK;
+}
+
 int check_heads(const pk_batch* B, int H) {
     if (H <= 0 || H % B->pool->kvh != 0)
         return fail(PK_ERR_INVALID_ARG, "n_heads=%d is not a positive multiple of n_kv_heads=%d", H,
@@ -408,7 +443,9 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.per_head_layout = P->tc_per_head;
         p.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
         p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
+        PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_tc_attention(P->d, B->nt, &P->tmk, &P->tmv, p, P->tc_smem, st));
+        PK_CUDA(prof_end(B, kProfTc, st));
         B->launches++;
         if (B->nsplit > 0) {
             pk::MergeParams m{};
@@ -426,7 +463,9 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
             m.g = g;
             m.H = H;
             m.D = P->d;
+            PK_CUDA(prof_begin(B, st));
             PK_CUDA(pk::launch_merge(m, B->nsplit, st));
+            PK_CUDA(prof_end(B, kProfMerge, st));
             B->launches++;
         }
     }
@@ -449,7 +488,9 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.D = P->d;
         p.bs = P->block_size;
         p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(P->d)));
+        PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_generic_attention(P->dtype, p, st));
+        PK_CUDA(prof_end(B, kProfGeneric, st));
         B->launches++;
     }
     return PK_OK;
@@ -636,6 +677,7 @@ int pk_batch_destroy(pk_batch* B) {
     B->err.release();
     B->ws.release();
     B->io.release();
+    for (cudaEvent_t e : B->ev_pool) cudaEventDestroy(e);
     delete B;
     return PK_OK;
 }
@@ -723,6 +765,7 @@ int pk_batch_attend(pk_batch* B, int layer, int n_heads, const float* q_dev, flo
     if (rc != PK_OK) return rc;
     if (layer < 0 || layer >= B->pool->n_layers) return fail(PK_ERR_OUT_OF_RANGE, "layer %d", layer);
     if (B->nrows > 0 && (!q_dev || !out_dev)) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    if ((rc = check_aligned(q_dev, "q")) || (rc = check_aligned(out_dev, "out"))) return rc;
     DeviceScope ds(B->pool->device);
     B->launches = 0;
     return attend_impl(B, layer, n_heads, q_dev, out_dev, static_cast<cudaStream_t>(stream));
@@ -737,12 +780,17 @@ int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* 
     if (layer < 0 || layer >= P->n_layers) return fail(PK_ERR_OUT_OF_RANGE, "layer %d", layer);
     if (B->nrows > 0 && (!q_dev || !k_dev || !v_dev || !out_dev))
         return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    if ((rc = check_aligned(q_dev, "q")) || (rc = check_aligned(k_dev, "k")) ||
+        (rc = check_aligned(v_dev, "v")) || (rc = check_aligned(out_dev, "out")))
+        return rc;
     DeviceScope ds(P->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     B->launches = 0;
     if (B->nrows > 0) {
+        PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_dev, v_dev,
                                   B->slots(), B->nrows, P->kvh * P->d, st));
+        PK_CUDA(prof_end(B, kProfAppend, st));
         B->launches++;
     }
     return attend_impl(B, layer, n_heads, q_dev, out_dev, st);
@@ -761,11 +809,12 @@ int pk_batch_write_and_attend_host(pk_batch* B, int layer, int n_heads, const fl
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t qn = static_cast<size_t>(B->nrows) * n_heads * P->d;
     const size_t kn = static_cast<size_t>(B->nrows) * P->kvh * P->d;
-    PK_CUDA(B->io.reserve((2 * qn + 2 * kn) * sizeof(float) + 1024));
+    const auto up = [](size_t floats) { return (floats + 63) & ~size_t(63); };  // 256 B
+    PK_CUDA(B->io.reserve((2 * up(qn) + 2 * up(kn)) * sizeof(float)));
     float* qd = static_cast<float*>(B->io.ptr);
-    float* kd = qd + qn;
-    float* vd = kd + kn;
-    float* od = vd + kn;
+    float* kd = qd + up(qn);
+    float* vd = kd + up(kn);
+    float* od = vd + up(kn);
     if (B->nrows > 0) {
         PK_CUDA(cudaMemcpyAsync(qd, q_host, qn * sizeof(float), cudaMemcpyHostToDevice, st));
         PK_CUDA(cudaMemcpyAsync(kd, k_host, kn * sizeof(float), cudaMemcpyHostToDevice, st));
@@ -802,6 +851,33 @@ int pk_batch_stats(const pk_batch* B, int64_t* s) {
     s[4] = B->nsplit;
     s[5] = B->ngeneric;
     s[6] = B->launches;
+    return PK_OK;
+}
+
+int pk_batch_profile(pk_batch* B, int enable) {
+    if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
+    B->profiling = enable != 0;
+    B->ev_used = 0;
+    B->ev_kind.clear();
+    return PK_OK;
+}
+
+int pk_batch_profile_read(pk_batch* B, double* ms4, int64_t* count4) {
+    if (!B || !ms4 || !count4) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    DeviceScope ds(B->pool->device);
+    for (int k = 0; k < kProfKinds; ++k) {
+        ms4[k] = 0.0;
+        count4[k] = 0;
+    }
+    for (size_t i = 0; i < B->ev_kind.size(); ++i) {
+        PK_CUDA(cudaEventSynchronize(B->ev_pool[2 * i + 1]));
+        float ms = 0.f;
+        PK_CUDA(cudaEventElapsedTime(&ms, B->ev_pool[2 * i], B->ev_pool[2 * i + 1]));
+        ms4[B->ev_kind[i]] += ms;
+        count4[B->ev_kind[i]] += 1;
+    }
+    B->ev_used = 0;
+    B->ev_kind.clear();
     return PK_OK;
 }
 

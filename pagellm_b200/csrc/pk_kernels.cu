@@ -231,7 +231,9 @@ cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, con
                           const float* v, const int64_t* slots, int64_t n, int rowlen,
                           cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    const bool vec = rowlen % 4 == 0;
+    // 4-wide path only when every row start is 16-byte aligned on both sides.
+    const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    const bool vec = rowlen % 4 == 0 && a16(k) && a16(v) && a16(pool_k_layer) && a16(pool_v_layer);
     const int64_t work = vec ? n * (rowlen / 4) : n * rowlen;
     const int grid = grid_for(work, 256);
     if (dtype == 0) {

@@ -1,0 +1,335 @@
+"""Parity of the CUDA path (libpagekv through its C ABI) with pagellm.
+
+* golden fixtures recorded from pagellm itself (``tests/golden``) replayed on the GPU;
+* every workload configuration C1..C5 against the CPU oracle on identical seeded inputs.
+
+Tolerances (stated per the north-star contract):
+* block tables, slot mapping, append and copy-on-write: bit-exact;
+* float32 pools: |got - ref| <= 1e-5 * |ref| + 1e-6 (relative 1e-5);
+* bfloat16 pools: max |got - ref| <= 2e-2 against the oracle run on the bf16-rounded K/V
+  widened to float32.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+from conftest import load_npz, step_inputs
+from gpu_util import (
+    Shape,
+    bf16_bits_of_tensor,
+    gather_rows,
+    make_pool,
+    oracle_rows,
+    step_inputs as dev_inputs,
+    torch_cuda,
+)
+
+from oracle import paged_oracle as po
+
+pytestmark = pytest.mark.gpu
+
+F32_RTOL, F32_ATOL = 1e-5, 1e-6
+BF16_ATOL = 2e-2
+
+
+def _close(got, ref, bf16: bool):
+    if bf16:
+        err = float(np.max(np.abs(got - ref))) if got.size else 0.0
+        assert err <= BF16_ATOL, f"max abs err {err}"
+    else:
+        np.testing.assert_allclose(got, ref, rtol=F32_RTOL, atol=F32_ATOL)
+
+
+# ----------------------------------------------------------------------------- golden
+@pytest.mark.parametrize("name", ["c1_gather", "c1_paged", "mixed_gather", "mixed_paged",
+                                  "bf16_c2shape", "bf16_verify"])
+def test_golden_step(name):
+    torch = torch_cuda()
+    from pagellm_b200.cache import PagedBatch, PagedKVPool
+
+    c = step_inputs(load_npz(f"step_{name}.npz"))
+    pool = PagedKVPool(Shape(1, c["KVH"], c["d"]), c["num_blocks"], c["bs"],
+                       "bfloat16" if c["bf16"] else np.float32)
+    idx = torch.as_tensor(c["ctx_slots"], device="cuda")
+    pool.k_flat[0].index_copy_(0, idx, torch.as_tensor(c["kc"], device="cuda").to(pool.k.dtype))
+    pool.v_flat[0].index_copy_(0, idx, torch.as_tensor(c["vc"], device="cuda").to(pool.v.dtype))
+    attn = "paged" if name.endswith("paged") else "gather"
+    batch = PagedBatch(pool, c["tables"], c["starts"], c["n_new"], attn)
+    np.testing.assert_array_equal(batch.positions, c["positions"])
+    np.testing.assert_array_equal(batch.slots, c["slots"])
+    out = batch.write_and_attend(0, c["q"], c["k"], c["v"])
+    assert out.dtype == c["q"].dtype and out.shape == c["q"].shape
+    _close(out, c["out"], c["bf16"])
+    kr, vr = gather_rows(pool, 0, c["slots"])
+    np.testing.assert_array_equal(kr, c["k"])
+    np.testing.assert_array_equal(vr, c["v"])
+
+
+def test_golden_paged_attention_cases():
+    from pagellm_b200.cache import paged_attention
+
+    z = load_npz("paged_attention_cases.npz")
+    for ci in range(int(z["ncases"])):
+        ctx, n, bs = (int(x) for x in z[f"c{ci}_meta"])
+        got = paged_attention(z[f"c{ci}_q"], z[f"c{ci}_kp"], z[f"c{ci}_vp"],
+                              z[f"c{ci}_table"].tolist(), ctx, ctx - n)
+        assert got.dtype == np.float64
+        np.testing.assert_allclose(got, z[f"c{ci}_paged"], rtol=F32_RTOL, atol=F32_ATOL)
+
+
+def test_golden_batched_decode_garbage_padding():
+    from pagellm_b200.cache import batched_decode_attention
+
+    z = load_npz("batched_decode.npz")
+    got = batched_decode_attention(z["q"], z["k"], z["v"], z["valid"])
+    np.testing.assert_allclose(got, z["out"], rtol=F32_RTOL, atol=F32_ATOL)
+
+
+def test_golden_slot_mapping():
+    from pagellm_b200.cache import slot_mapping
+
+    z = load_npz("slot_mapping.npz")
+    for ci in range(int(z["ncases"])):
+        got = slot_mapping(z[f"s{ci}_table"], z[f"s{ci}_pos"], int(z[f"s{ci}_bs"]))
+        assert got.dtype == np.int64
+        np.testing.assert_array_equal(got, z[f"s{ci}_slots"])
+
+
+# ----------------------------------------------------------------------------- configs
+def _run_config(w, check_seqs, seed=0):
+    torch = torch_cuda()
+    from pagellm_b200.cache import PagedBatch
+
+    pool = make_pool(w, seed)
+    if w.cow_pairs:
+        src = np.array([p[0] for p in w.cow_pairs])
+        before = pool.k[0, torch.as_tensor(src, device="cuda")].clone()
+        pool.copy_blocks(w.cow_pairs)
+        dst = torch.as_tensor(np.array([p[1] for p in w.cow_pairs]), device="cuda")
+        assert torch.equal(pool.k[0, dst], before)
+    batch = PagedBatch(pool, w.tables, w.starts, w.n_new)
+    meta = po.StepMeta(w.tables, w.starts, w.n_new, w.bs)
+    np.testing.assert_array_equal(batch.slots, meta.slots)
+    np.testing.assert_array_equal(batch.positions, meta.positions)
+    q, k, v = dev_inputs(w, seed + 1)
+    out = batch.write_and_attend(0, q, k, v)
+    batch.check()
+    # append: pool rows at the step's slots hold k, v rounded to the pool dtype, bit-exact
+    sl = torch.as_tensor(meta.slots, device="cuda")
+    if w.dtype == "bf16":
+        assert np.array_equal(bf16_bits_of_tensor(pool.k_flat[0].index_select(0, sl)),
+                              po.bf16_bits(k.cpu().numpy()).reshape(k.shape))
+        assert np.array_equal(bf16_bits_of_tensor(pool.v_flat[0].index_select(0, sl)),
+                              po.bf16_bits(v.cpu().numpy()).reshape(v.shape))
+    else:
+        assert torch.equal(pool.k_flat[0].index_select(0, sl), k)
+        assert torch.equal(pool.v_flat[0].index_select(0, sl), v)
+    got = out.cpu().numpy()
+    qh = q.cpu().numpy()
+    for i, (rows, ref) in oracle_rows(pool, w, check_seqs, qh).items():
+        _close(got[rows], ref, w.dtype == "bf16")
+    assert np.isfinite(got).all()
+    return pool, batch, got
+
+
+def test_c1_full_fp32():
+    from pagellm_b200 import workloads
+
+    w = workloads.c1(0)
+    _run_config(w, range(w.nseq))
+
+
+def test_c2_llama8b_decode_bf16():
+    from pagellm_b200 import workloads
+
+    w = workloads.c2(0)
+    L = w.ctx_lens
+    seqs = sorted({0, w.nseq - 1, int(np.argmax(L)), int(np.argmin(L)), 17, 40})
+    pool, batch, _ = _run_config(w, seqs)
+    assert pool.tensor_core_path[0], pool.tensor_core_path[1]
+    st = batch.stats()
+    assert st["tc_units"] == w.nseq and st["generic_rows"] == 0 and st["tc_ctas"] > 0
+
+
+def test_c2_split_units_merge():
+    """Two long sequences over ~150 CTAs: every unit is cut across many CTAs, so the
+    partial (max, sum, output) merge carries the whole result."""
+    from pagellm_b200 import workloads
+
+    w = workloads.c2(3, batch=2)
+    _, batch, _ = _run_config(w, [0, 1])
+    assert batch.stats()["split_units"] == 2
+
+
+def test_c3_mixed_chunked_prefill():
+    from pagellm_b200 import workloads
+
+    w = workloads.c3(0)
+    _run_config(w, [0, 7, 15, 16])
+
+
+def test_c4_prefix_sharing_cow_verify():
+    from pagellm_b200 import workloads
+
+    w = workloads.c4(0)
+    assert len(w.cow_pairs) == 192
+    _run_config(w, [0, 1, 2, 3, 100, 255])
+
+
+def test_c5_long_context_shard():
+    from pagellm_b200 import workloads
+
+    L = workloads.c5_lengths(0)
+    sel = [int(np.argmax(L)), int(np.argmin(L)), 5, 77]
+    w = workloads.c5(0, lengths=L[sel])
+    _run_config(w, range(w.nseq))
+
+
+def test_c5_head_sharded_shard_matches_full():
+    """Head-sharded variant: a rank holding KV heads [h0, h0+kh) computes exactly the
+    full computation's output for query heads [h0*g, (h0+kh)*g)."""
+    torch = torch_cuda()
+    from pagellm_b200 import workloads
+    from pagellm_b200.cache import PagedBatch
+
+    L = workloads.c5_lengths(0)[:6]
+    full = workloads.c5(0, lengths=L)
+    pool = make_pool(full, 0)
+    q, k, v = dev_inputs(full, 1)
+    out_full = PagedBatch(pool, full.tables, full.starts, full.n_new).write_and_attend(0, q, k, v)
+    kh, g = 2, full.H // full.KVH
+    for h0 in (0, 6):
+        part = workloads.c5(0, lengths=L, kv_heads=kh)
+        sp = make_pool(part, 0)
+        sp.k_flat[0].copy_(pool.k_flat[0][:, h0:h0 + kh])
+        sp.v_flat[0].copy_(pool.v_flat[0][:, h0:h0 + kh])
+        qs = q[:, h0 * g:(h0 + kh) * g].contiguous()
+        ks, vs = k[:, h0:h0 + kh].contiguous(), v[:, h0:h0 + kh].contiguous()
+        o = PagedBatch(sp, part.tables, part.starts, part.n_new).write_and_attend(0, qs, ks, vs)
+        assert torch.equal(o, out_full[:, h0 * g:(h0 + kh) * g])
+
+
+# ----------------------------------------------------------------------------- bit-exact ops
+def test_copy_blocks_bit_exact_and_ordered():
+    torch = torch_cuda()
+    from pagellm_b200 import workloads
+
+    w = workloads.c2(1, batch=4)
+    pool = make_pool(w, 5, layers=2)
+    kh = pool.k.float().cpu().numpy()
+    vh = pool.v.float().cpu().numpy()
+    # 3 -> 7 then 7 -> 9 must see the copied data (list order), 1 -> 2 independent
+    pairs = [(3, 7), (1, 2), (7, 9), (11, 3)]
+    po.copy_blocks(kh, vh, pairs)
+    pool.copy_blocks(pairs)
+    torch.cuda.synchronize()
+    assert np.array_equal(pool.k.float().cpu().numpy(), kh)
+    assert np.array_equal(pool.v.float().cpu().numpy(), vh)
+    with pytest.raises(IndexError):
+        pool.copy_blocks([(0, w.num_blocks)])
+
+
+def test_fp32_pool_append_exact():
+    torch = torch_cuda()
+    from pagellm_b200 import workloads
+    from pagellm_b200.cache import PagedBatch
+
+    w = workloads.c1(2)
+    pool = make_pool(w, 3, layers=3)
+    q, k, v = dev_inputs(w, 4)
+    b = PagedBatch(pool, w.tables, w.starts, w.n_new)
+    b.write_and_attend(2, q, k, v)
+    sl = torch.as_tensor(b.slots, device="cuda")
+    assert torch.equal(pool.k_flat[2].index_select(0, sl), k)
+    assert torch.equal(pool.v_flat[2].index_select(0, sl), v)
+
+
+# ----------------------------------------------------------------------------- edges
+def test_edge_cases_context_lengths():
+    """ctx 1, block-aligned contexts, a zero-row sequence and mixed window sizes."""
+    torch = torch_cuda()
+    from pagellm_b200.cache import PagedBatch, PagedKVPool
+
+    for dt, bf in ((np.float32, False), ("bfloat16", True)):
+        pool = PagedKVPool(Shape(1, 8, 128), 64, 16, dt)
+        g = torch.Generator(device="cuda").manual_seed(0)
+        pool.k.copy_(torch.randn(pool.k.shape, generator=g, device="cuda").to(pool.k.dtype))
+        pool.v.copy_(torch.randn(pool.v.shape, generator=g, device="cuda").to(pool.v.dtype))
+        ctx = [1, 16, 32, 17, 40, 7, 64]
+        n_new = [1, 1, 16, 1, 0, 3, 9]
+        perm = np.random.default_rng(0).permutation(64)
+        tables, used = [], 0
+        for c_ in ctx:
+            nb = -(-c_ // 16)
+            tables.append(perm[used:used + nb].tolist())
+            used += nb
+        starts = [c_ - n for c_, n in zip(ctx, n_new)]
+        b = PagedBatch(pool, tables, starts, n_new)
+        rows = sum(n_new)
+        q = torch.randn((rows, 32, 128), device="cuda")
+        k = torch.randn((rows, 8, 128), device="cuda")
+        v = torch.randn((rows, 8, 128), device="cuda")
+        out = b.write_and_attend(0, q, k, v).cpu().numpy()
+        meta = po.StepMeta(tables, starts, n_new, 16)
+        qh = q.cpu().numpy()
+        for i in range(len(ctx)):
+            if n_new[i] == 0:
+                continue
+            kc, vc = gather_rows(pool, 0, meta.ctx_slots[i])
+            a, z = meta.offsets[i], meta.offsets[i + 1]
+            _close(out[a:z], po.attention_dense(qh[a:z], kc, vc, starts[i]), bf)
+
+
+def test_empty_batch_and_errors():
+    torch = torch_cuda()
+    from pagellm_b200.cache import PagedBatch, PagedKVPool
+
+    pool = PagedKVPool(Shape(2, 2, 32), 8, 16)
+    b = PagedBatch(pool, [], [], [])
+    out = b.write_and_attend(0, np.zeros((0, 4, 32), np.float32), np.zeros((0, 2, 32), np.float32),
+                             np.zeros((0, 2, 32), np.float32))
+    assert out.shape == (0, 4, 32)
+    with pytest.raises(IndexError):  # table too short for position 16
+        PagedBatch(pool, [[0]], [16], [1])
+    with pytest.raises(IndexError):  # block id outside the pool
+        PagedBatch(pool, [[8]], [0], [1])
+    with pytest.raises(IndexError):
+        PagedBatch(pool, [[-1]], [0], [1])
+    with pytest.raises(ValueError):
+        PagedBatch(pool, [[0]], [0], [1], attn="flash")
+    b = PagedBatch(pool, [[0]], [0], [1])
+    with pytest.raises(ValueError):  # 3 query heads is not a multiple of 2 KV heads
+        b.write_and_attend(0, np.zeros((1, 3, 32), np.float32), np.zeros((1, 2, 32), np.float32),
+                           np.zeros((1, 2, 32), np.float32))
+    with pytest.raises(IndexError):
+        b.write_and_attend(2, np.zeros((1, 4, 32), np.float32), np.zeros((1, 2, 32), np.float32),
+                           np.zeros((1, 2, 32), np.float32))
+    torch.cuda.synchronize()
+
+
+def test_decode_loop_reuses_batch_handles():
+    """Ten decode steps through fresh PagedBatch objects: handles are recycled, and each
+    step matches the oracle on the cache the previous steps built."""
+    torch = torch_cuda()
+    from pagellm_b200 import workloads
+    from pagellm_b200.cache import PagedBatch
+
+    w = workloads.c2(4, batch=6)
+    pool = make_pool(w, 0)
+    starts = w.starts.copy()
+    spare = sorted(set(range(w.num_blocks)) - set(np.concatenate(w.tables).tolist()))
+    tables = [np.concatenate([t, [spare[i]]]).astype(np.int32) for i, t in enumerate(w.tables)]
+    for step in range(10):
+        b = PagedBatch(pool, tables, starts, w.n_new)
+        q = torch.randn((w.nseq, w.H, w.D), device="cuda")
+        k = torch.randn((w.nseq, w.KVH, w.D), device="cuda")
+        v = torch.randn((w.nseq, w.KVH, w.D), device="cuda")
+        out = b.write_and_attend(0, q, k, v).cpu().numpy()
+        if step in (0, 9):
+            meta = po.StepMeta(tables, starts, w.n_new, w.bs)
+            for i in (0, 5):
+                kc, vc = gather_rows(pool, 0, meta.ctx_slots[i])
+                _close(out[i:i + 1], po.attention_dense(q.cpu().numpy()[i:i + 1], kc, vc, int(starts[i])), True)
+        starts = starts + 1
+    assert len(pool._idle_batches) <= 2
