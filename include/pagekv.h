@@ -141,6 +141,27 @@ PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int ma
                       int64_t* cta_first_block, int* ncta);
 
 
+/* Decode attention that allocates nothing. No counterpart in the reference: pagellm has no
+ * device memory at all. For callers that cannot call cudaMalloc - a serving framework that
+ * hands out all of HBM through its own caching allocator, or a plugin host that forbids
+ * cudaMalloc/cudaFree on the request path because cudaFree synchronises the device.
+ * Sequence i has ctx_lens[i] tokens in the pool (its table: table_ids[table_indptr[i] ..],
+ * host arrays); its one query row q_dev[i] sits at position ctx_lens[i]-1 and attends over
+ * positions 0..ctx_lens[i]-1 (no append); out_dev[i] receives the result. Requires a pool
+ * the tensor-core kernel serves and at most 8 query heads per KV head.
+ * All scratch (tables, plan, partial results) lives in a 16 MiB array that every GPU
+ * loading this library holds until exit; a call that needs more, or has more than 512
+ * sequences, fails with PK_ERR_INVALID_ARG before launching anything. Every call on a device
+ * shares that array and leaves it dirty (the error word is cleared per call): calls that
+ * overlap on the GPU race. The first call on a device looks the array's address up - make it
+ * before any stream capture. err_dev (optional) receives 1 if a bounded device wait gave up.
+ * Pageable table_ids / ctx arrays are copied before return; pinned ones must stay valid until
+ * the stream has run the call. */
+PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, int n_heads, int nseq,
+                                   const int64_t* table_indptr, const int32_t* table_ids,
+                                   const int64_t* ctx_lens, const float* q_dev, float* out_dev,
+                                   int32_t* err_dev, void* stream);
+
 /* ---------------------------------------------------------------- block bookkeeping
  * Host-side replacement of BlockAllocator and BlockManager (cache/paged.py:47-274): FIFO
  * free list, int64 ref counts, LRU set of evictable cached blocks, hash -> block map and

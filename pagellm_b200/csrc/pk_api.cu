@@ -498,6 +498,27 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
 
 }  // namespace
 
+void pk_set_last_error(const char* msg) { g_err = msg ? msg : ""; }
+
+bool pk_pool_view(const pk_pool* P, pk::PoolView* v) {
+    if (!P || !v) return false;
+    v->device = P->device;
+    v->n_layers = P->n_layers;
+    v->num_blocks = P->num_blocks;
+    v->block_size = P->block_size;
+    v->kvh = P->kvh;
+    v->d = P->d;
+    v->dtype = P->dtype;
+    v->num_sms = P->num_sms;
+    v->tc_ok = P->tc_ok;
+    v->tc_per_head = P->tc_per_head;
+    v->tc_stages = P->tc_stages;
+    v->tc_smem = P->tc_smem;
+    v->tmk = &P->tmk;
+    v->tmv = &P->tmv;
+    return true;
+}
+
 extern "C" {
 
 const char* pk_last_error(void) { return g_err.c_str(); }

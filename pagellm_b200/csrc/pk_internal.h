@@ -80,6 +80,24 @@ struct GenericParams {
     float scale;  // 1/sqrt(D)
 };
 
+// Read-only view of a pool's fields for entry points outside pk_api.cu.
+struct PoolView {
+    int device;
+    int n_layers;
+    int64_t num_blocks;
+    int block_size;
+    int kvh;
+    int d;
+    int dtype;
+    int num_sms;
+    bool tc_ok;
+    int tc_per_head;
+    int tc_stages;
+    size_t tc_smem;
+    const CUtensorMap* tmk;
+    const CUtensorMap* tmv;
+};
+
 cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUtensorMap* tmv,
                                 const TcParams& p, size_t smem, cudaStream_t st);
 size_t tc_smem_bytes(int D, int bs, int kvh, int stages);
@@ -97,3 +115,9 @@ cudaError_t launch_slot_mapping(const int32_t* table, int64_t table_len, const i
                                 int64_t n, int bs, int64_t* slots, int32_t* err, cudaStream_t st);
 
 }  // namespace pk
+
+struct pk_pool;
+// Fills *out from `pool`; false if pool is NULL.
+bool pk_pool_view(const pk_pool* pool, pk::PoolView* out);
+// Sets the message pk_last_error() returns on this thread.
+void pk_set_last_error(const char* msg);
