@@ -105,11 +105,13 @@ _lib: C.CDLL | None = None
 
 
 def load(path: str | os.PathLike | None = None) -> C.CDLL:
-    """Load (once) and type the library. Raises if it has not been built."""
+    """Load (once) and type the library. Raises if it has not been built.
+
+    The in-tree build is used unless ``PAGEKV_LIB`` names another libpagekv.so."""
     global _lib
     if _lib is not None and path is None:
         return _lib
-    p = Path(path) if path else LIB_PATH
+    p = Path(path) if path else Path(os.environ.get("PAGEKV_LIB", LIB_PATH))
     if not p.exists():
         raise ImportError(
             f"{p} is missing: build it with `python -m pagellm_b200.build` (nvcc, sm_100a)"

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import ctypes as C
 import itertools
+import sys
 import weakref
 
 import numpy as np
@@ -202,6 +203,39 @@ class PagedKVPool:
             pass
 
 
+class _PinnedResults:
+    """Page-locked float32 result buffers, reused once the caller has dropped them.
+
+    Device-to-host copies into pageable memory run at a fraction of DMA speed, and pinning
+    a fresh buffer per call costs more than the copy; so results are handed out in pinned
+    arrays from a small cache, and a cached array is reused only when nothing outside the
+    cache still refers to it."""
+
+    def __init__(self, keep: int = 4):
+        self.keep = keep
+        self.bufs: list[np.ndarray] = []
+
+    def get(self, shape) -> np.ndarray:
+        shape = tuple(int(x) for x in shape)
+        for i, b in enumerate(self.bufs):
+            # references: the list slot, the loop variable, getrefcount's argument
+            if b.shape == shape and sys.getrefcount(b) <= 3:
+                return b
+        torch = _torch()
+        b = torch.empty(shape, dtype=torch.float32, pin_memory=True).numpy()
+        self.bufs.append(b)
+        if len(self.bufs) > self.keep:
+            self.bufs.pop(0)
+        return b
+
+
+_PINNED = _PinnedResults()
+
+
+def _pinned_empty(shape) -> np.ndarray:
+    return _PINNED.get(shape)
+
+
 def _aligned(t):
     """``t`` itself when its data starts on a 16-byte boundary, else an aligned copy."""
     return t if t.data_ptr() % 16 == 0 else t.clone()
@@ -256,9 +290,8 @@ class PagedBatch:
         self.offsets = np.zeros(len(n_new_a) + 1, dtype=np.int64)
         np.cumsum(n_new_a, out=self.offsets[1:])
         self.offsets = self.offsets.astype(int)
-        total = int(self.offsets[-1])
-        self.positions = (np.repeat(starts_a - self.offsets[:-1], n_new_a)
-                          + np.arange(total, dtype=np.int64)) if total else np.zeros(0, np.int64)
+        self._starts_a, self._n_new_a = starts_a, n_new_a
+        self._positions = None
         lib = _lib.load()
         self._lib = lib
         self._b = pool._acquire_batch()
@@ -272,6 +305,15 @@ class PagedBatch:
         self._slots = None
 
     # ------------------------------------------------------------------ step metadata
+    @property
+    def positions(self) -> np.ndarray:
+        """int64 absolute position of every new row (paged.py:412-414)."""
+        if self._positions is None:
+            total = int(self.offsets[-1])
+            self._positions = (np.repeat(self._starts_a - self.offsets[:-1], self._n_new_a)
+                               + np.arange(total, dtype=np.int64)) if total else np.zeros(0, np.int64)
+        return self._positions
+
     @property
     def slots(self) -> np.ndarray:
         """int64 pool slot of every new row, as computed by the device slot-mapping kernel."""
@@ -327,7 +369,7 @@ class PagedBatch:
             _lib.check(rc)
             return out if q.dtype == torch.float32 else out.to(q.dtype)
         qh = np.ascontiguousarray(q, dtype=np.float32)
-        out = np.empty(qh.shape, dtype=np.float32)
+        out = _pinned_empty(qh.shape)
         if append:
             kh = np.ascontiguousarray(k, dtype=np.float32)
             vh = np.ascontiguousarray(v, dtype=np.float32)

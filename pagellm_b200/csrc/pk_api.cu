@@ -11,6 +11,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "pagekv.h"
@@ -188,7 +189,14 @@ struct pk_batch {
     int nseq = 0;
     int64_t nrows = 0;
     std::vector<int32_t> indptr, ids, starts, nnew, offsets, row_seq;
-    Uploader meta;  // 0 indptr, 1 ids, 2 starts, 3 offsets, 4 row_seq
+    Uploader meta;  // 0 indptr, 1 ids, 2 starts, 3 offsets, 4 row_seq, 5 append rows
+    // Fused append is exact only if every slot written this step is read by nobody but the
+    // writing row's own unit; otherwise (shared or repeated blocks, duplicate slots) the
+    // step appends first with a separate kernel, last writer per slot, as pagellm does.
+    bool fuse_append_ok = true;
+    std::vector<int32_t> app_rows;  // winner rows when slots repeat (else empty = all rows)
+    std::vector<int32_t> writer_seq, writer_idx;  // per block id, scratch of the check
+    DevBuf counters;  // per (unit, KV head) merge counters, zero between launches
     DevBuf rows;    // positions [nrows] then slots [nrows]
     DevBuf err;     // one int
     // attention plan for plan_H query heads
@@ -356,7 +364,10 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         const size_t segs = static_cast<size_t>(B->nu) + B->ncta;
         B->ws_part_o_floats = segs * P->kvh * pk::kMaxCols * P->d;
         const size_t ws_bytes = (B->ws_part_o_floats + segs * P->kvh * pk::kMaxCols * 2) * sizeof(float);
-        if (B->nsplit > 0 || true) PK_CUDA(B->ws.reserve(ws_bytes));
+        PK_CUDA(B->ws.reserve(ws_bytes));
+        const size_t nctr = static_cast<size_t>(B->nu) * P->kvh;
+        PK_CUDA(B->counters.reserve(nctr * sizeof(int)));
+        PK_CUDA(cudaMemsetAsync(B->counters.ptr, 0, nctr * sizeof(int), st));
     }
     B->plan.begin();
     B->plan.add(B->u_seq.data(), B->u_seq.size() * 4);
@@ -409,7 +420,8 @@ int check_heads(const pk_batch* B, int H) {
     return PK_OK;
 }
 
-int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaStream_t st) {
+int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaStream_t st,
+                const float* k_new = nullptr, const float* v_new = nullptr) {
     pk_pool* P = B->pool;
     if (B->plan_H != H) {
         int rc = build_attention_plan(B, H, st);
@@ -443,11 +455,16 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.per_head_layout = P->tc_per_head;
         p.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
         p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
+        p.counters = static_cast<int*>(B->counters.ptr);
+        p.k_new = k_new;
+        p.v_new = v_new;
+        p.pool_k = reinterpret_cast<__nv_bfloat16*>(P->k_layer(layer));
+        p.pool_v = reinterpret_cast<__nv_bfloat16*>(P->v_layer(layer));
         PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_tc_attention(P->d, B->nt, &P->tmk, &P->tmv, p, P->tc_smem, st));
         PK_CUDA(prof_end(B, kProfTc, st));
         B->launches++;
-        if (B->nsplit > 0) {
+        if (B->nsplit > 0 && p.counters == nullptr) {
             pk::MergeParams m{};
             m.out = out;
             m.part_o = p.part_o;
@@ -659,7 +676,7 @@ int pk_pool_append(pk_pool* pool, int layer, const float* k_dev, const float* v_
     if (!k_dev || !v_dev || !slots_dev) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
     DeviceScope ds(pool->device);
     PK_CUDA(pk::launch_append(pool->dtype, pool->k_layer(layer), pool->v_layer(layer), k_dev, v_dev,
-                              slots_dev, n, pool->kvh * pool->d, static_cast<cudaStream_t>(stream)));
+                              slots_dev, nullptr, n, pool->kvh * pool->d, static_cast<cudaStream_t>(stream)));
     return PK_OK;
 }
 
@@ -697,6 +714,7 @@ int pk_batch_destroy(pk_batch* B) {
     B->rows.release();
     B->err.release();
     B->ws.release();
+    B->counters.release();
     B->io.release();
     for (cudaEvent_t e : B->ev_pool) cudaEventDestroy(e);
     delete B;
@@ -751,6 +769,57 @@ int pk_batch_plan(pk_batch* B, int nseq, const int64_t* table_indptr, const int3
         B->offsets.push_back(static_cast<int32_t>(rows));
         for (int64_t r = 0; r < n; ++r) B->row_seq.push_back(i);
     }
+    // Written blocks: which (sequence, table index) writes each; any other reference to
+    // such a block, or two writers, rules the fused append out for this step.
+    B->fuse_append_ok = true;
+    B->app_rows.clear();
+    if (B->writer_seq.size() != static_cast<size_t>(P->num_blocks)) {
+        B->writer_seq.assign(P->num_blocks, -1);
+        B->writer_idx.assign(P->num_blocks, -1);
+    }
+    std::vector<int32_t> touched;
+    bool dup_slot = false;
+    for (int i = 0; i < nseq && B->fuse_append_ok; ++i) {
+        for (int64_t pos = B->starts[i]; pos < static_cast<int64_t>(B->starts[i]) + B->nnew[i]; ++pos) {
+            const int32_t j = static_cast<int32_t>(pos / bs);
+            const int32_t b = B->ids[B->indptr[i] + j];
+            if (B->writer_seq[b] < 0) {
+                B->writer_seq[b] = i;
+                B->writer_idx[b] = j;
+                touched.push_back(b);
+            } else if (B->writer_seq[b] != i || B->writer_idx[b] != j) {
+                B->fuse_append_ok = false;
+                dup_slot = true;  // may share a slot: resolve last writers below
+                break;
+            }
+        }
+    }
+    for (int i = 0; i < nseq && B->fuse_append_ok; ++i)
+        for (int32_t j = 0; j < B->indptr[i + 1] - B->indptr[i]; ++j) {
+            const int32_t b = B->ids[B->indptr[i] + j];
+            if (B->writer_seq[b] >= 0 && (B->writer_seq[b] != i || B->writer_idx[b] != j)) {
+                B->fuse_append_ok = false;
+                break;
+            }
+        }
+    for (int32_t b : touched) B->writer_seq[b] = B->writer_idx[b] = -1;
+    if (dup_slot) {
+        // last row wins per slot (numpy fancy assignment order)
+        std::unordered_map<int64_t, int32_t> last;
+        last.reserve(static_cast<size_t>(rows) * 2);
+        int32_t r = 0;
+        for (int i = 0; i < nseq; ++i)
+            for (int64_t pos = B->starts[i]; pos < static_cast<int64_t>(B->starts[i]) + B->nnew[i]; ++pos, ++r) {
+                const int64_t slot = static_cast<int64_t>(B->ids[B->indptr[i] + pos / bs]) * bs + pos % bs;
+                last[slot] = r;
+            }
+        r = 0;
+        for (int i = 0; i < nseq; ++i)
+            for (int64_t pos = B->starts[i]; pos < static_cast<int64_t>(B->starts[i]) + B->nnew[i]; ++pos, ++r) {
+                const int64_t slot = static_cast<int64_t>(B->ids[B->indptr[i] + pos / bs]) * bs + pos % bs;
+                if (last[slot] == r) B->app_rows.push_back(r);
+            }
+    }
     B->nseq = nseq;
     B->nrows = rows;
     if (n_rows) *n_rows = rows;
@@ -762,6 +831,7 @@ int pk_batch_plan(pk_batch* B, int nseq, const int64_t* table_indptr, const int3
     B->meta.add(B->starts.data(), B->starts.size() * 4);
     B->meta.add(B->offsets.data(), B->offsets.size() * 4);
     B->meta.add(B->row_seq.data(), B->row_seq.size() * 4);
+    B->meta.add(B->app_rows.data(), B->app_rows.size() * 4);
     int rc = B->meta.commit(st);
     if (rc != PK_OK) return rc;
     PK_CUDA(B->rows.reserve(static_cast<size_t>(std::max<int64_t>(rows, 1)) * 16));
@@ -807,10 +877,19 @@ int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* 
     DeviceScope ds(P->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     B->launches = 0;
+    if (B->plan_H != n_heads) {
+        rc = build_attention_plan(B, n_heads, st);
+        if (rc != PK_OK) return rc;
+    }
+    if (B->use_tc && B->ngeneric == 0 && B->fuse_append_ok)
+        return attend_impl(B, layer, n_heads, q_dev, out_dev, st, k_dev, v_dev);
     if (B->nrows > 0) {
+        const bool listed = !B->app_rows.empty();
         PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_dev, v_dev,
-                                  B->slots(), B->nrows, P->kvh * P->d, st));
+                                  B->slots(), listed ? B->meta.at<int32_t>(5) : nullptr,
+                                  listed ? static_cast<int64_t>(B->app_rows.size()) : B->nrows,
+                                  P->kvh * P->d, st));
         PK_CUDA(prof_end(B, kProfAppend, st));
         B->launches++;
     }
@@ -858,6 +937,7 @@ int pk_batch_check(pk_batch* B, void* stream) {
     PK_CUDA(cudaMemcpy(&word, B->err.ptr, sizeof(int), cudaMemcpyDeviceToHost));
     if (word != 0) {
         PK_CUDA(cudaMemset(B->err.ptr, 0, sizeof(int)));
+        if (B->counters.ptr) PK_CUDA(cudaMemset(B->counters.ptr, 0, B->counters.cap));
         return fail(PK_ERR_TIMEOUT, "a bounded device wait timed out (error word %d)", word);
     }
     return PK_OK;

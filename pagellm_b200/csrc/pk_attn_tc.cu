@@ -12,7 +12,12 @@
 // blocks are laid end to end and the total is cut into `ncta` equal ranges: CTA c owns
 // blocks [c*T/ncta, (c+1)*T/ncta). A unit that falls inside one CTA is finished there;
 // a unit cut by CTA boundaries leaves one partial (max, sum, un-normalised output) per
-// CTA, merged by merge_kernel.
+// CTA; the last CTA to finish a (unit, KV head) merges them in place (per-unit counters),
+// or, without counters, merge_kernel does it in a second launch.
+//
+// Fused append: with k_new / v_new set, rows written in this step are taken from the fp32
+// inputs (rounded to bf16) when their block is consumed, and stored to the pool by the unit
+// that owns them, so no separate append launch is needed.
 //
 // CTA = 1 producer warp + one consumer warp per KV head. The producer streams each K/V
 // block of the layer into a ring of shared-memory stages with TMA bulk tensor loads (no
@@ -40,6 +45,67 @@ __device__ __forceinline__ int upper_bound_i32(const int32_t* a, int n, int x) {
         if (a[mid] <= x) lo = mid + 1; else hi = mid;
     }
     return lo;
+}
+
+// CTA whose block range [c*T/n, (c+1)*T/n) holds block j.
+__device__ __forceinline__ int cta_of_block(int j, int T, int n) {
+    int c = static_cast<int>(static_cast<int64_t>(j) * n / T);
+    while (c + 1 < n && static_cast<int64_t>(c + 1) * T / n <= j) ++c;
+    while (c > 0 && static_cast<int64_t>(c) * T / n > j) --c;
+    return c;
+}
+
+// One warp combines the partials of (unit u, KV head h) written by CTAs cf..cl:
+// out = sum_c 2^(m_c - M) o_c / sum_c 2^(m_c - M) l_c, M = max_c m_c (single pass with a
+// running max). Each lane owns up to four (column, 4-dim chunk) items so that the loads of
+// one segment are all in flight together.
+__device__ __forceinline__ void merge_head(const float* part_o, const float* part_ml, float* out,
+                                           int u, int h, int cf, int cl, int ncols, int kvh, int g,
+                                           int H, int D, int row0, int lane) {
+    const int chunks = D / 4;
+    const int items = ncols * chunks;
+    for (int base = 0; base < items; base += 128) {
+        float M[4], L[4];
+        float4 O[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            M[k] = -INFINITY;
+            L[k] = 0.f;
+            O[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        for (int c = cf; c <= cl; ++c) {
+            const size_t seg = (static_cast<size_t>(u) + c) * kvh + h;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int it = base + lane + 32 * k;
+                if (it >= items) continue;
+                const int col = it / chunks;
+                const size_t idx = seg * kMaxCols + col;
+                const float ms = __ldcg(part_ml + idx * 2);
+                const float ls = __ldcg(part_ml + idx * 2 + 1);
+                const float4 os = __ldcg(reinterpret_cast<const float4*>(part_o + idx * D) + (it % chunks));
+                const float mn = fmaxf(M[k], ms);
+                const float a = M[k] == -INFINITY ? 0.f : exp2f(M[k] - mn);
+                const float b = ms == -INFINITY ? 0.f : exp2f(ms - mn);
+                L[k] = L[k] * a + ls * b;
+                O[k].x = O[k].x * a + os.x * b;
+                O[k].y = O[k].y * a + os.y * b;
+                O[k].z = O[k].z * a + os.z * b;
+                O[k].w = O[k].w * a + os.w * b;
+                M[k] = mn;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int it = base + lane + 32 * k;
+            if (it >= items) continue;
+            const int col = it / chunks;
+            const float inv = 1.f / L[k];
+            float* op = out + (static_cast<size_t>(row0 + col / g) * H + h * g + col % g) * D;
+            reinterpret_cast<float4*>(op)[it % chunks] =
+                make_float4(O[k].x * inv, O[k].y * inv, O[k].z * inv, O[k].w * inv);
+        }
+    }
 }
 
 template <int D>
@@ -136,7 +202,8 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
     const int quad = lane & 3;   // column pair within an n8 tile
     const int grp = lane >> 2;   // row within an 8-row group
     int it = 0;
-    for (int j = lo, u = u_first; j < hi; ++u) {
+    bool alive = true;
+    for (int j = lo, u = u_first; j < hi && alive; ++u) {
         const int uend = min(hi, p.u_blk[u + 1]);
         const int ublk0 = p.u_blk[u];
         const int seq = p.u_seq[u];
@@ -191,7 +258,6 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.f;
         }
 
-        bool alive = true;
         for (; j < uend; ++j, ++it) {
             const int s = it % p.stages;
             // Every lane waits; the verdict is made warp-uniform (and the warp reconverged)
@@ -220,6 +286,42 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                         make_uint4(0, 0, 0, 0);
                 }
                 __syncwarp();
+            }
+            // Rows appended in this step (positions >= the sequence's start) come from the
+            // fp32 inputs, rounded to bf16, instead of from the pool; the unit whose own
+            // query rows they are also stores them to the pool (the fused append).
+            bool patched = false;
+            if (p.k_new != nullptr) {
+                const int s_start = p.starts[seq];
+                const int lo_pos = max(kpos0, s_start);
+                const int hi_pos = min(kpos0 + p.bs, uctx);
+                if (lo_pos < hi_pos) {
+                    patched = true;
+                    uint8_t* kgen = smem + s * 2 * tile_bytes;
+                    uint8_t* vgen = kgen + tile_bytes;
+                    const int phys = p.ids[p.indptr[seq] + (j - ublk0)];
+                    const int row_base = p.offsets[seq] - s_start;
+                    for (int pos = lo_pos; pos < hi_pos; ++pos) {
+                        const int t = pos - kpos0;
+                        const size_t src = (static_cast<size_t>(row_base + pos) * p.kvh + h) * D;
+                        const size_t dst = (static_cast<size_t>(phys) * p.bs + t) * p.kvh * D + h * D;
+                        for (int d0 = lane * 4; d0 < D; d0 += 128) {
+                            const float4 kx = *reinterpret_cast<const float4*>(p.k_new + src + d0);
+                            const float4 vx = *reinterpret_cast<const float4*>(p.v_new + src + d0);
+                            const uint2 kb = make_uint2(pack_bf16(kx.x, kx.y), pack_bf16(kx.z, kx.w));
+                            const uint2 vb = make_uint2(pack_bf16(vx.x, vx.y), pack_bf16(vx.z, vx.w));
+                            const uint32_t off = tile_off(d0 >> 6, h, t, (d0 & 63) >> 3, p.kvh, p.bs, CH,
+                                                          p.per_head_layout) + ((d0 & 7) ? 8u : 0u);
+                            *reinterpret_cast<uint2*>(kgen + off) = kb;
+                            *reinterpret_cast<uint2*>(vgen + off) = vb;
+                            if (pos >= qpos0) {
+                                *reinterpret_cast<uint2*>(p.pool_k + dst + d0) = kb;
+                                *reinterpret_cast<uint2*>(p.pool_v + dst + d0) = vb;
+                            }
+                        }
+                    }
+                    __syncwarp();
+                }
             }
             for (int mtile = 0; mtile < p.bs / 16; ++mtile) {
                 // ---- S^T = K . Q^T
@@ -291,7 +393,8 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                     }
                 }
             }
-            if (nvalid < p.bs) fence_proxy_async_smem();
+            // Generic-proxy writes into the stage must be ordered before the next TMA fill.
+            if (nvalid < p.bs || patched) fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
@@ -345,6 +448,24 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                         p.part_ml[(base + col) * 2 + 1] = l[nt][e];
                     }
                 }
+            if (p.counters != nullptr) {
+                // The last of the unit's CTAs to finish head h merges every partial of
+                // (unit, head h); the counter is left at zero for the next launch.
+                const int cf = cta_of_block(ublk0, p.total_blocks, p.ncta);
+                const int cl = cta_of_block(p.u_blk[u + 1] - 1, p.total_blocks, p.ncta);
+                __threadfence();
+                int last = 0;
+                if (lane == 0) {
+                    int* ctr = p.counters + static_cast<size_t>(u) * p.kvh + h;
+                    last = atomicAdd(ctr, 1) == cl - cf;
+                    if (last) *ctr = 0;
+                }
+                if (__shfl_sync(0xffffffffu, last, 0)) {
+                    __threadfence();
+                    merge_head(p.part_o, p.part_ml, p.out, u, h, cf, cl, nq * g, p.kvh, g, p.H, D,
+                               row0, lane);
+                }
+            }
         }
     }
 }

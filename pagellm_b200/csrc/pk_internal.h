@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -41,6 +42,15 @@ struct TcParams {
     int per_head_layout;   // 0: one TMA box per K/V block, 1: one box per (block, head)
     int64_t layer_slot0;   // first slot of the layer in the flat [layers*num_blocks*bs] axis
     float qscale;          // log2(e) / sqrt(D)
+    // In-kernel merge: one zero-initialised counter per (unit, KV head); NULL = leave the
+    // partials to merge_kernel.
+    int* counters;
+    // Fused append: fp32 rows [rows][kvh][D] of this step and the layer's bf16 pool bases;
+    // NULL k_new = attention only.
+    const float* k_new;
+    const float* v_new;
+    __nv_bfloat16* pool_k;
+    __nv_bfloat16* pool_v;
 };
 
 struct MergeParams {
@@ -107,8 +117,8 @@ cudaError_t launch_plan_rows(const int32_t* row_seq, const int32_t* offsets, con
                              const int32_t* indptr, const int32_t* ids, int bs, int64_t nrows,
                              int64_t* positions, int64_t* slots, cudaStream_t st);
 cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k,
-                          const float* v, const int64_t* slots, int64_t n, int rowlen,
-                          cudaStream_t st);
+                          const float* v, const int64_t* slots, const int32_t* rows, int64_t n,
+                          int rowlen, cudaStream_t st);
 cudaError_t launch_copy_blocks(void* k, void* v, const int64_t* pairs, int64_t npairs, int layers,
                                int64_t layer_bytes, int64_t block_bytes, cudaStream_t st);
 cudaError_t launch_slot_mapping(const int32_t* table, int64_t table_len, const int64_t* positions,

@@ -59,16 +59,20 @@ __device__ __forceinline__ void store4(__nv_bfloat16* dst, float4 x) {
 __device__ __forceinline__ void store1(float* dst, float x) { *dst = x; }
 __device__ __forceinline__ void store1(__nv_bfloat16* dst, float x) { *dst = __float2bfloat16_rn(x); }
 
+// rows == NULL: rows 0..n-1; otherwise only the listed rows (used when several rows of a
+// step share a slot: the list then holds the last writer of each slot).
 template <typename T>
 __global__ void append_vec4_kernel(T* __restrict__ pk_, T* __restrict__ pv_,
                                    const float* __restrict__ k, const float* __restrict__ v,
-                                   const int64_t* __restrict__ slots, int64_t n, int rowlen) {
+                                   const int64_t* __restrict__ slots, const int32_t* __restrict__ rows,
+                                   int64_t n, int rowlen) {
     const int per_row = rowlen / 4;
     const int64_t total = n * per_row;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t r = i / per_row;
-        const int c = static_cast<int>(i - r * per_row) * 4;
+        const int64_t ri = i / per_row;
+        const int c = static_cast<int>(i - ri * per_row) * 4;
+        const int64_t r = rows ? rows[ri] : ri;
         const int64_t dst = slots[r] * rowlen + c;
         store4(pk_ + dst, *reinterpret_cast<const float4*>(k + r * rowlen + c));
         store4(pv_ + dst, *reinterpret_cast<const float4*>(v + r * rowlen + c));
@@ -78,14 +82,16 @@ __global__ void append_vec4_kernel(T* __restrict__ pk_, T* __restrict__ pv_,
 template <typename T>
 __global__ void append_scalar_kernel(T* __restrict__ pk_, T* __restrict__ pv_,
                                      const float* __restrict__ k, const float* __restrict__ v,
-                                     const int64_t* __restrict__ slots, int64_t n, int rowlen) {
+                                     const int64_t* __restrict__ slots, const int32_t* __restrict__ rows,
+                                     int64_t n, int rowlen) {
     const int64_t total = n * rowlen;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t r = i / rowlen;
-        const int c = static_cast<int>(i - r * rowlen);
-        store1(pk_ + slots[r] * rowlen + c, k[i]);
-        store1(pv_ + slots[r] * rowlen + c, v[i]);
+        const int64_t ri = i / rowlen;
+        const int c = static_cast<int>(i - ri * rowlen);
+        const int64_t r = rows ? rows[ri] : ri;
+        store1(pk_ + slots[r] * rowlen + c, k[r * rowlen + c]);
+        store1(pv_ + slots[r] * rowlen + c, v[r * rowlen + c]);
     }
 }
 
@@ -228,8 +234,8 @@ cudaError_t launch_slot_mapping(const int32_t* table, int64_t table_len, const i
 }
 
 cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k,
-                          const float* v, const int64_t* slots, int64_t n, int rowlen,
-                          cudaStream_t st) {
+                          const float* v, const int64_t* slots, const int32_t* rows, int64_t n,
+                          int rowlen, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
     // 4-wide path only when every row start is 16-byte aligned on both sides.
     const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
@@ -239,13 +245,13 @@ cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, con
     if (dtype == 0) {
         float* pk_ = static_cast<float*>(pool_k_layer);
         float* pv_ = static_cast<float*>(pool_v_layer);
-        if (vec) append_vec4_kernel<float><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, n, rowlen);
-        else append_scalar_kernel<float><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, n, rowlen);
+        if (vec) append_vec4_kernel<float><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, rows, n, rowlen);
+        else append_scalar_kernel<float><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, rows, n, rowlen);
     } else {
         auto* pk_ = static_cast<__nv_bfloat16*>(pool_k_layer);
         auto* pv_ = static_cast<__nv_bfloat16*>(pool_v_layer);
-        if (vec) append_vec4_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, n, rowlen);
-        else append_scalar_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, n, rowlen);
+        if (vec) append_vec4_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, rows, n, rowlen);
+        else append_scalar_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, rows, n, rowlen);
     }
     return cudaGetLastError();
 }

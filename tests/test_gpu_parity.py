@@ -333,3 +333,49 @@ def test_decode_loop_reuses_batch_handles():
                 _close(out[i:i + 1], po.attention_dense(q.cpu().numpy()[i:i + 1], kc, vc, int(starts[i])), True)
         starts = starts + 1
     assert len(pool._idle_batches) <= 2
+
+
+def test_shared_and_repeated_written_blocks_follow_pagellm():
+    """Outside what BlockManager produces: two sequences write the same slot of a shared
+    block, a sequence reads that shared block, and a table repeats a block id. pagellm's
+    numpy semantics - all rows appended first, last writer of a slot wins, then attention
+    reads the pool - hold exactly (the step falls back to the separate append kernel)."""
+    torch = torch_cuda()
+    from pagellm_b200.cache import PagedBatch, PagedKVPool
+
+    pool = PagedKVPool(Shape(1, 8, 128), 16, 16, "bfloat16")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    pool.k.copy_(torch.randn(pool.k.shape, generator=g, device="cuda").to(pool.k.dtype))
+    pool.v.copy_(torch.randn(pool.v.shape, generator=g, device="cuda").to(pool.v.dtype))
+    tables = [[0, 1], [2, 1], [3, 4], [5, 5]]
+    starts = [19, 19, 31, 29]
+    n_new = [1, 1, 1, 1]
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((4, 32, 128), dtype=np.float32)
+    k = po.bf16_round(rng.standard_normal((4, 8, 128), dtype=np.float32))
+    v = po.bf16_round(rng.standard_normal((4, 8, 128), dtype=np.float32))
+    kf = pool.k_flat[0].float().cpu().numpy()
+    vf = pool.v_flat[0].float().cpu().numpy()
+    meta = po.StepMeta(tables, starts, n_new, 16)
+    ref = po.write_and_attend(kf, vf, meta, q, k, v)
+    b = PagedBatch(pool, tables, starts, n_new)
+    out = b.write_and_attend(0, q, k, v)
+    assert b.stats()["launches"] >= 2  # append kernel ran on its own
+    np.testing.assert_array_equal(pool.k_flat[0].float().cpu().numpy(), kf)
+    np.testing.assert_array_equal(pool.v_flat[0].float().cpu().numpy(), vf)
+    _close(out, ref, True)
+
+
+def test_fused_append_single_launch_c2():
+    """The common case: private written blocks -> one kernel launch per layer (append
+    and partial merge folded into the attention kernel)."""
+    from pagellm_b200 import workloads
+    from pagellm_b200.cache import PagedBatch
+
+    w = workloads.c2(5, batch=16)
+    pool = make_pool(w, 0)
+    q, k, v = dev_inputs(w, 2)
+    b = PagedBatch(pool, w.tables, w.starts, w.n_new)
+    b.write_and_attend(0, q, k, v)
+    st = b.stats()
+    assert st["launches"] == 1 and st["split_units"] > 0
