@@ -217,7 +217,7 @@ class _PinnedResults:
 
     def get(self, shape) -> np.ndarray:
         shape = tuple(int(x) for x in shape)
-        for i, b in enumerate(self.bufs):
+        for b in self.bufs:
             # references: the list slot, the loop variable, getrefcount's argument
             if b.shape == shape and sys.getrefcount(b) <= 3:
                 return b

@@ -55,57 +55,27 @@ __device__ __forceinline__ int cta_of_block(int j, int T, int n) {
     return c;
 }
 
-// One warp combines the partials of (unit u, KV head h) written by CTAs cf..cl:
-// out = sum_c 2^(m_c - M) o_c / sum_c 2^(m_c - M) l_c, M = max_c m_c (single pass with a
-// running max). Each lane owns up to four (column, 4-dim chunk) items so that the loads of
-// one segment are all in flight together.
-__device__ __forceinline__ void merge_head(const float* part_o, const float* part_ml, float* out,
-                                           int u, int h, int cf, int cl, int ncols, int kvh, int g,
-                                           int H, int D, int row0, int lane) {
-    const int chunks = D / 4;
-    const int items = ncols * chunks;
-    for (int base = 0; base < items; base += 128) {
-        float M[4], L[4];
-        float4 O[4];
+// Normalised output of the columns a lane holds (C-fragment layout of O^T: dims
+// mt*16 + grp (+8), columns nt*8 + 2*quad + e) for the live query tokens of a unit.
+template <int D, int NT>
+__device__ __forceinline__ void store_rows(float* out, const float (&acc)[D / 16][NT][4],
+                                           const float (&l)[NT][2], int nq, int g, int H,
+                                           int row0, int h, int quad, int grp) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            M[k] = -INFINITY;
-            L[k] = 0.f;
-            O[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        for (int c = cf; c <= cl; ++c) {
-            const size_t seg = (static_cast<size_t>(u) + c) * kvh + h;
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int it = base + lane + 32 * k;
-                if (it >= items) continue;
-                const int col = it / chunks;
-                const size_t idx = seg * kMaxCols + col;
-                const float ms = __ldcg(part_ml + idx * 2);
-                const float ls = __ldcg(part_ml + idx * 2 + 1);
-                const float4 os = __ldcg(reinterpret_cast<const float4*>(part_o + idx * D) + (it % chunks));
-                const float mn = fmaxf(M[k], ms);
-                const float a = M[k] == -INFINITY ? 0.f : exp2f(M[k] - mn);
-                const float b = ms == -INFINITY ? 0.f : exp2f(ms - mn);
-                L[k] = L[k] * a + ls * b;
-                O[k].x = O[k].x * a + os.x * b;
-                O[k].y = O[k].y * a + os.y * b;
-                O[k].z = O[k].z * a + os.z * b;
-                O[k].w = O[k].w * a + os.w * b;
-                M[k] = mn;
+        for (int e = 0; e < 2; ++e) {
+            const int col = nt * 8 + 2 * quad + e;
+            const int tq = col / g;
+            if (tq >= nq) continue;
+            const float inv = 1.f / l[nt][e];
+            float* op = out + (static_cast<size_t>(row0 + tq) * H + h * g + col % g) * D;
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
+                op[mt * 16 + grp] = acc[mt][nt][e] * inv;
+                op[mt * 16 + grp + 8] = acc[mt][nt][2 + e] * inv;
             }
         }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int it = base + lane + 32 * k;
-            if (it >= items) continue;
-            const int col = it / chunks;
-            const float inv = 1.f / L[k];
-            float* op = out + (static_cast<size_t>(row0 + col / g) * H + h * g + col % g) * D;
-            reinterpret_cast<float4*>(op)[it % chunks] =
-                make_float4(O[k].x * inv, O[k].y * inv, O[k].z * inv, O[k].w * inv);
-        }
-    }
 }
 
 template <int D>
@@ -146,6 +116,9 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
         fence_mbar_init();
     }
     __syncthreads();
+    // Let a programmatically dependent launch (the partial merge) be scheduled now: its CTAs
+    // fit beside this one on each SM and can load their metadata while this grid runs.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     const int c = blockIdx.x;
     const int lo = static_cast<int>(static_cast<int64_t>(c) * p.total_blocks / p.ncta);
@@ -413,21 +386,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             }
         const bool whole = ublk0 >= lo && p.u_blk[u + 1] <= hi;
         if (whole) {
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int col = nt * 8 + 2 * quad + e;
-                    const int tq = col / g;
-                    if (tq >= nq) continue;
-                    const float inv = 1.f / l[nt][e];
-                    float* op = p.out + (static_cast<size_t>(row0 + tq) * p.H + h * g + col % g) * D;
-#pragma unroll
-                    for (int mt = 0; mt < KS; ++mt) {
-                        op[mt * 16 + grp] = acc[mt][nt][e] * inv;
-                        op[mt * 16 + grp + 8] = acc[mt][nt][2 + e] * inv;
-                    }
-                }
+            store_rows<D, NT>(p.out, acc, l, nq, g, p.H, row0, h, quad, grp);
         } else {
             const size_t seg = static_cast<size_t>(u) + c;
             const size_t base = (seg * p.kvh + h) * kMaxCols;
@@ -449,21 +408,74 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                     }
                 }
             if (p.counters != nullptr) {
-                // The last of the unit's CTAs to finish head h merges every partial of
-                // (unit, head h); the counter is left at zero for the next launch.
+                // The last of the unit's CTAs to finish head h merges: its own partial is
+                // still in registers, every other CTA's partial is fetched with one batch of
+                // independent loads per CTA. The counter is left at zero for the next launch.
                 const int cf = cta_of_block(ublk0, p.total_blocks, p.ncta);
                 const int cl = cta_of_block(p.u_blk[u + 1] - 1, p.total_blocks, p.ncta);
-                __threadfence();
+                __syncwarp();
                 int last = 0;
                 if (lane == 0) {
+                    __threadfence();  // release the warp's partial (ordered by __syncwarp)
                     int* ctr = p.counters + static_cast<size_t>(u) * p.kvh + h;
                     last = atomicAdd(ctr, 1) == cl - cf;
                     if (last) *ctr = 0;
                 }
                 if (__shfl_sync(0xffffffffu, last, 0)) {
                     __threadfence();
-                    merge_head(p.part_o, p.part_ml, p.out, u, h, cf, cl, nq * g, p.kvh, g, p.H, D,
-                               row0, lane);
+                    // Two passes in CTA order cf..cl, so the result does not depend on which
+                    // CTA merges: the global max, then the weighted sums in that order, with
+                    // this CTA's own partial (bit-identical to what it stored) taken from
+                    // registers at its place in the order.
+                    float mx[NT][2], den[NT][2];
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            mx[nt][e] = -INFINITY;
+                            den[nt][e] = 0.f;
+                        }
+                    for (int cc = cf; cc <= cl; ++cc) {
+                        const size_t ob = ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols;
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const int col = nt * 8 + 2 * quad + e;
+                                const float mc = cc == c ? m[nt][e] : __ldcg(p.part_ml + (ob + col) * 2);
+                                mx[nt][e] = fmaxf(mx[nt][e], mc);
+                            }
+                    }
+                    float num[KS][NT][4];
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) num[mt][nt][i] = 0.f;
+                    for (int cc = cf; cc <= cl; ++cc) {
+                        const size_t ob = ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols;
+                        const bool own = cc == c;
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const int col = nt * 8 + 2 * quad + e;
+                                const float mc = own ? m[nt][e] : __ldcg(p.part_ml + (ob + col) * 2);
+                                const float lc = own ? l[nt][e] : __ldcg(p.part_ml + (ob + col) * 2 + 1);
+                                const float w = mc == -INFINITY ? 0.f : exp2f(mc - mx[nt][e]);
+                                den[nt][e] += lc * w;
+                                const float* po = p.part_o + (ob + col) * D;
+#pragma unroll
+                                for (int mt = 0; mt < KS; ++mt) {
+                                    const float o0 = own ? acc[mt][nt][e] : __ldcg(po + mt * 16 + grp);
+                                    const float o1 = own ? acc[mt][nt][2 + e] : __ldcg(po + mt * 16 + grp + 8);
+                                    num[mt][nt][e] += o0 * w;
+                                    num[mt][nt][2 + e] += o1 * w;
+                                }
+                            }
+                    }
+                    store_rows<D, NT>(p.out, num, den, nq, g, p.H, row0, h, quad, grp);
                 }
             }
         }
@@ -504,6 +516,66 @@ __global__ void merge_kernel(const MergeParams p) {
     }
 }
 
+// Merge of split units launched as a programmatic dependent of the attention kernel: one
+// CTA per split unit, one warp per KV head. Metadata is read before griddepcontrol.wait
+// (it does not come from the attention kernel); the partials after it, when the attention
+// grid has completed and its writes are visible. Each lane owns up to four
+// (column, 4-dim chunk) items so one segment's loads are in flight together.
+__global__ void __launch_bounds__(kTcMaxKvHeads * 32) merge_pdl_kernel(const MergeParams p) {
+    const int e = blockIdx.x;
+    const int h = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int u = p.split_u[e];
+    const int c0 = p.split_c0[e];
+    const int c1 = p.split_c1[e];
+    const int row0 = p.offsets[p.u_seq[u]] + p.u_t0[u];
+    const int ncols = p.u_n[u] * p.g;
+    const int chunks = p.D / 4;
+    const int items = ncols * chunks;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int base = 0; base < items; base += 128) {
+        float M[4], L[4];
+        float4 O[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            M[k] = -INFINITY;
+            L[k] = 0.f;
+            O[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        for (int c = c0; c <= c1; ++c) {
+            const size_t seg = (static_cast<size_t>(u) + c) * p.kvh + h;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int it = base + lane + 32 * k;
+                if (it >= items) continue;
+                const size_t idx = seg * kMaxCols + it / chunks;
+                const float ms = p.part_ml[idx * 2];
+                const float ls = p.part_ml[idx * 2 + 1];
+                const float4 os = reinterpret_cast<const float4*>(p.part_o + idx * p.D)[it % chunks];
+                const float mn = fmaxf(M[k], ms);
+                const float a = M[k] == -INFINITY ? 0.f : exp2f(M[k] - mn);
+                const float b = ms == -INFINITY ? 0.f : exp2f(ms - mn);
+                L[k] = L[k] * a + ls * b;
+                O[k].x = O[k].x * a + os.x * b;
+                O[k].y = O[k].y * a + os.y * b;
+                O[k].z = O[k].z * a + os.z * b;
+                O[k].w = O[k].w * a + os.w * b;
+                M[k] = mn;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int it = base + lane + 32 * k;
+            if (it >= items) continue;
+            const int col = it / chunks;
+            const float inv = 1.f / L[k];
+            float* op = p.out + (static_cast<size_t>(row0 + col / p.g) * p.H + h * p.g + col % p.g) * p.D;
+            reinterpret_cast<float4*>(op)[it % chunks] =
+                make_float4(O[k].x * inv, O[k].y * inv, O[k].z * inv, O[k].w * inv);
+        }
+    }
+}
+
 template <int D, int NT>
 cudaError_t launch_tc_t(const CUtensorMap* tmk, const CUtensorMap* tmv, const TcParams& p,
                         size_t smem, cudaStream_t st) {
@@ -529,6 +601,21 @@ cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUt
     if (D == 128 && NT == 2) return launch_tc_t<128, 2>(tmk, tmv, p, smem, st);
     if (D == 256 && NT == 1) return launch_tc_t<256, 1>(tmk, tmv, p, smem, st);
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_merge_dependent(const MergeParams& p, int nsplit, cudaStream_t st) {
+    if (nsplit <= 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nsplit);
+    cfg.blockDim = dim3(p.kvh * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, merge_pdl_kernel, p);
 }
 
 cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st) {

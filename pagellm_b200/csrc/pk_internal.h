@@ -112,6 +112,8 @@ cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUt
                                 const TcParams& p, size_t smem, cudaStream_t st);
 size_t tc_smem_bytes(int D, int bs, int kvh, int stages);
 cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st);
+// Same merge as a programmatic dependent launch of the preceding attention kernel.
+cudaError_t launch_merge_dependent(const MergeParams& p, int nsplit, cudaStream_t st);
 cudaError_t launch_generic_attention(int dtype, const GenericParams& p, cudaStream_t st);
 cudaError_t launch_plan_rows(const int32_t* row_seq, const int32_t* offsets, const int32_t* starts,
                              const int32_t* indptr, const int32_t* ids, int bs, int64_t nrows,
