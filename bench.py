@@ -38,6 +38,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode-attn tokens/s & achieved HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
+RESULT_OUT = sys.stdout
 
 
 def peaks():
@@ -173,7 +174,20 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    w = workloads.make(args.config, seed=rank)
+    from pagellm_b200.sharding import gather_heads, shard_sequences
+
+    head_mode = args.config == "c5" and args.shard == "head"
+    if args.config == "c5":
+        # one fixed batch of 128 sequences split over the ranks: strong scaling
+        L = workloads.c5_lengths(0)
+        if head_mode:
+            w = workloads.c5(0, lengths=L, kv_heads=8 // world)
+        else:
+            w = workloads.c5(0, lengths=L[shard_sequences(L, world)[rank]])
+        scaling, total_rows = "strong", len(L)
+    else:
+        w = workloads.make(args.config, seed=rank)
+        scaling, total_rows = "weak", None
 
     class Shape:
         n_layers, n_kv_heads, head_dim = 1, w.KVH, w.D
@@ -182,7 +196,9 @@ def run_ours(args):
     g = torch.Generator(device=dev).manual_seed(rank)
     for t in (pool.k, pool.v):
         t[0].copy_(torch.randn(t[0].shape, generator=g, device=dev).to(t.dtype))
+    pairs_dev = None
     if w.cow_pairs:
+        pairs_dev = torch.as_tensor(np.asarray(w.cow_pairs, dtype=np.int64).reshape(-1, 2), device=dev)
         pool.copy_blocks(w.cow_pairs)
     indptr, ids = w.csr()
     batch = PagedBatch(pool, (indptr, ids), w.starts, w.n_new)
@@ -195,6 +211,20 @@ def run_ours(args):
     st = stream.cuda_stream
 
     def step():
+        if head_mode:
+            attend_layer()
+            gather_heads(out)
+            return
+        if pairs_dev is not None:  # the step's copy-on-write copies (fork of the shared block)
+            rc = lib.pk_pool_copy_blocks_dev(pool.handle, pairs_dev.data_ptr(), len(pairs_dev), st)
+            if rc:
+                _lib.check(rc)
+        rc = lib.pk_batch_write_and_attend(batch._b, 0, w.H, q.data_ptr(), k.data_ptr(),
+                                           v.data_ptr(), out.data_ptr(), st)
+        if rc:
+            _lib.check(rc)
+
+    def attend_layer():
         rc = lib.pk_batch_write_and_attend(batch._b, 0, w.H, q.data_ptr(), k.data_ptr(),
                                            v.data_ptr(), out.data_ptr(), st)
         if rc:
@@ -224,12 +254,12 @@ def run_ours(args):
         barrier()
         ms = max_over_ranks(e0.elapsed_time(e1))
         batch.check()
-        launches_per_step = batch.stats()["launches"]
+        launches_per_step = batch.stats()["launches"] + (1 if pairs_dev is not None else 0)
 
         # kernel timing for the roofline (events on the launching stream, same K steps)
         lib.pk_batch_profile(batch._b, 1)
         for _ in range(args.steps):
-            step()
+            (attend_layer if head_mode else step)()
         prof_ms = (C.c_double * 4)()
         prof_n = (C.c_int64 * 4)()
         _lib.check(lib.pk_batch_profile_read(batch._b, prof_ms, prof_n))
@@ -252,18 +282,22 @@ def run_ours(args):
         a0.record(stream)
         for _ in range(e_steps):
             res = PagedBatch(pool, (indptr, ids), w.starts, w.n_new).write_and_attend(0, qn, kn, vn)
+            if head_mode:  # slices back to the GPU, all-gather, full output to the host
+                res = gather_heads(torch.from_numpy(res).to(dev)).cpu().numpy()
         a1.record(stream)
         barrier()
         e2e_ms = max_over_ranks(a0.elapsed_time(a1))
         assert np.isfinite(res).all()
     clk = clocks.summary()
 
-    tokens_per_step = w.rows
-    value = world * tokens_per_step * args.steps / (ms / 1e3)
-    e2e_value = world * tokens_per_step * e_steps / (e2e_ms / 1e3)
+    job_rows = total_rows if total_rows is not None else world * w.rows
+    value = job_rows * args.steps / (ms / 1e3)
+    e2e_value = job_rows * e_steps / (e2e_ms / 1e3)
     hbm, hbm_src = peaks()
-    # dominant kernel: tensor-core split-KV attention (kind 1); algorithmic bytes per launch
-    alg_attn = (w.kv_read_bytes() + w.rows * w.H * w.D * 8
+    # dominant kernel: tensor-core split-KV attention (kind 1); algorithmic bytes per launch:
+    # the distinct K/V blocks it must read (shared blocks once), q in, out, tables, metadata
+    uniq = w.unique_kv_bytes()
+    alg_attn = (uniq + w.rows * w.H * w.D * 8
                 + int(sum(-(-int(L) // w.bs) for L in w.ctx_lens)) * 4 + w.nseq * 12)
     kind = 1 if prof_n[1] else 3
     avg_ms = prof_ms[kind] / max(1, prof_n[kind])
@@ -278,7 +312,7 @@ def run_ours(args):
         "warmup": max(args.warmup, 3),
         "ms_per_step": round(ms / args.steps, 5),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling,
         "vs_baseline": None,
         "dtype": "bf16" if w.dtype == "bf16" else "f32",
         "data": "synthetic (seeded N(0,1) K/V/q; scattered block tables)",
@@ -294,12 +328,22 @@ def run_ours(args):
             "rows_per_gpu": w.rows,
             "context_tokens_per_gpu": int(w.ctx_lens.sum()),
             "kv_bytes_per_step_per_gpu": w.kv_read_bytes(),
+            "kv_unique_bytes_per_step_per_gpu": uniq,
+            "attention_gflop_per_step_per_gpu": round(w.attention_flops() / 1e9, 3),
+            "attention_tflops_per_gpu": round(w.attention_flops() / (ms / args.steps / 1e3) / 1e12, 2),
+            "cow_pairs_per_step": len(w.cow_pairs),
+            "cow_bytes_per_step": w.cow_bytes(),
             "step_algorithmic_bytes_per_gpu": step_bytes,
             "step_gbs_per_gpu": round(step_bytes / (ms / args.steps / 1e3) / 1e9, 1),
-            "l2": "inputs larger than L2 (K/V read per step > 126 MB)" if w.kv_read_bytes() > 126e6
-                  else "K/V read per step fits in L2 (not flushed)",
-            "parallelism": f"sequence-sharded x{world} (own pool per GPU, no collective)",
-            "step": "append + split-KV attention (+ partial merge), one layer",
+            "l2": "inputs larger than L2 (distinct K/V per step > 126 MB)" if uniq > 126e6
+                  else "distinct K/V per step fits in L2 (126 MB): not flushed, achieved GB/s counts distinct bytes",
+            "parallelism": (f"head-sharded x{world}: {w.KVH} KV heads per GPU for all sequences, "
+                            "NCCL all-gather of the output slices inside the step") if head_mode else
+                           (f"sequence-sharded x{world} (own pool per GPU, no collective)"
+                            + (", 128-sequence batch split longest-first" if args.config == "c5" else "")),
+            "job_rows_per_step": job_rows,
+            "step": ("copy-on-write copies + " if w.cow_pairs else "")
+                    + "append + split-KV attention with in-kernel partial merge, one layer",
         },
         "roofline": {
             "bound": "hbm",
@@ -338,7 +382,7 @@ def run_ours(args):
                       f"{os.cpu_count()} logical CPUs)",
         }
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        print(json.dumps(result), file=RESULT_OUT, flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -375,16 +419,29 @@ def run_reference(args):
                          "sample": f"{min(args.cpu_seqs, w.nseq)} of {w.nseq} sequences per step, "
                                    f"{reps} steps ({cpu_model()}, {os.cpu_count()} logical CPUs)"},
         "e2e": {"value": round(tps, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    }), file=RESULT_OUT, flush=True)
+
+
+def _claim_stdout():
+    """Keep stdout for the one JSON line: libraries (NCCL prints a version banner) write
+    through file descriptor 1, which is pointed at stderr for the rest of the run."""
+    out = os.fdopen(os.dup(1), "w", buffering=1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
+    return out
 
 
 def main():
+    global RESULT_OUT
+    RESULT_OUT = _claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--shard", default="seq", choices=["seq", "head"],
+                    help="c5 multi-GPU layout: whole sequences per GPU, or KV heads per GPU + all-gather")
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)

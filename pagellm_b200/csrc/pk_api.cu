@@ -279,9 +279,11 @@ void setup_tc(pk_pool* P) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, P->device);
     const size_t stage = static_cast<size_t>(2) * P->block_size * P->kvh * P->d * 2;
-    int stages = 4;
-    while (stages >= 2 && pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages) > static_cast<size_t>(optin))
-        --stages;
+    // As many stages as fit in ~200 KB (at most 8): small tiles (few KV heads per GPU in the
+    // head-sharded layout) need more of them to keep enough bytes in flight per SM.
+    int stages = 8;
+    const size_t budget = std::min<size_t>(static_cast<size_t>(optin), size_t(200) << 10);
+    while (stages >= 2 && pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages) > budget) --stages;
     (void)stage;
     if (stages < 2) return no("K/V block too large for two shared-memory stages");
     std::string why;

@@ -73,6 +73,26 @@ class Workload:
         once per sequence (decode) - sum_i 2 * L_i * KVH * D * elem."""
         return int(2 * self.ctx_lens.sum() * self.KVH * self.D * self.elem_bytes)
 
+    def unique_kv_bytes(self) -> int:
+        """K+V bytes of the distinct blocks the step's attention touches (shared prefix
+        blocks once): what must come from HBM at least once."""
+        used = set()
+        for t, L in zip(self.tables, self.ctx_lens):
+            used.update(np.asarray(t[: -(-int(L) // self.bs)]).tolist())
+        return int(2 * len(used) * self.bs * self.KVH * self.D * self.elem_bytes)
+
+    def attention_flops(self) -> int:
+        """2 * (QK^T + PV) multiply-adds: 4 * visible keys * H * D per query row."""
+        keys = 0
+        for s, n in zip(self.starts, self.n_new):
+            s, n = int(s), int(n)
+            keys += n * s + n * (n + 1) // 2
+        return int(4 * keys * self.H * self.D)
+
+    def cow_bytes(self) -> int:
+        """Bytes a copy-on-write step moves: every pair reads and writes one K and one V block."""
+        return int(len(self.cow_pairs) * 2 * 2 * self.bs * self.KVH * self.D * self.elem_bytes)
+
     def algorithmic_bytes(self) -> int:
         """Bytes a perfect decode step moves: K/V context reads, q in + out (fp32), the
         block-table entries, the append (fp32 rows read, pool rows written) and slots."""
@@ -180,19 +200,6 @@ def c5(seed: int = 0, batch: int = 128, lengths: np.ndarray | None = None,
     return Workload("c5", 8 * kvh, kvh, 128, 16, "bf16", nb, tables, (L - 1).astype(np.int64),
                     np.ones(len(L), np.int64),
                     notes={"L": f"clip(lognormal(ln 8192, {C5_SIGMA}), 1024, 32768)"})
-
-
-def shard_longest_first(lengths, world: int) -> list[list[int]]:
-    """Sequence indices per rank: longest first, each to the rank with the least total
-    context so far (ties to the lowest rank)."""
-    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
-    load = [0] * world
-    parts: list[list[int]] = [[] for _ in range(world)]
-    for i in order:
-        r = min(range(world), key=lambda k: (load[k], k))
-        parts[r].append(i)
-        load[r] += int(lengths[i])
-    return [sorted(p) for p in parts]
 
 
 BUILDERS = {"c1": c1, "c2": c2, "c3": c3, "c4": c4, "c5": c5}
