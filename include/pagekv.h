@@ -124,17 +124,19 @@ PK_API int pk_batch_write_and_attend_host(pk_batch* batch, int layer, int n_head
 /* Reads (and clears) the device error word that bounded waits set on timeout.
  * Synchronises `stream`. Returns PK_ERR_TIMEOUT if any kernel of this batch gave up. */
 PK_API int pk_batch_check(pk_batch* batch, void* stream);
-/* Planning statistics of the last plan: [0] rows, [1] sequences on the tensor-core split-KV
- * kernel, [2] its CTAs, [3] its total K/V blocks, [4] split sequences needing the merge
- * kernel, [5] rows on the CUDA-core kernel, [6] kernels launched per write_and_attend. */
-PK_API int pk_batch_stats(const pk_batch* batch, int64_t* stats7);
+/* Planning statistics of the last plan: [0] rows, [1] units on the tensor-core split-KV
+ * kernel, [2] its CTAs, [3] its total K/V blocks, [4] units split across CTAs (merged),
+ * [5] rows on the CUDA-core kernel, [6] kernels launched by the last call, [7] wide-tile
+ * work items (128 query rows each) on the tcgen05 kernel. */
+PK_API int pk_batch_stats(const pk_batch* batch, int64_t* stats8);
 
 /* Per-kernel timing of this batch's own launches: with profiling on, CUDA events are
  * recorded on the launching stream around every kernel. pk_batch_profile_read synchronises
- * them and returns, per kind [0 append, 1 tensor-core attention, 2 partial merge,
- * 3 CUDA-core attention], the summed milliseconds and launch counts, then resets. */
+ * them and returns, per kind [0 append, 1 split-KV tensor-core attention, 2 partial merge,
+ * 3 CUDA-core attention, 4 wide-tile tcgen05 attention], the summed milliseconds and launch
+ * counts, then resets. */
 PK_API int pk_batch_profile(pk_batch* batch, int enable);
-PK_API int pk_batch_profile_read(pk_batch* batch, double* ms4, int64_t* count4);
+PK_API int pk_batch_profile_read(pk_batch* batch, double* ms5, int64_t* count5);
 /* Host-only dry run of the split-KV planner (no device needed): given per-unit block
  * counts, returns for each CTA its first block [ncta+1] (ncta = min(total, max_ctas)). */
 PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,

@@ -331,9 +331,10 @@ class PagedBatch:
         return torch.as_tensor(_CudaArray(sl.value, (n,), "<i8", self), device=self.pool.device)
 
     def stats(self) -> dict:
-        s = (C.c_int64 * 7)()
+        s = (C.c_int64 * 8)()
         _lib.check(self._lib.pk_batch_stats(self._b, s))
-        keys = ("rows", "tc_units", "tc_ctas", "tc_blocks", "split_units", "generic_rows", "launches")
+        keys = ("rows", "tc_units", "tc_ctas", "tc_blocks", "split_units", "generic_rows", "launches",
+                "wide_items")
         return dict(zip(keys, list(s)))
 
     # ------------------------------------------------------------------ per layer

@@ -176,6 +176,10 @@ struct pk_pool {
     std::string tc_why;
     CUtensorMap tmk{};
     CUtensorMap tmv{};
+    // wide-tile (tcgen05) kernel: one (block, head, 64-dim chunk) per TMA box
+    bool wide_ok = false;
+    CUtensorMap tmk1{};
+    CUtensorMap tmv1{};
     Uploader pairs_up;
 
     size_t layer_bytes() const { return static_cast<size_t>(layer_elems) * esize; }
@@ -205,7 +209,9 @@ struct pk_batch {
     int nu = 0, total_blocks = 0, ncta = 0, nt = 1, nsplit = 0;
     int ngeneric = 0;
     std::vector<int32_t> u_seq, u_t0, u_n, u_blk, sp_u, sp_c0, sp_c1, gen_rows;
-    Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows
+    int nwide = 0;                           // wide-tile work items
+    std::vector<int32_t> w_seq, w_t0, w_rows;  // items; rows they cover (appended separately)
+    Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows 8 w_seq 9 w_t0 10 w_rows
     DevBuf ws;
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
@@ -227,6 +233,31 @@ namespace {
 // pool as [chunk of 64 dims][kv head][slot][64 dims] so that one box = one whole K (or V)
 // block with each (head, chunk) slice's tokens on consecutive 128-byte rows; layout 1
 // is the natural order, one box per (block, head).
+// One (block, head, 64-dim chunk) per box over the layout-0 view: the wide kernel's tiles.
+bool encode_chunk_maps(pk_pool* P, std::string* why) {
+    auto enc = tensor_map_encoder();
+    if (!enc) {
+        *why = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    const cuuint64_t slots = static_cast<cuuint64_t>(P->n_layers) * P->num_blocks * P->block_size;
+    cuuint64_t dims[4] = {64, slots, static_cast<cuuint64_t>(P->kvh), static_cast<cuuint64_t>(P->d / 64)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(P->kvh) * P->d * 2, static_cast<cuuint64_t>(P->d) * 2, 128};
+    cuuint32_t box[4] = {64, static_cast<cuuint32_t>(P->block_size), 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    for (int t = 0; t < 2; ++t) {
+        CUresult r = enc(t == 0 ? &P->tmk1 : &P->tmv1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                         t == 0 ? P->k : P->v, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            *why = "cuTensorMapEncodeTiled(chunk box) failed";
+            return false;
+        }
+    }
+    return true;
+}
+
 bool encode_pool_maps(pk_pool* P, int layout, std::string* why) {
     auto enc = tensor_map_encoder();
     if (!enc) {
@@ -299,9 +330,17 @@ void setup_tc(pk_pool* P) {
     P->tc_smem = pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages);
     P->tc_ok = true;
     P->tc_why.clear();
+    // wide tiles: head_dim 128, 64-key tiles made of whole blocks, the layout-0 view
+    std::string why2;
+    P->wide_ok = P->d == 128 && 64 % P->block_size == 0 && P->tc_per_head == 0 &&
+                 static_cast<size_t>(optin) >= pk::wide_smem_bytes() && encode_chunk_maps(P, &why2);
 }
 
 int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+// Sequences with at least this many new query rows (tokens x heads per KV head) go to the
+// wide-tile tensor-core kernel; fewer rows stay on the split-KV kernel's units.
+constexpr int64_t kWideMinRows = 64;
 
 // CTA c of n owns blocks [c*T/n, (c+1)*T/n).
 inline int64_t cta_lo(int64_t c, int64_t T, int64_t n) { return c * T / n; }
@@ -327,10 +366,25 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         qmax = std::max(1, pk::kMaxCols / g);
         if (P->d == 256) qmax = g <= 8 ? std::max(1, 8 / g) : 0;  // one n8 tile only at D=256
     }
+    B->w_seq.clear();
+    B->w_t0.clear();
+    B->w_rows.clear();
+    B->nwide = 0;
+    const bool wide_ok = P->wide_ok && g <= 128 && 128 % g == 0;
     int64_t T = 0;
     for (int i = 0; i < B->nseq; ++i) {
         const int n = B->nnew[i];
         if (n <= 0) continue;
+        if (wide_ok && static_cast<int64_t>(n) * g >= kWideMinRows) {
+            // 128 query rows (128/g tokens) per work item, longest contexts first below
+            const int tpt = 128 / g;
+            for (int t0 = 0; t0 < n; t0 += tpt) {
+                B->w_seq.push_back(i);
+                B->w_t0.push_back(t0);
+            }
+            for (int r = 0; r < n; ++r) B->w_rows.push_back(B->offsets[i] + r);
+            continue;
+        }
         if (qmax == 0) {
             for (int r = 0; r < n; ++r) B->gen_rows.push_back(B->offsets[i] + r);
             continue;
@@ -347,6 +401,22 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         }
     }
     if (T >= (int64_t(1) << 31)) return fail(PK_ERR_UNSUPPORTED, "step reads 2^31 blocks or more");
+    // wide items with the most keys first, so the longest CTAs start in the first wave
+    {
+        std::vector<int> order(B->w_seq.size());
+        for (size_t x = 0; x < order.size(); ++x) order[x] = static_cast<int>(x);
+        std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+            return B->starts[B->w_seq[a]] + B->w_t0[a] > B->starts[B->w_seq[b]] + B->w_t0[b];
+        });
+        std::vector<int32_t> ws(order.size()), wt(order.size());
+        for (size_t x = 0; x < order.size(); ++x) {
+            ws[x] = B->w_seq[order[x]];
+            wt[x] = B->w_t0[order[x]];
+        }
+        B->w_seq.swap(ws);
+        B->w_t0.swap(wt);
+        B->nwide = static_cast<int>(B->w_seq.size());
+    }
     B->nu = static_cast<int>(B->u_seq.size());
     B->ngeneric = static_cast<int>(B->gen_rows.size());
     if (B->nu > 0) {
@@ -380,6 +450,9 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan.add(B->sp_c0.data(), B->sp_c0.size() * 4);
     B->plan.add(B->sp_c1.data(), B->sp_c1.size() * 4);
     B->plan.add(B->gen_rows.data(), B->gen_rows.size() * 4);
+    B->plan.add(B->w_seq.data(), B->w_seq.size() * 4);
+    B->plan.add(B->w_t0.data(), B->w_t0.size() * 4);
+    B->plan.add(B->w_rows.data(), B->w_rows.size() * 4);
     int rc = B->plan.commit(st);
     if (rc != PK_OK) return rc;
     B->plan_H = H;
@@ -387,7 +460,7 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
 }
 
 // Kinds reported by pk_batch_profile_read.
-enum ProfKind { kProfAppend = 0, kProfTc = 1, kProfMerge = 2, kProfGeneric = 3, kProfKinds = 4 };
+enum ProfKind { kProfAppend = 0, kProfTc = 1, kProfMerge = 2, kProfGeneric = 3, kProfWide = 4, kProfKinds = 5 };
 
 cudaError_t prof_mark(pk_batch* B, cudaStream_t st) {
     if (!B->profiling) return cudaSuccess;
@@ -487,6 +560,29 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
             PK_CUDA(prof_end(B, kProfMerge, st));
             B->launches++;
         }
+    }
+    if (B->nwide > 0) {
+        pk::WideParams w{};
+        w.q = q;
+        w.out = out;
+        w.err = static_cast<int*>(B->err.ptr);
+        w.indptr = B->meta.at<int32_t>(0);
+        w.ids = B->meta.at<int32_t>(1);
+        w.starts = B->meta.at<int32_t>(2);
+        w.offsets = B->meta.at<int32_t>(3);
+        w.w_seq = B->plan.at<int32_t>(8);
+        w.w_t0 = B->plan.at<int32_t>(9);
+        w.nitems = B->nwide;
+        w.H = H;
+        w.kvh = P->kvh;
+        w.g = g;
+        w.bs = P->block_size;
+        w.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
+        w.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
+        PK_CUDA(prof_begin(B, st));
+        PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, st));
+        PK_CUDA(prof_end(B, kProfWide, st));
+        B->launches++;
     }
     if (B->ngeneric > 0) {
         if (P->d > 512) return fail(PK_ERR_UNSUPPORTED, "head_dim %d > 512", P->d);
@@ -883,8 +979,19 @@ int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* 
         rc = build_attention_plan(B, n_heads, st);
         if (rc != PK_OK) return rc;
     }
-    if (B->use_tc && B->ngeneric == 0 && B->fuse_append_ok)
+    if (B->ngeneric == 0 && B->fuse_append_ok && (B->use_tc || B->nwide > 0)) {
+        // split-KV units append their own rows inside the attention kernel; rows of
+        // wide-tile sequences are appended first by the row-list append kernel
+        if (B->nwide > 0) {
+            PK_CUDA(prof_begin(B, st));
+            PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_dev, v_dev,
+                                      B->slots(), B->plan.at<int32_t>(10),
+                                      static_cast<int64_t>(B->w_rows.size()), P->kvh * P->d, st));
+            PK_CUDA(prof_end(B, kProfAppend, st));
+            B->launches++;
+        }
         return attend_impl(B, layer, n_heads, q_dev, out_dev, st, k_dev, v_dev);
+    }
     if (B->nrows > 0) {
         const bool listed = !B->app_rows.empty();
         PK_CUDA(prof_begin(B, st));
@@ -947,6 +1054,7 @@ int pk_batch_check(pk_batch* B, void* stream) {
 
 int pk_batch_stats(const pk_batch* B, int64_t* s) {
     if (!B || !s) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    s[7] = B->nwide;
     s[0] = B->nrows;
     s[1] = B->nu;
     s[2] = B->ncta;
@@ -965,7 +1073,9 @@ int pk_batch_profile(pk_batch* B, int enable) {
     return PK_OK;
 }
 
-int pk_batch_profile_read(pk_batch* B, double* ms4, int64_t* count4) {
+int pk_batch_profile_read(pk_batch* B, double* ms5, int64_t* count5) {
+    double* ms4 = ms5;
+    int64_t* count4 = count5;
     if (!B || !ms4 || !count4) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
     DeviceScope ds(B->pool->device);
     for (int k = 0; k < kProfKinds; ++k) {

@@ -1,0 +1,455 @@
+// Causal chunked-prefill / speculative-verify attention over the paged cache on the
+// 5th-generation tensor cores (tcgen05 + TMEM), bf16 pools, head_dim 128.
+//
+// Semantics: pagellm cache/paged.py:454-463 -> model/transformer.py:116-146: the query at
+// absolute position p sees keys 0..p of its sequence, keys read through the block table.
+//
+// One CTA per (work item = 128 query rows of one sequence, KV head h). Rows are
+// (token, head-in-group) pairs, row r = t*g + j, so a tile holds 128/g query tokens whose
+// g heads share every K/V tile. Keys stream in tiles of 64 (64/bs blocks).
+//
+// Warp roles (192 threads):
+//   warp 0  producer: one lane issues TMA loads (no multicast) of each block's K and V,
+//           one 64-dim chunk per copy, into a 3-stage ring; mbarrier completion.
+//   warp 1  TMEM owner (alloc/dealloc, 256 columns) and, on one lane, the MMA issuer:
+//           S_j = Q . K_j^T   (M=128, N=64,  K=128, bf16 -> fp32 TMEM, Q as bf16 hi + lo)
+//           O  += P_j . V_j   (M=128, N=128, K=64;  P from shared memory, V MN-major)
+//   warps 2-5 softmax warpgroup: thread = row. Loads S_j from TMEM, masks by absolute
+//           position, online max/sum in the exp2 domain, rescales O in TMEM when the max
+//           grows, writes P_j (bf16) to shared memory, and finally O / l to global.
+// S is double-buffered in TMEM (columns 0-63, 64-127), O lives in columns 128-255.
+// Every wait is bounded; on a timeout the CTA records the error, unwinds and frees TMEM.
+
+#include "pk_device.cuh"
+#include "pk_internal.h"
+
+namespace pk {
+
+namespace {
+
+constexpr int kWRows = 128;       // query rows per CTA (UMMA M)
+constexpr int kWKeys = 64;        // keys per tile (UMMA N of S, K of P.V)
+constexpr int kWD = 128;          // head dim
+constexpr int kWStages = 3;
+constexpr int kWThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+
+// shared memory carve-up (bytes from a 1024-aligned base)
+constexpr int kQBytes = kWRows * kWD * 2;            // 32 KB per Q half (hi, lo): [chunk][row][64]
+constexpr int kKVBytes = kWKeys * kWD * 2;           // 16 KB per K or V tile: [chunk][key][64]
+constexpr int kStageBytes = 2 * kKVBytes;
+constexpr int kPBytes = kWRows * kWKeys * 2;         // 16 KB: [row][64 keys]
+constexpr int kOffQhi = 0;
+constexpr int kOffQlo = kOffQhi + kQBytes;
+constexpr int kOffStage = kOffQlo + kQBytes;
+constexpr int kOffP = kOffStage + kWStages * kStageBytes;
+constexpr int kOffBar = kOffP + kPBytes;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;
+
+// ---------------------------------------------------------------- tcgen05 wrappers
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+        "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]),
+        "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]),
+        "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 format: version 1).
+// lbo / sbo in bytes (multiples of 16).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
+    d |= static_cast<uint64_t>(1) << 46;  // version
+    d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 x bf16 -> fp32, M = 128.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n, bool b_mn_major) {
+    return (1u << 4)                  // D format f32
+           | (1u << 7)                // A bf16
+           | (1u << 10)               // B bf16
+           | (0u << 15)               // A K-major
+           | ((b_mn_major ? 1u : 0u) << 16)
+           | (static_cast<uint32_t>(n >> 3) << 17)
+           | (static_cast<uint32_t>(kWRows >> 4) << 24);
+}
+
+constexpr uint32_t kIdescS = idesc_bf16(kWKeys, false);
+constexpr uint32_t kIdescO = idesc_bf16(kWD, true);
+
+// Offset of 16-byte unit u of row r in a [rows][128 B] tile with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t sw128(int r, int u) {
+    return static_cast<uint32_t>(r * 128 + ((u ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kWThreads, 1)
+    wide_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                     const WideParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* empty = full + kWStages;
+    uint64_t* sfull = empty + kWStages;  // [2]
+    uint64_t* sfree = sfull + 2;         // [2]
+    uint64_t* pfull = sfree + 2;
+    uint64_t* pvdone = pfull + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pvdone + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x;
+    const int h = blockIdx.y;
+    const int seq = p.w_seq[item];
+    const int t0 = p.w_t0[item];
+    const int g = p.g;
+    const int nseq_rows = p.offsets[seq + 1] - p.offsets[seq];
+    const int tok_per_tile = kWRows / g;
+    const int ntok = min(tok_per_tile, nseq_rows - t0);  // live query tokens in this tile
+    const int qpos0 = p.starts[seq] + t0;
+    const int kv_end = qpos0 + ntok;                       // keys 0..kv_end-1
+    const int ntiles = (kv_end + kWKeys - 1) / kWKeys;
+    const int nblk_ctx = (kv_end + p.bs - 1) / p.bs;
+    const int32_t* tbl = p.ids + p.indptr[seq];
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kWStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sfull[b], 1);
+            mbar_init(&sfree[b], 4);
+        }
+        mbar_init(pfull, 4);
+        mbar_init(pvdone, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+
+    // ---- Q tile -> shared memory (softmax warps): scale into the exp2 domain, bf16 hi + lo
+    if (warp >= 2) {
+        const int r = 32 * (warp & 3) + lane;
+        const int t = r / g, j = r % g;
+        const bool live = t < ntok;
+        const float* qp = p.q + (static_cast<size_t>(p.offsets[seq] + t0 + (live ? t : 0)) * p.H + h * g + j) * kWD;
+        for (int c = 0; c < 2; ++c)
+            for (int u = 0; u < 8; ++u) {
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+                if (live) {
+                    a = *reinterpret_cast<const float4*>(qp + c * 64 + u * 8);
+                    b = *reinterpret_cast<const float4*>(qp + c * 64 + u * 8 + 4);
+                }
+                const float x[8] = {a.x * p.qscale, a.y * p.qscale, a.z * p.qscale, a.w * p.qscale,
+                                    b.x * p.qscale, b.y * p.qscale, b.z * p.qscale, b.w * p.qscale};
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    hi[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
+                    lo[e] = pack_bf16(x[2 * e] - bf16_lo_f(hi[e]), x[2 * e + 1] - bf16_hi_f(hi[e]));
+                }
+                const uint32_t off = c * (kWRows * 128) + sw128(r, u);
+                *reinterpret_cast<uint4*>(smem + kOffQhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(smem + kOffQlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+        fence_proxy_async_smem();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t smem_base = smem_u32(smem);
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            prefetch_tensormap(&tmk);
+            prefetch_tensormap(&tmv);
+            const int per_tile = kWKeys / p.bs;
+            int issued = 0;
+            for (int jt = 0; jt < ntiles; ++jt) {
+                const int s = jt % kWStages;
+                if (!mbar_wait_bounded(&empty[s], ((jt / kWStages) & 1u) ^ 1u) || *abort_flag) {
+                    *abort_flag = 1;
+                    atomicExch(p.err, kErrTimeout);
+                    break;
+                }
+                uint8_t* kd = smem + kOffStage + s * kStageBytes;
+                uint8_t* vd = kd + kKVBytes;
+                mbar_arrive_expect_tx(&full[s], kStageBytes);
+                for (int b = 0; b < per_tile; ++b) {
+                    const int bi = min(jt * per_tile + b, nblk_ctx - 1);  // past the end: a valid block, masked
+                    const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(tbl[bi]) * p.bs);
+                    for (int c = 0; c < 2; ++c) {
+                        const int off = c * (kWKeys * 128) + b * p.bs * 128;
+                        tma_load_4d(kd + off, &tmk, 0, slot0, h, c, &full[s]);
+                        tma_load_4d(vd + off, &tmv, 0, slot0, h, c, &full[s]);
+                    }
+                }
+                ++issued;
+            }
+            for (int t = max(0, issued - kWStages); t < issued; ++t)
+                mbar_wait_bounded(&full[t % kWStages], static_cast<uint32_t>(t / kWStages) & 1u);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t qhi = smem_base + kOffQhi, qlo = smem_base + kOffQlo;
+            const uint32_t pbuf = smem_base + kOffP;
+            bool ok = true;
+            auto pv = [&](int i) {
+                if (!mbar_wait_bounded(pfull, static_cast<uint32_t>(i) & 1u) || *abort_flag) return false;
+                tc_fence_after();
+                const uint32_t vb = smem_base + kOffStage + (i % kWStages) * kStageBytes + kKVBytes;
+#pragma unroll
+                for (int kk = 0; kk < kWKeys / 16; ++kk) {
+                    // A = P [128 rows][64 keys] K-major; B = V [key][128 dims] MN-major
+                    const uint64_t ad = smem_desc(pbuf + kk * 32, 16, 1024);
+                    const uint64_t bd = smem_desc(vb + kk * 16 * 128, kWKeys * 128, 1024);
+                    umma_bf16(tmem + 128, ad, bd, kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(pvdone);
+                umma_commit(&empty[i % kWStages]);
+                return true;
+            };
+            for (int jt = 0; jt < ntiles && ok; ++jt) {
+                const int s = jt % kWStages;
+                if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(jt / kWStages) & 1u) || *abort_flag) {
+                    ok = false;
+                    break;
+                }
+                if (jt >= 2 && (!mbar_wait_bounded(&sfree[jt & 1], static_cast<uint32_t>((jt - 2) / 2) & 1u) ||
+                                *abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t kb = smem_base + kOffStage + s * kStageBytes;
+                const uint32_t sd = tmem + (jt & 1) * kWKeys;
+#pragma unroll
+                for (int kk = 0; kk < kWD / 16; ++kk) {
+                    // A = Q [128 rows][128 dims] K-major, B = K [64 keys][128 dims] K-major
+                    const uint32_t qoff = (kk >> 2) * (kWRows * 128) + (kk & 3) * 32;
+                    const uint32_t koff = (kk >> 2) * (kWKeys * 128) + (kk & 3) * 32;
+                    const uint64_t bd = smem_desc(kb + koff, 16, 1024);
+                    umma_bf16(sd, smem_desc(qhi + qoff, 16, 1024), bd, kIdescS, kk > 0 ? 1u : 0u);
+                    umma_bf16(sd, smem_desc(qlo + qoff, 16, 1024), bd, kIdescS, 1u);
+                }
+                umma_commit(&sfull[jt & 1]);
+                if (jt >= 1 && !pv(jt - 1)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (ok && ntiles > 0 && !pv(ntiles - 1)) ok = false;
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(p.err, kErrTimeout);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ softmax warpgroup
+        const int q4 = warp & 3;
+        const int r = 32 * q4 + lane;
+        const int t = r / g, jh = r % g;
+        const bool live = t < ntok;
+        const int qpos = qpos0 + t;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int jt = 0; jt < ntiles; ++jt) {
+            const int kbase = jt * kWKeys;
+            const bool got = mbar_wait_bounded(&sfull[jt & 1], static_cast<uint32_t>(jt / 2) & 1u);
+            if (!__all_sync(0xffffffffu, got) || *abort_flag) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sv[64];
+            {
+                float a[32], b[32];
+                tmem_ld32(trow + (jt & 1) * kWKeys, a);
+                tmem_ld32(trow + (jt & 1) * kWKeys + 32, b);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    sv[i] = a[i];
+                    sv[32 + i] = b[i];
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sfree[jt & 1]);
+            // mask (absolute positions) + online softmax for this row
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                const int kp = kbase + i;
+                if (!(live && kp <= qpos && kp < kv_end)) sv[i] = -INFINITY;
+                mx = fmaxf(mx, sv[i]);
+            }
+            const float mnew = fmaxf(m, mx);
+            const float base = mnew == -INFINITY ? 0.f : mnew;
+            const float corr = m == -INFINITY ? 0.f : exp2f(m - base);
+            float sum = 0.f;
+            uint32_t pk[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float a = exp2f(sv[2 * i] - base), b = exp2f(sv[2 * i + 1] - base);
+                sum += a + b;
+                pk[i] = pack_bf16(a, b);
+            }
+            l = l * corr + sum;
+            m = mnew;
+            if (jt >= 1) {
+                const bool done = mbar_wait_bounded(pvdone, static_cast<uint32_t>(jt - 1) & 1u);
+                if (!__all_sync(0xffffffffu, done) || *abort_flag) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll 1
+                    for (int c = 0; c < kWD / 32; ++c) {
+                        float o[32];
+                        tmem_ld32(trow + 128 + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= corr;
+                        tmem_st32(trow + 128 + c * 32, o);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            if (jt == ntiles - 1 && kv_end < kbase + kWKeys) {
+                // keys past the context in the last tile: zero their V rows so P = 0 meets 0
+                const int s = jt % kWStages;
+                const bool landed = mbar_wait_bounded(&full[s], static_cast<uint32_t>(jt / kWStages) & 1u);
+                if (!__all_sync(0xffffffffu, landed)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* vd = smem + kOffStage + s * kStageBytes + kKVBytes;
+                const int first = kv_end - kbase;
+                const int units = (kWKeys - first) * 2 * 8;
+                for (int x = threadIdx.x - 64; x < units; x += 128) {
+                    const int key = first + x / 16;
+                    const int c = (x / 8) & 1;
+                    *reinterpret_cast<uint4*>(vd + c * (kWKeys * 128) + sw128(key, x & 7)) = make_uint4(0, 0, 0, 0);
+                }
+            }
+            // P row -> shared memory (A operand of P.V)
+            uint8_t* prow = smem + kOffP;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                *reinterpret_cast<uint4*>(prow + sw128(r, u)) =
+                    make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            fence_proxy_async_smem();
+            tc_fence_before();
+            // one arrival per warp (count 4): the MMA starts once all rows of P are written
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pfull);
+        }
+        if (ok && ntiles > 0) {
+            const bool done = mbar_wait_bounded(pvdone, static_cast<uint32_t>(ntiles - 1) & 1u);
+            ok = __all_sync(0xffffffffu, done) && !*abort_flag;
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            if (lane == 0) atomicExch(p.err, kErrTimeout);
+        } else {
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            float* op = p.out + (static_cast<size_t>(p.offsets[seq] + t0 + (live ? t : 0)) * p.H + h * g + jh) * kWD;
+#pragma unroll 1
+            for (int c = 0; c < kWD / 32; ++c) {
+                float o[32];
+                tmem_ld32(trow + 128 + c * 32, o);
+                tmem_wait_ld();
+                if (live)
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(op + c * 32 + i) =
+                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+size_t wide_smem_bytes() { return kSmemBytes; }
+
+cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tmv1, const WideParams& p,
+                                  cudaStream_t st) {
+    if (p.nitems <= 0) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(wide_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    wide_attn_kernel<<<dim3(p.nitems, p.kvh), kWThreads, kSmemBytes, st>>>(*tmk1, *tmv1, p);
+    return cudaGetLastError();
+}
+
+}  // namespace pk

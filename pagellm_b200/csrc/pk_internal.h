@@ -90,6 +90,27 @@ struct GenericParams {
     float scale;  // 1/sqrt(D)
 };
 
+// Tensor-core (tcgen05) wide-tile attention: one CTA per (work item, KV head); a work
+// item is 128 query rows (= 128/g tokens) of one sequence.
+struct WideParams {
+    const float* q;
+    float* out;
+    int* err;
+    const int32_t* indptr;
+    const int32_t* ids;
+    const int32_t* starts;
+    const int32_t* offsets;
+    const int32_t* w_seq;  // [nitems] sequence of each work item
+    const int32_t* w_t0;   // [nitems] first query token of the item within its sequence
+    int nitems;
+    int H;
+    int kvh;
+    int g;
+    int bs;
+    int64_t layer_slot0;
+    float qscale;
+};
+
 // Read-only view of a pool's fields for entry points outside pk_api.cu.
 struct PoolView {
     int device;
@@ -112,6 +133,9 @@ cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUt
                                 const TcParams& p, size_t smem, cudaStream_t st);
 size_t tc_smem_bytes(int D, int bs, int kvh, int stages);
 cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st);
+size_t wide_smem_bytes();
+cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tmv1, const WideParams& p,
+                                  cudaStream_t st);
 // Same merge as a programmatic dependent launch of the preceding attention kernel.
 cudaError_t launch_merge_dependent(const MergeParams& p, int nsplit, cudaStream_t st);
 cudaError_t launch_generic_attention(int dtype, const GenericParams& p, cudaStream_t st);

@@ -379,3 +379,48 @@ def test_fused_append_single_launch_c2():
     b.write_and_attend(0, q, k, v)
     st = b.stats()
     assert st["launches"] == 1 and st["split_units"] > 0
+
+
+@pytest.mark.parametrize("H,KVH,bs", [(32, 8, 16), (64, 8, 16), (16, 4, 32)])
+def test_wide_tile_chunks_match_oracle(H, KVH, bs):
+    """Chunked prefill / long verify windows on the tcgen05 wide-tile kernel: prefill from
+    position 0, chunks over a cached prefix with lengths off the 128-row tile, next to
+    decode rows (split-KV kernel) in one step."""
+    torch = torch_cuda()
+    from pagellm_b200.cache import PagedBatch, PagedKVPool
+
+    g = H // KVH
+    ctx = [100, 1536, 333, 57, 900, 64]
+    n_new = [100, 512, 48, 1, 1, 20]
+    nb = sum(-(-c // bs) for c in ctx) + 8
+    rng = np.random.default_rng(H + bs)
+    perm = rng.permutation(nb)
+    tables, used = [], 0
+    for c in ctx:
+        k_ = -(-c // bs)
+        tables.append(perm[used:used + k_].tolist())
+        used += k_
+    starts = [c - n for c, n in zip(ctx, n_new)]
+    pool = PagedKVPool(Shape(1, KVH, 128), nb, bs, "bfloat16")
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    pool.k.copy_(torch.randn(pool.k.shape, generator=gen, device="cuda").to(pool.k.dtype))
+    pool.v.copy_(torch.randn(pool.v.shape, generator=gen, device="cuda").to(pool.v.dtype))
+    rows = sum(n_new)
+    q = torch.randn((rows, H, 128), generator=gen, device="cuda")
+    k = torch.randn((rows, KVH, 128), generator=gen, device="cuda")
+    v = torch.randn((rows, KVH, 128), generator=gen, device="cuda")
+    b = PagedBatch(pool, tables, starts, n_new)
+    out = b.write_and_attend(0, q, k, v)
+    b.check()
+    st = b.stats()
+    assert st["wide_items"] > 0, st
+    got, qh = out.cpu().numpy(), q.cpu().numpy()
+    meta = po.StepMeta(tables, starts, n_new, bs)
+    for i in range(len(ctx)):
+        kc, vc = gather_rows(pool, 0, meta.ctx_slots[i])
+        a, z = meta.offsets[i], meta.offsets[i + 1]
+        _close(got[a:z], po.attention_dense(qh[a:z], kc, vc, starts[i]), True)
+    # the appended rows of every sequence (wide and split-KV) are in the pool, bit for bit
+    sl = torch.as_tensor(meta.slots, device="cuda")
+    assert np.array_equal(bf16_bits_of_tensor(pool.k_flat[0].index_select(0, sl)),
+                          po.bf16_bits(k.cpu().numpy()).reshape(k.shape))
