@@ -137,8 +137,14 @@ PK_API int pk_batch_stats(const pk_batch* batch, int64_t* stats8);
  * counts, then resets. */
 PK_API int pk_batch_profile(pk_batch* batch, int enable);
 PK_API int pk_batch_profile_read(pk_batch* batch, double* ms5, int64_t* count5);
+/* Self-test of the bounded device waits (no counterpart in pagellm): launches a kernel
+ * that waits on a barrier phase nothing completes; the wait gives up after limit_ns
+ * (<= 2 s) and the kernel reports it. *timed_out = 1 when that happened as designed.
+ * Synchronises the device. */
+PK_API int pk_selftest_bounded_wait(int device, int64_t limit_ns, int* timed_out);
 /* Host-only dry run of the split-KV planner (no device needed): given per-unit block
- * counts, returns for each CTA its first block [ncta+1] (ncta = min(total, max_ctas)). */
+ * counts, returns for each CTA its first block [ncta+1], with
+ * ncta = max(1, min(max_ctas, total / 16)) - the planner gives a CTA at least 16 blocks. */
 PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,
                       int64_t* cta_first_block, int* ncta);
 

@@ -16,6 +16,7 @@
 
 #include "pagekv.h"
 #include "pk_internal.h"
+#include "pk_device.cuh"
 
 namespace {
 
@@ -201,6 +202,10 @@ struct pk_batch {
     std::vector<int32_t> app_rows;  // winner rows when slots repeat (else empty = all rows)
     std::vector<int32_t> writer_seq, writer_idx;  // per block id, scratch of the check
     DevBuf counters;  // per (unit, KV head) merge counters, zero between launches
+    // Wide-tile work runs on a side stream, forked from and joined back into the caller's
+    // stream with events, so it overlaps the split-KV kernel.
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     DevBuf rows;    // positions [nrows] then slots [nrows]
     DevBuf err;     // one int
     // attention plan for plan_H query heads
@@ -338,6 +343,9 @@ void setup_tc(pk_pool* P) {
 
 int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
+// Fewest K/V blocks a split-KV CTA is given when there are fewer than 148 such shares.
+constexpr int64_t kMinBlocksPerCta = 16;
+
 // Sequences with at least this many new query rows (tokens x heads per KV head) go to the
 // wide-tile tensor-core kernel; fewer rows stay on the split-KV kernel's units.
 constexpr int64_t kWideMinRows = 64;
@@ -422,7 +430,10 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     if (B->nu > 0) {
         B->use_tc = true;
         B->total_blocks = static_cast<int>(T);
-        B->ncta = static_cast<int>(std::min<int64_t>(T, P->num_sms));
+        // One CTA per SM, but at least kMinBlocksPerCta blocks each: on small steps more
+        // CTAs would cut every unit into many partials whose merge outweighs the bandwidth
+        // the extra SMs add.
+        B->ncta = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(P->num_sms, T / kMinBlocksPerCta)));
         for (int u = 0; u < B->nu; ++u) {
             const int c0 = cta_of_block(B->u_blk[u], T, B->ncta);
             const int c1 = cta_of_block(B->u_blk[u + 1] - 1, T, B->ncta);
@@ -497,6 +508,8 @@ int check_heads(const pk_batch* B, int H) {
 
 int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaStream_t st,
                 const float* k_new = nullptr, const float* v_new = nullptr) {
+    // k_new set: fused append - the split-KV kernel appends its units' rows, and the rows
+    // of wide-tile sequences are appended just before the wide kernel, on its stream.
     pk_pool* P = B->pool;
     if (B->plan_H != H) {
         int rc = build_attention_plan(B, H, st);
@@ -504,6 +517,47 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
     }
     if (B->nrows == 0) return PK_OK;
     const int g = H / P->kvh;
+    // ---- wide-tile part (side stream when split-KV work runs beside it)
+    cudaStream_t ws = st;
+    if (B->nwide > 0 && B->use_tc) {
+        if (!B->side) PK_CUDA(cudaStreamCreateWithFlags(&B->side, cudaStreamNonBlocking));
+        if (!B->ev_fork) PK_CUDA(cudaEventCreateWithFlags(&B->ev_fork, cudaEventDisableTiming));
+        if (!B->ev_join) PK_CUDA(cudaEventCreateWithFlags(&B->ev_join, cudaEventDisableTiming));
+        PK_CUDA(cudaEventRecord(B->ev_fork, st));
+        PK_CUDA(cudaStreamWaitEvent(B->side, B->ev_fork, 0));
+        ws = B->side;
+    }
+    if (B->nwide > 0) {
+        if (k_new != nullptr) {
+            PK_CUDA(prof_begin(B, ws));
+            PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_new, v_new,
+                                      B->slots(), B->plan.at<int32_t>(10),
+                                      static_cast<int64_t>(B->w_rows.size()), P->kvh * P->d, ws));
+            PK_CUDA(prof_end(B, kProfAppend, ws));
+            B->launches++;
+        }
+        pk::WideParams w{};
+        w.q = q;
+        w.out = out;
+        w.err = static_cast<int*>(B->err.ptr);
+        w.indptr = B->meta.at<int32_t>(0);
+        w.ids = B->meta.at<int32_t>(1);
+        w.starts = B->meta.at<int32_t>(2);
+        w.offsets = B->meta.at<int32_t>(3);
+        w.w_seq = B->plan.at<int32_t>(8);
+        w.w_t0 = B->plan.at<int32_t>(9);
+        w.nitems = B->nwide;
+        w.H = H;
+        w.kvh = P->kvh;
+        w.g = g;
+        w.bs = P->block_size;
+        w.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
+        w.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
+        PK_CUDA(prof_begin(B, ws));
+        PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, ws));
+        PK_CUDA(prof_end(B, kProfWide, ws));
+        B->launches++;
+    }
     if (B->use_tc) {
         pk::TcParams p{};
         p.q = q;
@@ -561,28 +615,9 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
             B->launches++;
         }
     }
-    if (B->nwide > 0) {
-        pk::WideParams w{};
-        w.q = q;
-        w.out = out;
-        w.err = static_cast<int*>(B->err.ptr);
-        w.indptr = B->meta.at<int32_t>(0);
-        w.ids = B->meta.at<int32_t>(1);
-        w.starts = B->meta.at<int32_t>(2);
-        w.offsets = B->meta.at<int32_t>(3);
-        w.w_seq = B->plan.at<int32_t>(8);
-        w.w_t0 = B->plan.at<int32_t>(9);
-        w.nitems = B->nwide;
-        w.H = H;
-        w.kvh = P->kvh;
-        w.g = g;
-        w.bs = P->block_size;
-        w.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
-        w.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
-        PK_CUDA(prof_begin(B, st));
-        PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, st));
-        PK_CUDA(prof_end(B, kProfWide, st));
-        B->launches++;
+    if (ws != st) {
+        PK_CUDA(cudaEventRecord(B->ev_join, ws));
+        PK_CUDA(cudaStreamWaitEvent(st, B->ev_join, 0));
     }
     if (B->ngeneric > 0) {
         if (P->d > 512) return fail(PK_ERR_UNSUPPORTED, "head_dim %d > 512", P->d);
@@ -815,6 +850,9 @@ int pk_batch_destroy(pk_batch* B) {
     B->counters.release();
     B->io.release();
     for (cudaEvent_t e : B->ev_pool) cudaEventDestroy(e);
+    if (B->ev_fork) cudaEventDestroy(B->ev_fork);
+    if (B->ev_join) cudaEventDestroy(B->ev_join);
+    if (B->side) cudaStreamDestroy(B->side);
     delete B;
     return PK_OK;
 }
@@ -979,19 +1017,8 @@ int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* 
         rc = build_attention_plan(B, n_heads, st);
         if (rc != PK_OK) return rc;
     }
-    if (B->ngeneric == 0 && B->fuse_append_ok && (B->use_tc || B->nwide > 0)) {
-        // split-KV units append their own rows inside the attention kernel; rows of
-        // wide-tile sequences are appended first by the row-list append kernel
-        if (B->nwide > 0) {
-            PK_CUDA(prof_begin(B, st));
-            PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_dev, v_dev,
-                                      B->slots(), B->plan.at<int32_t>(10),
-                                      static_cast<int64_t>(B->w_rows.size()), P->kvh * P->d, st));
-            PK_CUDA(prof_end(B, kProfAppend, st));
-            B->launches++;
-        }
+    if (B->ngeneric == 0 && B->fuse_append_ok && (B->use_tc || B->nwide > 0))
         return attend_impl(B, layer, n_heads, q_dev, out_dev, st, k_dev, v_dev);
-    }
     if (B->nrows > 0) {
         const bool listed = !B->app_rows.empty();
         PK_CUDA(prof_begin(B, st));
@@ -1094,6 +1121,24 @@ int pk_batch_profile_read(pk_batch* B, double* ms5, int64_t* count5) {
     return PK_OK;
 }
 
+int pk_selftest_bounded_wait(int device, int64_t limit_ns, int* timed_out) {
+    if (!timed_out || limit_ns <= 0 || limit_ns > 2000000000LL)
+        return fail(PK_ERR_INVALID_ARG, "limit_ns must be in (0, 2e9]");
+    DeviceScope ds(device);
+    if (ds.err != cudaSuccess) return fail(PK_ERR_CUDA, "cudaSetDevice(%d)", device);
+    int* word = nullptr;
+    PK_CUDA(cudaMalloc(&word, sizeof(int)));
+    cudaError_t e = cudaMemset(word, 0, sizeof(int));
+    if (e == cudaSuccess) e = pk::launch_bounded_wait_selftest(word, static_cast<unsigned long long>(limit_ns), nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    int v = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&v, word, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(word);
+    if (e != cudaSuccess) return fail(PK_ERR_CUDA, "bounded-wait self-test: %s", cudaGetErrorString(e));
+    *timed_out = v == pk::kErrTimeout ? 1 : 0;
+    return PK_OK;
+}
+
 int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,
                       int64_t* cta_first_block, int* ncta) {
     if (n_units < 0 || max_ctas <= 0 || !ncta) return fail(PK_ERR_INVALID_ARG, "bad arguments");
@@ -1102,7 +1147,7 @@ int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,
         if (unit_blocks[i] <= 0) return fail(PK_ERR_INVALID_ARG, "unit %lld has no blocks", (long long)i);
         T += unit_blocks[i];
     }
-    const int64_t n = std::min<int64_t>(T, max_ctas);
+    const int64_t n = T == 0 ? 0 : std::max<int64_t>(1, std::min<int64_t>(max_ctas, T / kMinBlocksPerCta));
     *ncta = static_cast<int>(n);
     if (cta_first_block)
         for (int64_t c = 0; c <= n; ++c) cta_first_block[c] = n ? cta_lo(c, T, n) : 0;

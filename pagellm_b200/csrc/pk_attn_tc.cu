@@ -435,6 +435,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                             mx[nt][e] = -INFINITY;
                             den[nt][e] = 0.f;
                         }
+#pragma unroll 4
                     for (int cc = cf; cc <= cl; ++cc) {
                         const size_t ob = ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols;
 #pragma unroll
@@ -453,6 +454,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                             for (int i = 0; i < 4; ++i) num[mt][nt][i] = 0.f;
+#pragma unroll 2
                     for (int cc = cf; cc <= cl; ++cc) {
                         const size_t ob = ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols;
                         const bool own = cc == c;

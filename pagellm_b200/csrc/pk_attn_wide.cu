@@ -15,8 +15,9 @@
 //           S_j = Q . K_j^T   (M=128, N=64,  K=128, bf16 -> fp32 TMEM, Q as bf16 hi + lo)
 //           O  += P_j . V_j   (M=128, N=128, K=64;  P from shared memory, V MN-major)
 //   warps 2-5 softmax warpgroup: thread = row. Loads S_j from TMEM, masks by absolute
-//           position, online max/sum in the exp2 domain, rescales O in TMEM when the max
-//           grows, writes P_j (bf16) to shared memory, and finally O / l to global.
+//           position, online max/sum in the exp2 domain (the base moves only when a tile's
+//           max exceeds it by 2^8, and only then is O in TMEM rescaled), writes P_j (bf16)
+//           to shared memory, and finally O / l to global.
 // S is double-buffered in TMEM (columns 0-63, 64-127), O lives in columns 128-255.
 // Every wait is bounded; on a timeout the CTA records the error, unwinds and frees TMEM.
 
@@ -345,7 +346,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 if (!(live && kp <= qpos && kp < kv_end)) sv[i] = -INFINITY;
                 mx = fmaxf(mx, sv[i]);
             }
-            const float mnew = fmaxf(m, mx);
+            // Lazy rescale: keep the exponent base of earlier tiles unless this tile's max
+            // exceeds it by more than 8 (P stays <= 2^8 in bf16, l and O in fp32), so O in
+            // TMEM is rescaled only when the base actually moves.
+            const float mnew = (m == -INFINITY || mx > m + 8.f) ? mx : m;
             const float base = mnew == -INFINITY ? 0.f : mnew;
             const float corr = m == -INFINITY ? 0.f : exp2f(m - base);
             float sum = 0.f;

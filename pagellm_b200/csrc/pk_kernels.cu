@@ -207,6 +207,19 @@ cudaError_t launch_generic_t(const GenericParams& p, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// Self-test of the bounded wait every pipeline uses: wait on an mbarrier phase that nothing
+// completes; the wait must give up after limit_ns and report through the error word.
+__global__ void bounded_wait_selftest_kernel(int* err, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const bool done = mbar_wait_bounded(&bar, 0u, limit_ns);
+    if (!done && threadIdx.x == 0) atomicExch(err, kErrTimeout);
+}
+
 int grid_for(int64_t work, int threads) {
     int64_t b = (work + threads - 1) / threads;
     if (b < 1) b = 1;
@@ -270,6 +283,11 @@ cudaError_t launch_copy_blocks(void* k, void* v, const int64_t* pairs, int64_t n
         copy_blocks_kernel<uint32_t><<<grid, 256, 0, st>>>(kb, vb, pairs, layer_bytes, block_bytes);
     else
         copy_blocks_kernel<uint16_t><<<grid, 256, 0, st>>>(kb, vb, pairs, layer_bytes, block_bytes);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bounded_wait_selftest(int* err, unsigned long long limit_ns, cudaStream_t st) {
+    bounded_wait_selftest_kernel<<<1, 32, 0, st>>>(err, limit_ns);
     return cudaGetLastError();
 }
 

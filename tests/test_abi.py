@@ -47,18 +47,18 @@ def test_pool_create_rejects_bad_arguments_before_touching_cuda():
                                          ([1], 148), (list(range(1, 300)), 148)])
 def test_split_kv_partition_is_balanced_and_complete(blocks, ctas):
     """CTA c owns blocks [c*T/n, (c+1)*T/n): every block once, sizes differ by at most 1,
-    n = min(T, max_ctas) so no CTA is empty."""
+    n = max(1, min(max_ctas, T // 16)) so no CTA is empty or tiny."""
     lib = _lib.load()
     b = np.asarray(blocks, dtype=np.int64)
     T = int(b.sum())
-    n = min(T, ctas)
+    n = max(1, min(ctas, T // 16))
     first = np.zeros(n + 1, dtype=np.int64)
     got = C.c_int()
     assert lib.pk_plan_partition(b.ctypes.data_as(C.POINTER(C.c_int64)), len(b), ctas,
                                  first.ctypes.data_as(C.POINTER(C.c_int64)), C.byref(got)) == 0
     assert got.value == n and first[0] == 0 and first[-1] == T
     sizes = np.diff(first)
-    assert sizes.min() >= 1 and sizes.max() - sizes.min() <= 1
+    assert sizes.min() >= min(T, 16) and sizes.max() - sizes.min() <= 1
 
 
 def test_partition_rejects_empty_units():

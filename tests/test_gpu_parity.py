@@ -424,3 +424,24 @@ def test_wide_tile_chunks_match_oracle(H, KVH, bs):
     sl = torch.as_tensor(meta.slots, device="cuda")
     assert np.array_equal(bf16_bits_of_tensor(pool.k_flat[0].index_select(0, sl)),
                           po.bf16_bits(k.cpu().numpy()).reshape(k.shape))
+
+
+def test_bounded_wait_gives_up_and_context_survives():
+    """Failure detection without a GPU fault: a wait on a barrier phase that nothing
+    completes returns after its limit with an error status the host reads; the context
+    is still usable afterwards."""
+    import ctypes as C
+    import time
+
+    torch = torch_cuda()
+    from pagellm_b200 import _lib, workloads
+
+    lib = _lib.load()
+    flag = C.c_int(-1)
+    t0 = time.perf_counter()
+    assert lib.pk_selftest_bounded_wait(0, 50_000_000, C.byref(flag)) == 0, _lib.last_error()
+    assert flag.value == 1
+    assert time.perf_counter() - t0 < 10.0
+    w = workloads.c2(2, batch=3)
+    _run_config(w, [0, 1, 2])
+    torch.cuda.synchronize()
