@@ -248,11 +248,14 @@ bool encode_chunk_maps(pk_pool* P, std::string* why) {
     const cuuint64_t slots = static_cast<cuuint64_t>(P->n_layers) * P->num_blocks * P->block_size;
     cuuint64_t dims[4] = {64, slots, static_cast<cuuint64_t>(P->kvh), static_cast<cuuint64_t>(P->d / 64)};
     cuuint64_t strides[3] = {static_cast<cuuint64_t>(P->kvh) * P->d * 2, static_cast<cuuint64_t>(P->d) * 2, 128};
-    cuuint32_t box[4] = {64, static_cast<cuuint32_t>(P->block_size), 1, 1};
+    // K: one 64-dim chunk of one block per box; V: both chunks of one block per box
+    const cuuint32_t box_k[4] = {64, static_cast<cuuint32_t>(P->block_size), 1, 1};
+    const cuuint32_t box_v[4] = {64, static_cast<cuuint32_t>(P->block_size), 1, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     for (int t = 0; t < 2; ++t) {
         CUresult r = enc(t == 0 ? &P->tmk1 : &P->tmv1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
-                         t == 0 ? P->k : P->v, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         t == 0 ? P->k : P->v, dims, strides, t == 0 ? box_k : box_v, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) {

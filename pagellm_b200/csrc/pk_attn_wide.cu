@@ -9,16 +9,18 @@
 // g heads share every K/V tile. Keys stream in tiles of 64 (64/bs blocks).
 //
 // Warp roles (192 threads):
-//   warp 0  producer: one lane issues TMA loads (no multicast) of each block's K and V,
-//           one 64-dim chunk per copy, into a 3-stage ring; mbarrier completion.
-//   warp 1  TMEM owner (alloc/dealloc, 256 columns) and, on one lane, the MMA issuer:
+//   warp 0  producer: one lane issues TMA loads (no multicast) of each block's K (one copy
+//           per 64-dim chunk, tile [chunk][key][64]) and V (one copy per block, tile
+//           [block][chunk][token][64]) into a 5-stage ring; mbarrier completion.
+//   warp 1  TMEM owner (alloc/dealloc, 512 columns) and, on one lane, the MMA issuer:
 //           S_j = Q . K_j^T   (M=128, N=64,  K=128, bf16 -> fp32 TMEM, Q as bf16 hi + lo)
-//           O  += P_j . V_j   (M=128, N=128, K=64;  P from shared memory, V MN-major)
+//           O  += P_j . V_j   (M=128, N=128, K=64;  P from TMEM, V MN-major from smem)
 //   warps 2-5 softmax warpgroup: thread = row. Loads S_j from TMEM, masks by absolute
 //           position, online max/sum in the exp2 domain (the base moves only when a tile's
 //           max exceeds it by 2^8, and only then is O in TMEM rescaled), writes P_j (bf16)
-//           to shared memory, and finally O / l to global.
-// S is double-buffered in TMEM (columns 0-63, 64-127), O lives in columns 128-255.
+//           into TMEM, and finally O / l to global.
+// S is double-buffered in TMEM (columns 0-63, 64-127), O lives in columns 128-255, and P
+// (bf16) is double-buffered in columns 256-319 as the A operand of the P.V MMA.
 // Every wait is bounded; on a timeout the CTA records the error, unwinds and frees TMEM.
 
 #include "pk_device.cuh"
@@ -31,20 +33,22 @@ namespace {
 constexpr int kWRows = 128;       // query rows per CTA (UMMA M)
 constexpr int kWKeys = 64;        // keys per tile (UMMA N of S, K of P.V)
 constexpr int kWD = 128;          // head dim
-constexpr int kWStages = 3;
+constexpr int kWStages = 5;
 constexpr int kWThreads = 192;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;
+// TMEM columns: S double buffer [0,64) [64,128); O [128,256); P double buffer (bf16 pairs)
+// [256,288) [288,320).
+constexpr uint32_t kColO = 128;
+constexpr uint32_t kColP = 256;
 
 // shared memory carve-up (bytes from a 1024-aligned base)
 constexpr int kQBytes = kWRows * kWD * 2;            // 32 KB per Q half (hi, lo): [chunk][row][64]
-constexpr int kKVBytes = kWKeys * kWD * 2;           // 16 KB per K or V tile: [chunk][key][64]
+constexpr int kKVBytes = kWKeys * kWD * 2;           // 16 KB per K or V tile
 constexpr int kStageBytes = 2 * kKVBytes;
-constexpr int kPBytes = kWRows * kWKeys * 2;         // 16 KB: [row][64 keys]
 constexpr int kOffQhi = 0;
 constexpr int kOffQlo = kOffQhi + kQBytes;
 constexpr int kOffStage = kOffQlo + kQBytes;
-constexpr int kOffP = kOffStage + kWStages * kStageBytes;
-constexpr int kOffBar = kOffP + kPBytes;
+constexpr int kOffBar = kOffStage + kWStages * kStageBytes;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 
 // ---------------------------------------------------------------- tcgen05 wrappers
@@ -70,6 +74,15 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// A operand from TMEM (rows = lanes, K packed two bf16 per 32-bit column).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -103,6 +116,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 2^x on the special-function unit (approximate, flush-to-zero; 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // Shared-memory matrix descriptor, 128-byte swizzle (sm_100 format: version 1).
 // lbo / sbo in bytes (multiples of 16).
@@ -145,9 +165,9 @@ __global__ void __launch_bounds__(kWThreads, 1)
     uint64_t* empty = full + kWStages;
     uint64_t* sfull = empty + kWStages;  // [2]
     uint64_t* sfree = sfull + 2;         // [2]
-    uint64_t* pfull = sfree + 2;
-    uint64_t* pvdone = pfull + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pvdone + 1);
+    uint64_t* pfull = sfree + 2;         // [2] per P buffer
+    uint64_t* pvdone = pfull + 2;        // [2] per P buffer
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pvdone + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -175,8 +195,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
             mbar_init(&sfull[b], 1);
             mbar_init(&sfree[b], 4);
         }
-        mbar_init(pfull, 4);
-        mbar_init(pvdone, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&pfull[b], 4);
+            mbar_init(&pvdone[b], 1);
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -238,10 +260,11 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 for (int b = 0; b < per_tile; ++b) {
                     const int bi = min(jt * per_tile + b, nblk_ctx - 1);  // past the end: a valid block, masked
                     const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(tbl[bi]) * p.bs);
+                    // K: [chunk][key][64] (one copy per 64-dim chunk); V: [block][chunk][token][64]
+                    // (one copy per block: both chunks)
                     for (int c = 0; c < 2; ++c) {
-                        const int off = c * (kWKeys * 128) + b * p.bs * 128;
-                        tma_load_4d(kd + off, &tmk, 0, slot0, h, c, &full[s]);
-                        tma_load_4d(vd + off, &tmv, 0, slot0, h, c, &full[s]);
+                        tma_load_4d(kd + c * (kWKeys * 128) + b * p.bs * 128, &tmk, 0, slot0, h, c, &full[s]);
+                        tma_load_4d(vd + c * (kWKeys * 128) + b * p.bs * 128, &tmv, 0, slot0, h, c, &full[s]);
                     }
                 }
                 ++issued;
@@ -251,55 +274,67 @@ __global__ void __launch_bounds__(kWThreads, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        // Issues S_j and PV_{j-1} in whichever order their inputs become ready (polling
+        // both barriers without blocking), so P.V never waits behind the next K/V load.
         if (lane == 0) {
-            const uint32_t qhi = smem_base + kOffQhi, qlo = smem_base + kOffQlo;
-            const uint32_t pbuf = smem_base + kOffP;
+            // Descriptors: Q's are loop invariant; K's and V's are a base plus the 16-byte
+            // units of the stage / k-step offset (the start-address field is the low 14 bits).
+            uint64_t qd_hi[kWD / 16], qd_lo[kWD / 16];
+#pragma unroll
+            for (int kk = 0; kk < kWD / 16; ++kk) {
+                const uint32_t qoff = (kk >> 2) * (kWRows * 128) + (kk & 3) * 32;
+                qd_hi[kk] = smem_desc(smem_base + kOffQhi + qoff, 16, 1024);
+                qd_lo[kk] = smem_desc(smem_base + kOffQlo + qoff, 16, 1024);
+            }
+            const uint64_t kd0 = smem_desc(smem_base + kOffStage, 16, 1024);
+            const uint64_t vd0 = smem_desc(smem_base + kOffStage + kKVBytes, kWKeys * 128, 1024);
+            int js = 0, jp = 0;  // next S tile / next P.V tile to issue
+            unsigned long long idle_since = global_ns();
             bool ok = true;
-            auto pv = [&](int i) {
-                if (!mbar_wait_bounded(pfull, static_cast<uint32_t>(i) & 1u) || *abort_flag) return false;
-                tc_fence_after();
-                const uint32_t vb = smem_base + kOffStage + (i % kWStages) * kStageBytes + kKVBytes;
+            while (jp < ntiles) {
+                bool progressed = false;
+                if (js < ntiles && mbar_test_wait(&full[js % kWStages], static_cast<uint32_t>(js / kWStages) & 1u) &&
+                    (js < 2 || mbar_test_wait(&sfree[js & 1], static_cast<uint32_t>((js - 2) / 2) & 1u))) {
+                    tc_fence_after();
+                    const uint32_t sbase = static_cast<uint32_t>((js % kWStages) * kStageBytes);
+                    const uint32_t sd = tmem + (js & 1) * kWKeys;
 #pragma unroll
-                for (int kk = 0; kk < kWKeys / 16; ++kk) {
-                    // A = P [128 rows][64 keys] K-major; B = V [key][128 dims] MN-major
-                    const uint64_t ad = smem_desc(pbuf + kk * 32, 16, 1024);
-                    const uint64_t bd = smem_desc(vb + kk * 16 * 128, kWKeys * 128, 1024);
-                    umma_bf16(tmem + 128, ad, bd, kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < kWD / 16; ++kk) {
+                        // A = Q [128 rows][128 dims] K-major, B = K [64 keys][128 dims] K-major
+                        const uint32_t koff = sbase + (kk >> 2) * (kWKeys * 128) + (kk & 3) * 32;
+                        const uint64_t bd = kd0 + (koff >> 4);
+                        umma_bf16(sd, qd_hi[kk], bd, kIdescS, kk > 0 ? 1u : 0u);
+                        umma_bf16(sd, qd_lo[kk], bd, kIdescS, 1u);
+                    }
+                    umma_commit(&sfull[js & 1]);
+                    ++js;
+                    progressed = true;
                 }
-                umma_commit(pvdone);
-                umma_commit(&empty[i % kWStages]);
-                return true;
-            };
-            for (int jt = 0; jt < ntiles && ok; ++jt) {
-                const int s = jt % kWStages;
-                if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>(jt / kWStages) & 1u) || *abort_flag) {
-                    ok = false;
-                    break;
-                }
-                if (jt >= 2 && (!mbar_wait_bounded(&sfree[jt & 1], static_cast<uint32_t>((jt - 2) / 2) & 1u) ||
-                                *abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t kb = smem_base + kOffStage + s * kStageBytes;
-                const uint32_t sd = tmem + (jt & 1) * kWKeys;
+                if (jp < js && mbar_test_wait(&pfull[jp & 1], static_cast<uint32_t>(jp / 2) & 1u)) {
+                    tc_fence_after();
+                    const uint32_t sbase = static_cast<uint32_t>((jp % kWStages) * kStageBytes);
 #pragma unroll
-                for (int kk = 0; kk < kWD / 16; ++kk) {
-                    // A = Q [128 rows][128 dims] K-major, B = K [64 keys][128 dims] K-major
-                    const uint32_t qoff = (kk >> 2) * (kWRows * 128) + (kk & 3) * 32;
-                    const uint32_t koff = (kk >> 2) * (kWKeys * 128) + (kk & 3) * 32;
-                    const uint64_t bd = smem_desc(kb + koff, 16, 1024);
-                    umma_bf16(sd, smem_desc(qhi + qoff, 16, 1024), bd, kIdescS, kk > 0 ? 1u : 0u);
-                    umma_bf16(sd, smem_desc(qlo + qoff, 16, 1024), bd, kIdescS, 1u);
+                    for (int kk = 0; kk < kWKeys / 16; ++kk) {
+                        // A = P in TMEM (16 keys = 8 columns per step); B = V MN-major: keys
+                        // 16kk..16kk+15 lie in block (16kk)/bs, chunks bs*128 bytes apart
+                        const int key0 = kk * 16;
+                        const uint32_t voff = sbase + key0 * 128;
+                        const uint64_t bd = vd0 + (voff >> 4);
+                        umma_bf16_ts(tmem + kColO, tmem + kColP + (jp & 1) * 32 + kk * 8, bd, kIdescO,
+                                     (jp > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&pvdone[jp & 1]);
+                    umma_commit(&empty[jp % kWStages]);
+                    ++jp;
+                    progressed = true;
                 }
-                umma_commit(&sfull[jt & 1]);
-                if (jt >= 1 && !pv(jt - 1)) {
+                if (progressed) {
+                    idle_since = global_ns();
+                } else if (*abort_flag || global_ns() - idle_since > kWaitLimitNs) {
                     ok = false;
                     break;
                 }
             }
-            if (ok && ntiles > 0 && !pv(ntiles - 1)) ok = false;
             if (!ok) {
                 *abort_flag = 1;
                 atomicExch(p.err, kErrTimeout);
@@ -338,46 +373,67 @@ __global__ void __launch_bounds__(kWThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sfree[jt & 1]);
-            // mask (absolute positions) + online softmax for this row
-            float mx = -INFINITY;
+            // mask by absolute position, only on tiles that reach past this row's position
+            // (earlier tiles are fully visible; dead rows mask everything)
+            if (!(live && kbase + kWKeys - 1 <= qpos)) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                const int kp = kbase + i;
-                if (!(live && kp <= qpos && kp < kv_end)) sv[i] = -INFINITY;
-                mx = fmaxf(mx, sv[i]);
+                for (int i = 0; i < 64; ++i)
+                    if (!(live && kbase + i <= qpos)) sv[i] = -INFINITY;
             }
+            // row max and sum as 8 independent chains (the serial chains were the slow part)
+            float mx8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                mx8[k] = sv[k];
+#pragma unroll
+                for (int i = k + 8; i < 64; i += 8) mx8[k] = fmaxf(mx8[k], sv[i]);
+            }
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             // Lazy rescale: keep the exponent base of earlier tiles unless this tile's max
             // exceeds it by more than 8 (P stays <= 2^8 in bf16, l and O in fp32), so O in
             // TMEM is rescaled only when the base actually moves.
             const float mnew = (m == -INFINITY || mx > m + 8.f) ? mx : m;
             const float base = mnew == -INFINITY ? 0.f : mnew;
-            const float corr = m == -INFINITY ? 0.f : exp2f(m - base);
-            float sum = 0.f;
+            const float corr = m == -INFINITY ? 0.f : ex2_approx(m - base);
+            float sum8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) sum8[k] = 0.f;
             uint32_t pk[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                const float a = exp2f(sv[2 * i] - base), b = exp2f(sv[2 * i + 1] - base);
-                sum += a + b;
+                const float a = ex2_approx(sv[2 * i] - base), b = ex2_approx(sv[2 * i + 1] - base);
+                sum8[i & 7] += a + b;
                 pk[i] = pack_bf16(a, b);
             }
+            const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
             l = l * corr + sum;
             m = mnew;
-            if (jt >= 1) {
-                const bool done = mbar_wait_bounded(pvdone, static_cast<uint32_t>(jt - 1) & 1u);
+            // P_j goes to TMEM buffer jt&1, last read by PV(jt-2)
+            if (jt >= 2) {
+                const bool done = mbar_wait_bounded(&pvdone[jt & 1], static_cast<uint32_t>((jt - 2) / 2) & 1u);
+                if (!__all_sync(0xffffffffu, done) || *abort_flag) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (jt >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+                // O must include PV(jt-1) before it is rescaled
+                const bool done = mbar_wait_bounded(&pvdone[(jt - 1) & 1], static_cast<uint32_t>((jt - 1) / 2) & 1u);
                 if (!__all_sync(0xffffffffu, done) || *abort_flag) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, corr != 1.f)) {
+                {
 #pragma unroll 1
                     for (int c = 0; c < kWD / 32; ++c) {
                         float o[32];
-                        tmem_ld32(trow + 128 + c * 32, o);
+                        tmem_ld32(trow + kColO + c * 32, o);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; ++i) o[i] *= corr;
-                        tmem_st32(trow + 128 + c * 32, o);
+                        tmem_st32(trow + kColO + c * 32, o);
                     }
                     tmem_wait_st();
                 }
@@ -399,20 +455,22 @@ __global__ void __launch_bounds__(kWThreads, 1)
                     *reinterpret_cast<uint4*>(vd + c * (kWKeys * 128) + sw128(key, x & 7)) = make_uint4(0, 0, 0, 0);
                 }
             }
-            // P row -> shared memory (A operand of P.V)
-            uint8_t* prow = smem + kOffP;
+            // P row -> TMEM (A operand of P.V), bf16 pairs along the columns
+            {
+                float pf[32];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                *reinterpret_cast<uint4*>(prow + sw128(r, u)) =
-                    make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-            fence_proxy_async_smem();
+                for (int i = 0; i < 32; ++i) pf[i] = __uint_as_float(pk[i]);
+                tmem_st32(trow + kColP + (jt & 1) * 32, pf);
+                tmem_wait_st();
+            }
+            fence_proxy_async_smem();  // the zeroed V rows (generic writes) before the MMA reads them
             tc_fence_before();
             // one arrival per warp (count 4): the MMA starts once all rows of P are written
             __syncwarp();
-            if (lane == 0) mbar_arrive(pfull);
+            if (lane == 0) mbar_arrive(&pfull[jt & 1]);
         }
         if (ok && ntiles > 0) {
-            const bool done = mbar_wait_bounded(pvdone, static_cast<uint32_t>(ntiles - 1) & 1u);
+            const bool done = mbar_wait_bounded(&pvdone[(ntiles - 1) & 1], static_cast<uint32_t>((ntiles - 1) / 2) & 1u);
             ok = __all_sync(0xffffffffu, done) && !*abort_flag;
         }
         if (!ok) {
@@ -425,7 +483,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
 #pragma unroll 1
             for (int c = 0; c < kWD / 32; ++c) {
                 float o[32];
-                tmem_ld32(trow + 128 + c * 32, o);
+                tmem_ld32(trow + kColO + c * 32, o);
                 tmem_wait_ld();
                 if (live)
 #pragma unroll
