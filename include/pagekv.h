@@ -129,6 +129,16 @@ PK_API int pk_batch_check(pk_batch* batch, void* stream);
  * [5] rows on the CUDA-core kernel, [6] kernels launched by the last call, [7] wide-tile
  * work items (128 query rows each) on the tcgen05 kernel. */
 PK_API int pk_batch_stats(const pk_batch* batch, int64_t* stats8);
+/* Shared-prefix (cascade) attention - no counterpart in pagellm, whose attention reads every
+ * sequence's keys separately (cache/paged.py:454-463): sequences of a step whose block
+ * tables begin with the same block ids (forks, prefix-cache hits) have the shared keys
+ * attended once per 128 query rows on the tcgen05 kernel, merged with the split-KV result
+ * for the rest of each sequence. `mode`: 0 off, 1 (default) where a cost estimate says it
+ * is faster than reading the prefix once per sequence, 2 for every eligible group; it
+ * applies from the next plan. pk_batch_prefix_stats: [0] prefix groups, [1] shared-prefix
+ * work items, [2] shared keys summed over the groups. */
+PK_API int pk_batch_set_prefix_sharing(pk_batch* batch, int mode);
+PK_API int pk_batch_prefix_stats(const pk_batch* batch, int64_t* stats3);
 
 /* Per-kernel timing of this batch's own launches: with profiling on, CUDA events are
  * recorded on the launching stream around every kernel. pk_batch_profile_read synchronises
@@ -144,7 +154,8 @@ PK_API int pk_batch_profile_read(pk_batch* batch, double* ms5, int64_t* count5);
 PK_API int pk_selftest_bounded_wait(int device, int64_t limit_ns, int* timed_out);
 /* Host-only dry run of the split-KV planner (no device needed): given per-unit block
  * counts, returns for each CTA its first block [ncta+1], with
- * ncta = max(1, min(max_ctas, total / 16)) - the planner gives a CTA at least 16 blocks. */
+ * ncta = max(1, min(max_ctas, total, max(total / 16, ceil(n_units / 3)))): at least 16
+ * blocks per CTA, unless many short units are better spread 3 per CTA. */
 PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,
                       int64_t* cta_first_block, int* ncta);
 

@@ -296,6 +296,8 @@ class PagedBatch:
         self._lib = lib
         self._b = pool._acquire_batch()
         self._fin = weakref.finalize(self, pool._release_batch, self._b)
+        _lib.check(lib.pk_batch_set_prefix_sharing(self._b, 1))  # recycled handles: default
+        self._prefix_sharing = "auto"
         rows = C.c_int64()
         _lib.check(lib.pk_batch_plan(
             self._b, len(n_new_a), indptr.ctypes.data_as(C.POINTER(C.c_int64)),
@@ -336,6 +338,28 @@ class PagedBatch:
         keys = ("rows", "tc_units", "tc_ctas", "tc_blocks", "split_units", "generic_rows", "launches",
                 "wide_items")
         return dict(zip(keys, list(s)))
+
+    _PREFIX_MODES = {False: 0, "off": 0, True: 1, "auto": 1, "always": 2}
+
+    @property
+    def prefix_sharing(self) -> str:
+        """Shared-prefix (cascade) attention for sequences whose block tables begin with the
+        same blocks: "auto" (default: where a cost estimate favours it), "always" or "off".
+        Not in pagellm; results are the same either way within floating-point rounding."""
+        return self._prefix_sharing
+
+    @prefix_sharing.setter
+    def prefix_sharing(self, mode) -> None:
+        if mode not in self._PREFIX_MODES:
+            raise ValueError(f"prefix_sharing must be 'off', 'auto' or 'always', not {mode!r}")
+        code = self._PREFIX_MODES[mode]
+        _lib.check(self._lib.pk_batch_set_prefix_sharing(self._b, code))
+        self._prefix_sharing = ("off", "auto", "always")[code]
+
+    def prefix_stats(self) -> dict:
+        s = (C.c_int64 * 3)()
+        _lib.check(self._lib.pk_batch_prefix_stats(self._b, s))
+        return dict(zip(("groups", "items", "shared_keys"), list(s)))
 
     # ------------------------------------------------------------------ per layer
     def write_and_attend(self, layer: int, q, k, v):

@@ -214,9 +214,18 @@ struct pk_batch {
     int nu = 0, total_blocks = 0, ncta = 0, nt = 1, nsplit = 0;
     int ngeneric = 0;
     std::vector<int32_t> u_seq, u_t0, u_n, u_blk, sp_u, sp_c0, sp_c1, gen_rows;
-    int nwide = 0;                           // wide-tile work items
-    std::vector<int32_t> w_seq, w_t0, w_rows;  // items; rows they cover (appended separately)
-    Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows 8 w_seq 9 w_t0 10 w_rows
+    // Wide-tile work items: [0, nwide) chunk items (side stream), then [nwide, nwide +
+    // nprefix) shared-prefix items (after the split-KV kernel, merged into its rows).
+    int nwide = 0, nprefix = 0, nprefix_groups = 0;
+    int64_t prefix_keys = 0;  // shared keys summed over the prefix groups
+    int prefix_sharing = 1;   // 0 off, 1 where the cost estimate favours it, 2 always
+    std::vector<int32_t> w_seq, w_tok0, w_ntok, w_kend, tok_row, tok_pos;
+    std::vector<int32_t> w_rows;   // rows of chunk items (appended separately)
+    std::vector<int32_t> u_kb0;    // per unit: first block read (after a shared prefix)
+    std::vector<int32_t> seq_kb0;  // scratch: per sequence
+    DevBuf lse;                    // [rows][H] when shared-prefix items exist
+    Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows 8 w_seq
+                    // 9 w_tok0 10 w_rows 11 w_ntok 12 w_kend 13 tok_row 14 tok_pos 15 u_kb0
     DevBuf ws;
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
@@ -248,7 +257,7 @@ bool encode_chunk_maps(pk_pool* P, std::string* why) {
     const cuuint64_t slots = static_cast<cuuint64_t>(P->n_layers) * P->num_blocks * P->block_size;
     cuuint64_t dims[4] = {64, slots, static_cast<cuuint64_t>(P->kvh), static_cast<cuuint64_t>(P->d / 64)};
     cuuint64_t strides[3] = {static_cast<cuuint64_t>(P->kvh) * P->d * 2, static_cast<cuuint64_t>(P->d) * 2, 128};
-    // K: one 64-dim chunk of one block per box; V: both chunks of one block per box
+    // one 64-dim chunk of one block per box, for K and V alike
     const cuuint32_t box_k[4] = {64, static_cast<cuuint32_t>(P->block_size), 1, 1};
     const cuuint32_t box_v[4] = {64, static_cast<cuuint32_t>(P->block_size), 1, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -346,8 +355,18 @@ void setup_tc(pk_pool* P) {
 
 int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
-// Fewest K/V blocks a split-KV CTA is given when there are fewer than 148 such shares.
+// Split-KV CTA count: one per SM at most; at least kMinBlocksPerCta blocks each, unless
+// the step has many short units (each unit costs a query load, a fill of the pipeline and
+// a store on top of its blocks), which are then spread kUnitsPerCta per CTA; never more
+// CTAs than blocks.
 constexpr int64_t kMinBlocksPerCta = 16;
+constexpr int64_t kUnitsPerCta = 3;
+
+int64_t split_kv_ctas(int64_t T, int64_t nu, int64_t max_ctas) {
+    if (T <= 0) return 0;
+    const int64_t want = std::max(T / kMinBlocksPerCta, (nu + kUnitsPerCta - 1) / kUnitsPerCta);
+    return std::max<int64_t>(1, std::min({max_ctas, T, want}));
+}
 
 // Sequences with at least this many new query rows (tokens x heads per KV head) go to the
 // wide-tile tensor-core kernel; fewer rows stay on the split-KV kernel's units.
@@ -361,6 +380,81 @@ int cta_of_block(int64_t j, int64_t T, int64_t n) {
     while (c + 1 < n && cta_lo(c + 1, T, n) <= j) ++c;
     while (c > 0 && cta_lo(c, T, n) > j) --c;
     return static_cast<int>(c);
+}
+
+// Shared prefixes (cascade attention). Sequences whose block tables begin with the same
+// block ids - forks and prefix-cache hits in pagellm (cache/paged.py:187-203, :257-263) -
+// hold bit-identical K/V there. For a group of them, the wide-tile kernel attends every
+// group token to the shared keys once per 128 rows, and the split-KV units start after the
+// prefix; the two partials are merged per row. A group is the sequences with the same first
+// block id; its prefix is the common run of ids, cut to whole blocks before every member's
+// first new token (so no key of it is written this step and every query sees all of it).
+// In mode 1 it is taken only where a cost estimate says reading the prefix once per
+// sequence (the split-KV path) would take longer than the wide-tile CTAs over it.
+constexpr int64_t kPrefixMinKeys = 64;
+constexpr double kWideUsPerKeyTile = 0.8;     // one 128-row x 64-key tile on one SM
+constexpr double kSplitKvBytesPerUs = 6.0e6;  // split-KV streaming rate (HBM / L2)
+
+void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>& tc_seqs) {
+    pk_pool* P = B->pool;
+    std::vector<std::pair<int32_t, int>> keyed;
+    for (int i : tc_seqs)
+        if (B->indptr[i + 1] > B->indptr[i]) keyed.emplace_back(B->ids[B->indptr[i]], i);
+    std::stable_sort(keyed.begin(), keyed.end(),
+                     [](const std::pair<int32_t, int>& a, const std::pair<int32_t, int>& b) { return a.first < b.first; });
+    const double blk_bytes = static_cast<double>(P->block_bytes()) * 2.0;  // K + V, all heads
+    for (size_t a = 0; a < keyed.size();) {
+        size_t b = a + 1;
+        while (b < keyed.size() && keyed[b].first == keyed[a].first) ++b;
+        if (b - a >= 2) {
+            const int ref = keyed[a].second;
+            const int32_t* rt = B->ids.data() + B->indptr[ref];
+            int64_t pb = std::min<int64_t>(B->indptr[ref + 1] - B->indptr[ref], B->starts[ref] / P->block_size);
+            int64_t toks = 0, units = 0;
+            for (size_t x = a; x < b && pb > 0; ++x) {
+                const int s = keyed[x].second;
+                const int32_t* stb = B->ids.data() + B->indptr[s];
+                const int64_t lim = std::min<int64_t>({pb, B->indptr[s + 1] - B->indptr[s],
+                                                       B->starts[s] / P->block_size});
+                int64_t k = 0;
+                while (k < lim && stb[k] == rt[k]) ++k;
+                pb = k;
+                toks += B->nnew[s];
+                units += ceil_div(B->nnew[s], qmax);
+            }
+            const int64_t keys = pb * P->block_size;
+            if (keys >= kPrefixMinKeys) {
+                const int64_t tiles = ceil_div(toks, tpt);
+                const double waves = static_cast<double>(ceil_div(tiles * P->kvh, std::max(1, P->num_sms)));
+                const double est_wide = waves * static_cast<double>(ceil_div(keys, 64)) * kWideUsPerKeyTile;
+                const double est_split = static_cast<double>(units) * pb * blk_bytes / kSplitKvBytesPerUs;
+                if (B->prefix_sharing == 2 || est_wide < est_split) {
+                    // the group's tokens, member by member, cut into items of tpt tokens
+                    int fill = 0;
+                    auto close_item = [&]() {
+                        B->w_seq.push_back(ref);
+                        B->w_tok0.push_back(static_cast<int32_t>(B->tok_row.size()) - fill);
+                        B->w_ntok.push_back(fill);
+                        B->w_kend.push_back(static_cast<int32_t>(keys));
+                        fill = 0;
+                    };
+                    for (size_t x = a; x < b; ++x) {
+                        const int s = keyed[x].second;
+                        B->seq_kb0[s] = static_cast<int32_t>(pb);
+                        for (int t = 0; t < B->nnew[s]; ++t) {
+                            B->tok_row.push_back(B->offsets[s] + t);
+                            B->tok_pos.push_back(B->starts[s] + t);
+                            if (++fill == tpt) close_item();
+                        }
+                    }
+                    if (fill > 0) close_item();
+                    B->nprefix_groups++;
+                    B->prefix_keys += keys;
+                }
+            }
+        }
+        a = b;
+    }
 }
 
 int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
@@ -377,21 +471,29 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         qmax = std::max(1, pk::kMaxCols / g);
         if (P->d == 256) qmax = g <= 8 ? std::max(1, 8 / g) : 0;  // one n8 tile only at D=256
     }
-    B->w_seq.clear();
-    B->w_t0.clear();
-    B->w_rows.clear();
-    B->nwide = 0;
+    B->w_seq.clear(); B->w_tok0.clear(); B->w_ntok.clear(); B->w_kend.clear();
+    B->tok_row.clear(); B->tok_pos.clear(); B->w_rows.clear(); B->u_kb0.clear();
+    B->nwide = B->nprefix = B->nprefix_groups = 0;
+    B->prefix_keys = 0;
+    B->seq_kb0.assign(B->nseq, 0);
     const bool wide_ok = P->wide_ok && g <= 128 && 128 % g == 0;
-    int64_t T = 0;
+    const int tpt = wide_ok ? 128 / g : 0;  // query tokens per wide item
+    std::vector<int> tc_seqs;
     for (int i = 0; i < B->nseq; ++i) {
         const int n = B->nnew[i];
         if (n <= 0) continue;
         if (wide_ok && static_cast<int64_t>(n) * g >= kWideMinRows) {
-            // 128 query rows (128/g tokens) per work item, longest contexts first below
-            const int tpt = 128 / g;
+            // chunk items: 128 query rows (128/g consecutive tokens) each
             for (int t0 = 0; t0 < n; t0 += tpt) {
+                const int nt = std::min(tpt, n - t0);
+                for (int t = t0; t < t0 + nt; ++t) {
+                    B->tok_row.push_back(B->offsets[i] + t);
+                    B->tok_pos.push_back(B->starts[i] + t);
+                }
                 B->w_seq.push_back(i);
-                B->w_t0.push_back(t0);
+                B->w_tok0.push_back(static_cast<int32_t>(B->tok_row.size()) - nt);
+                B->w_ntok.push_back(nt);
+                B->w_kend.push_back(B->starts[i] + t0 + nt);
             }
             for (int r = 0; r < n; ++r) B->w_rows.push_back(B->offsets[i] + r);
             continue;
@@ -400,43 +502,56 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
             for (int r = 0; r < n; ++r) B->gen_rows.push_back(B->offsets[i] + r);
             continue;
         }
+        tc_seqs.push_back(i);
+    }
+    B->nwide = static_cast<int>(B->w_seq.size());
+    if (wide_ok && B->prefix_sharing != 0 && tc_seqs.size() >= 2) plan_shared_prefixes(B, qmax, tpt, tc_seqs);
+    B->nprefix = static_cast<int>(B->w_seq.size()) - B->nwide;
+    int64_t T = 0;
+    for (int i : tc_seqs) {
+        const int n = B->nnew[i];
+        const int kb0 = B->seq_kb0[i];
         for (int t0 = 0; t0 < n; t0 += qmax) {
             const int nu = std::min(qmax, n - t0);
             const int64_t ctx = static_cast<int64_t>(B->starts[i]) + t0 + nu;
-            T += ceil_div(ctx, P->block_size);
+            T += ceil_div(ctx, P->block_size) - kb0;
             B->u_seq.push_back(i);
             B->u_t0.push_back(t0);
             B->u_n.push_back(nu);
             B->u_blk.push_back(static_cast<int32_t>(T));
+            B->u_kb0.push_back(kb0);
             B->nt = std::max(B->nt, ceil_div(static_cast<int64_t>(nu) * g, 8));
         }
     }
     if (T >= (int64_t(1) << 31)) return fail(PK_ERR_UNSUPPORTED, "step reads 2^31 blocks or more");
-    // wide items with the most keys first, so the longest CTAs start in the first wave
-    {
-        std::vector<int> order(B->w_seq.size());
-        for (size_t x = 0; x < order.size(); ++x) order[x] = static_cast<int>(x);
-        std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
-            return B->starts[B->w_seq[a]] + B->w_t0[a] > B->starts[B->w_seq[b]] + B->w_t0[b];
-        });
-        std::vector<int32_t> ws(order.size()), wt(order.size());
+    // within each kind, the items with the most keys first, so the longest CTAs start in
+    // the first wave
+    auto sort_items = [&](int a0, int a1) {
+        std::vector<int> order;
+        for (int x = a0; x < a1; ++x) order.push_back(x);
+        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return B->w_kend[a] > B->w_kend[b]; });
+        std::vector<int32_t> ws(order.size()), w0(order.size()), wn(order.size()), wk(order.size());
         for (size_t x = 0; x < order.size(); ++x) {
             ws[x] = B->w_seq[order[x]];
-            wt[x] = B->w_t0[order[x]];
+            w0[x] = B->w_tok0[order[x]];
+            wn[x] = B->w_ntok[order[x]];
+            wk[x] = B->w_kend[order[x]];
         }
-        B->w_seq.swap(ws);
-        B->w_t0.swap(wt);
-        B->nwide = static_cast<int>(B->w_seq.size());
-    }
+        std::copy(ws.begin(), ws.end(), B->w_seq.begin() + a0);
+        std::copy(w0.begin(), w0.end(), B->w_tok0.begin() + a0);
+        std::copy(wn.begin(), wn.end(), B->w_ntok.begin() + a0);
+        std::copy(wk.begin(), wk.end(), B->w_kend.begin() + a0);
+    };
+    sort_items(0, B->nwide);
+    sort_items(B->nwide, B->nwide + B->nprefix);
     B->nu = static_cast<int>(B->u_seq.size());
     B->ngeneric = static_cast<int>(B->gen_rows.size());
     if (B->nu > 0) {
         B->use_tc = true;
         B->total_blocks = static_cast<int>(T);
-        // One CTA per SM, but at least kMinBlocksPerCta blocks each: on small steps more
-        // CTAs would cut every unit into many partials whose merge outweighs the bandwidth
-        // the extra SMs add.
-        B->ncta = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(P->num_sms, T / kMinBlocksPerCta)));
+        // On small steps more CTAs would cut every unit into many partials whose merge
+        // outweighs the bandwidth the extra SMs add.
+        B->ncta = static_cast<int>(split_kv_ctas(T, B->nu, P->num_sms));
         for (int u = 0; u < B->nu; ++u) {
             const int c0 = cta_of_block(B->u_blk[u], T, B->ncta);
             const int c1 = cta_of_block(B->u_blk[u + 1] - 1, T, B->ncta);
@@ -465,8 +580,14 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan.add(B->sp_c1.data(), B->sp_c1.size() * 4);
     B->plan.add(B->gen_rows.data(), B->gen_rows.size() * 4);
     B->plan.add(B->w_seq.data(), B->w_seq.size() * 4);
-    B->plan.add(B->w_t0.data(), B->w_t0.size() * 4);
+    B->plan.add(B->w_tok0.data(), B->w_tok0.size() * 4);
     B->plan.add(B->w_rows.data(), B->w_rows.size() * 4);
+    B->plan.add(B->w_ntok.data(), B->w_ntok.size() * 4);
+    B->plan.add(B->w_kend.data(), B->w_kend.size() * 4);
+    B->plan.add(B->tok_row.data(), B->tok_row.size() * 4);
+    B->plan.add(B->tok_pos.data(), B->tok_pos.size() * 4);
+    B->plan.add(B->u_kb0.data(), B->u_kb0.size() * 4);
+    if (B->nprefix > 0) PK_CUDA(B->lse.reserve(static_cast<size_t>(B->nrows) * H * sizeof(float)));
     int rc = B->plan.commit(st);
     if (rc != PK_OK) return rc;
     B->plan_H = H;
@@ -509,6 +630,33 @@ int check_heads(const pk_batch* B, int H) {
     return PK_OK;
 }
 
+// Wide-tile launch parameters for items [first, first + n) of the plan.
+pk::WideParams wide_params(pk_batch* B, int layer, int H, const float* q, float* out, int first, int n,
+                           const float* lse) {
+    pk_pool* P = B->pool;
+    pk::WideParams w{};
+    w.q = q;
+    w.out = out;
+    w.err = static_cast<int*>(B->err.ptr);
+    w.indptr = B->meta.at<int32_t>(0);
+    w.ids = B->meta.at<int32_t>(1);
+    w.w_seq = B->plan.at<int32_t>(8) + first;
+    w.w_tok0 = B->plan.at<int32_t>(9) + first;
+    w.w_ntok = B->plan.at<int32_t>(11) + first;
+    w.w_kend = B->plan.at<int32_t>(12) + first;
+    w.tok_row = B->plan.at<int32_t>(13);
+    w.tok_pos = B->plan.at<int32_t>(14);
+    w.lse = lse;
+    w.nitems = n;
+    w.H = H;
+    w.kvh = P->kvh;
+    w.g = H / P->kvh;
+    w.bs = P->block_size;
+    w.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
+    w.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
+    return w;
+}
+
 int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaStream_t st,
                 const float* k_new = nullptr, const float* v_new = nullptr) {
     // k_new set: fused append - the split-KV kernel appends its units' rows, and the rows
@@ -539,23 +687,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
             PK_CUDA(prof_end(B, kProfAppend, ws));
             B->launches++;
         }
-        pk::WideParams w{};
-        w.q = q;
-        w.out = out;
-        w.err = static_cast<int*>(B->err.ptr);
-        w.indptr = B->meta.at<int32_t>(0);
-        w.ids = B->meta.at<int32_t>(1);
-        w.starts = B->meta.at<int32_t>(2);
-        w.offsets = B->meta.at<int32_t>(3);
-        w.w_seq = B->plan.at<int32_t>(8);
-        w.w_t0 = B->plan.at<int32_t>(9);
-        w.nitems = B->nwide;
-        w.H = H;
-        w.kvh = P->kvh;
-        w.g = g;
-        w.bs = P->block_size;
-        w.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
-        w.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
+        const pk::WideParams w = wide_params(B, layer, H, q, out, 0, B->nwide, nullptr);
         PK_CUDA(prof_begin(B, ws));
         PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, ws));
         PK_CUDA(prof_end(B, kProfWide, ws));
@@ -576,6 +708,8 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.u_t0 = B->plan.at<int32_t>(1);
         p.u_n = B->plan.at<int32_t>(2);
         p.u_blk = B->plan.at<int32_t>(3);
+        p.u_kb0 = B->nprefix > 0 ? B->plan.at<int32_t>(15) : nullptr;
+        p.lse = B->nprefix > 0 ? static_cast<float*>(B->lse.ptr) : nullptr;
         p.nu = B->nu;
         p.total_blocks = B->total_blocks;
         p.ncta = B->ncta;
@@ -617,6 +751,15 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
             PK_CUDA(prof_end(B, kProfMerge, st));
             B->launches++;
         }
+    }
+    if (B->nprefix > 0) {
+        // shared-prefix items: after the split-KV kernel has written the rows they merge into
+        const pk::WideParams w = wide_params(B, layer, H, q, out, B->nwide, B->nprefix,
+                                             static_cast<const float*>(B->lse.ptr));
+        PK_CUDA(prof_begin(B, st));
+        PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, st));
+        PK_CUDA(prof_end(B, kProfWide, st));
+        B->launches++;
     }
     if (ws != st) {
         PK_CUDA(cudaEventRecord(B->ev_join, ws));
@@ -1095,6 +1238,24 @@ int pk_batch_stats(const pk_batch* B, int64_t* s) {
     return PK_OK;
 }
 
+int pk_batch_set_prefix_sharing(pk_batch* B, int mode) {
+    if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
+    if (mode < 0 || mode > 2) return fail(PK_ERR_INVALID_ARG, "prefix sharing mode %d not in 0..2", mode);
+    if (B->prefix_sharing != mode) {
+        B->prefix_sharing = mode;
+        B->plan_H = -1;
+    }
+    return PK_OK;
+}
+
+int pk_batch_prefix_stats(const pk_batch* B, int64_t* s) {
+    if (!B || !s) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    s[0] = B->nprefix_groups;
+    s[1] = B->nprefix;
+    s[2] = B->prefix_keys;
+    return PK_OK;
+}
+
 int pk_batch_profile(pk_batch* B, int enable) {
     if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
     B->profiling = enable != 0;
@@ -1150,7 +1311,7 @@ int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,
         if (unit_blocks[i] <= 0) return fail(PK_ERR_INVALID_ARG, "unit %lld has no blocks", (long long)i);
         T += unit_blocks[i];
     }
-    const int64_t n = T == 0 ? 0 : std::max<int64_t>(1, std::min<int64_t>(max_ctas, T / kMinBlocksPerCta));
+    const int64_t n = split_kv_ctas(T, n_units, max_ctas);
     *ncta = static_cast<int>(n);
     if (cta_first_block)
         for (int64_t c = 0; c <= n; ++c) cta_first_block[c] = n ? cta_lo(c, T, n) : 0;

@@ -8,7 +8,8 @@
 //
 // Work split. Every sequence's query rows are cut into "units" of at most 16/g query
 // tokens (g = query heads per KV head), so one unit's (token, head) columns fit one or two
-// n8 MMA tiles. A unit reads the blocks that hold positions 0..unit_ctx-1. All units'
+// n8 MMA tiles. A unit reads the blocks that hold positions 0..unit_ctx-1 (from block
+// u_kb0 on when a shared prefix is attended by the wide-tile kernel instead). All units'
 // blocks are laid end to end and the total is cut into `ncta` equal ranges: CTA c owns
 // blocks [c*T/ncta, (c+1)*T/ncta). A unit that falls inside one CTA is finished there;
 // a unit cut by CTA boundaries leaves one partial (max, sum, un-normalised output) per
@@ -57,10 +58,12 @@ __device__ __forceinline__ int cta_of_block(int j, int T, int n) {
 
 // Normalised output of the columns a lane holds (C-fragment layout of O^T: dims
 // mt*16 + grp (+8), columns nt*8 + 2*quad + e) for the live query tokens of a unit.
+// With `lse` set, also the row's log2-domain log-sum-exp m + log2(l) ([rows][H]).
 template <int D, int NT>
 __device__ __forceinline__ void store_rows(float* out, const float (&acc)[D / 16][NT][4],
-                                           const float (&l)[NT][2], int nq, int g, int H,
-                                           int row0, int h, int quad, int grp) {
+                                           const float (&m)[NT][2], const float (&l)[NT][2],
+                                           float* lse, int nq, int g, int H, int row0, int h,
+                                           int quad, int grp) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -69,7 +72,9 @@ __device__ __forceinline__ void store_rows(float* out, const float (&acc)[D / 16
             const int tq = col / g;
             if (tq >= nq) continue;
             const float inv = 1.f / l[nt][e];
-            float* op = out + (static_cast<size_t>(row0 + tq) * H + h * g + col % g) * D;
+            const size_t orow = static_cast<size_t>(row0 + tq) * H + h * g + col % g;
+            if (lse != nullptr && grp == 0) lse[orow] = m[nt][e] + log2f(l[nt][e]);
+            float* op = out + orow * D;
 #pragma unroll
             for (int mt = 0; mt < D / 16; ++mt) {
                 op[mt * 16 + grp] = acc[mt][nt][e] * inv;
@@ -135,7 +140,8 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             for (int j = lo, u = u_first; j < hi && ok; ++u) {
                 const int uend = min(hi, p.u_blk[u + 1]);
                 const int seq = p.u_seq[u];
-                const int tbase = p.indptr[seq] - p.u_blk[u];
+                const int kb0 = p.u_kb0 != nullptr ? p.u_kb0[u] : 0;
+                const int tbase = p.indptr[seq] + kb0 - p.u_blk[u];
                 for (; j < uend; ++j, ++it) {
                     const int s = it % p.stages;
                     const uint32_t k = static_cast<uint32_t>(it / p.stages);
@@ -183,7 +189,8 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
         const int t0 = p.u_t0[u];
         const int nq = p.u_n[u];
         const int qpos0 = p.starts[seq] + t0;  // absolute position of the unit's first query
-        const int uctx = qpos0 + nq;           // keys 0..uctx-1 are read
+        const int uctx = qpos0 + nq;           // keys kb0*bs..uctx-1 are read
+        const int kb0 = p.u_kb0 != nullptr ? p.u_kb0[u] : 0;
         const int row0 = p.offsets[seq] + t0;
 
         // Q^T as the B operand: column n = lane/4 of each n8 tile, dims 2*quad(+1), +8.
@@ -243,7 +250,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             }
             const uint32_t kst = smem_u32(smem + s * 2 * tile_bytes);
             const uint32_t vst = kst + tile_bytes;
-            const int kpos0 = (j - ublk0) * p.bs;
+            const int kpos0 = (j - ublk0 + kb0) * p.bs;
             const int nvalid = min(p.bs, uctx - kpos0);
             if (nvalid < p.bs) {
                 // Slots past the context may hold anything; zero this head's V rows there so
@@ -272,24 +279,42 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                     patched = true;
                     uint8_t* kgen = smem + s * 2 * tile_bytes;
                     uint8_t* vgen = kgen + tile_bytes;
-                    const int phys = p.ids[p.indptr[seq] + (j - ublk0)];
+                    const int phys = p.ids[p.indptr[seq] + kb0 + (j - ublk0)];
                     const int row_base = p.offsets[seq] - s_start;
-                    for (int pos = lo_pos; pos < hi_pos; ++pos) {
-                        const int t = pos - kpos0;
-                        const size_t src = (static_cast<size_t>(row_base + pos) * p.kvh + h) * D;
-                        const size_t dst = (static_cast<size_t>(phys) * p.bs + t) * p.kvh * D + h * D;
-                        for (int d0 = lane * 4; d0 < D; d0 += 128) {
-                            const float4 kx = *reinterpret_cast<const float4*>(p.k_new + src + d0);
-                            const float4 vx = *reinterpret_cast<const float4*>(p.v_new + src + d0);
-                            const uint2 kb = make_uint2(pack_bf16(kx.x, kx.y), pack_bf16(kx.z, kx.w));
-                            const uint2 vb = make_uint2(pack_bf16(vx.x, vx.y), pack_bf16(vx.z, vx.w));
+                    // (position, 4-dim) items, lane-strided; each batch issues all its loads
+                    // (read-only inputs) before any store, so the rows' latencies overlap.
+                    constexpr int kPerRow = D / 4;
+                    constexpr int kBatch = (NT == 1 && D <= 128) ? 2 : 1;  // register budget
+                    const int items = (hi_pos - lo_pos) * kPerRow;
+                    for (int base = 0; base < items; base += 32 * kBatch) {
+                        float4 kx[kBatch], vx[kBatch];
+#pragma unroll
+                        for (int e = 0; e < kBatch; ++e) {
+                            const int it = base + e * 32 + lane;
+                            if (it < items) {
+                                const size_t src = (static_cast<size_t>(row_base + lo_pos + it / kPerRow) * p.kvh + h) * D +
+                                                   (it % kPerRow) * 4;
+                                kx[e] = __ldg(reinterpret_cast<const float4*>(p.k_new + src));
+                                vx[e] = __ldg(reinterpret_cast<const float4*>(p.v_new + src));
+                            }
+                        }
+#pragma unroll
+                        for (int e = 0; e < kBatch; ++e) {
+                            const int it = base + e * 32 + lane;
+                            if (it >= items) continue;
+                            const int pos = lo_pos + it / kPerRow;
+                            const int d0 = (it % kPerRow) * 4;
+                            const int t = pos - kpos0;
+                            const uint2 kb = make_uint2(pack_bf16(kx[e].x, kx[e].y), pack_bf16(kx[e].z, kx[e].w));
+                            const uint2 vb = make_uint2(pack_bf16(vx[e].x, vx[e].y), pack_bf16(vx[e].z, vx[e].w));
                             const uint32_t off = tile_off(d0 >> 6, h, t, (d0 & 63) >> 3, p.kvh, p.bs, CH,
                                                           p.per_head_layout) + ((d0 & 7) ? 8u : 0u);
                             *reinterpret_cast<uint2*>(kgen + off) = kb;
                             *reinterpret_cast<uint2*>(vgen + off) = vb;
                             if (pos >= qpos0) {
-                                *reinterpret_cast<uint2*>(p.pool_k + dst + d0) = kb;
-                                *reinterpret_cast<uint2*>(p.pool_v + dst + d0) = vb;
+                                const size_t dst = (static_cast<size_t>(phys) * p.bs + t) * p.kvh * D + h * D + d0;
+                                *reinterpret_cast<uint2*>(p.pool_k + dst) = kb;
+                                *reinterpret_cast<uint2*>(p.pool_v + dst) = vb;
                             }
                         }
                     }
@@ -386,7 +411,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             }
         const bool whole = ublk0 >= lo && p.u_blk[u + 1] <= hi;
         if (whole) {
-            store_rows<D, NT>(p.out, acc, l, nq, g, p.H, row0, h, quad, grp);
+            store_rows<D, NT>(p.out, acc, m, l, p.lse, nq, g, p.H, row0, h, quad, grp);
         } else {
             const size_t seg = static_cast<size_t>(u) + c;
             const size_t base = (seg * p.kvh + h) * kMaxCols;
@@ -477,7 +502,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                                 }
                             }
                     }
-                    store_rows<D, NT>(p.out, num, den, nq, g, p.H, row0, h, quad, grp);
+                    store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp);
                 }
             }
         }

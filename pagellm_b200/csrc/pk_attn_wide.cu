@@ -4,14 +4,22 @@
 // Semantics: pagellm cache/paged.py:454-463 -> model/transformer.py:116-146: the query at
 // absolute position p sees keys 0..p of its sequence, keys read through the block table.
 //
-// One CTA per (work item = 128 query rows of one sequence, KV head h). Rows are
-// (token, head-in-group) pairs, row r = t*g + j, so a tile holds 128/g query tokens whose
-// g heads share every K/V tile. Keys stream in tiles of 64 (64/bs blocks).
+// One CTA per (work item, KV head h). A work item is up to 128/g query tokens read through
+// one block table: rows are (token, head-in-group) pairs, row r = t*g + j, so the g heads
+// of a token share every K/V tile. Keys 0..kend-1 stream in tiles of 64 (64/bs blocks).
+// Two kinds of item:
+//   chunk   consecutive tokens of one sequence (a prefill chunk or a wide verify window);
+//           causal by absolute position.
+//   prefix  tokens of several sequences whose block tables begin with the same blocks
+//           (forks / prefix-cache hits); kend = the shared blocks' keys, all before every
+//           token's position. Each such K/V tile is read once for 128 rows instead of once
+//           per sequence; the partial is merged into the row that the split-KV kernel wrote
+//           for the rest of the sequence (cascade attention).
 //
 // Warp roles (192 threads):
-//   warp 0  producer: one lane issues TMA loads (no multicast) of each block's K (one copy
-//           per 64-dim chunk, tile [chunk][key][64]) and V (one copy per block, tile
-//           [block][chunk][token][64]) into a 5-stage ring; mbarrier completion.
+//   warp 0  producer: one lane issues TMA loads (no multicast) of each block's K and V,
+//           one 64-dim chunk per copy (tiles [chunk][key][64]), into a 5-stage ring;
+//           mbarrier completion. (One copy per block for both chunks measured slower.)
 //   warp 1  TMEM owner (alloc/dealloc, 512 columns) and, on one lane, the MMA issuer:
 //           S_j = Q . K_j^T   (M=128, N=64,  K=128, bf16 -> fp32 TMEM, Q as bf16 hi + lo)
 //           O  += P_j . V_j   (M=128, N=128, K=64;  P from TMEM, V MN-major from smem)
@@ -175,13 +183,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
     const int item = blockIdx.x;
     const int h = blockIdx.y;
     const int seq = p.w_seq[item];
-    const int t0 = p.w_t0[item];
+    const int tok0 = p.w_tok0[item];
     const int g = p.g;
-    const int nseq_rows = p.offsets[seq + 1] - p.offsets[seq];
-    const int tok_per_tile = kWRows / g;
-    const int ntok = min(tok_per_tile, nseq_rows - t0);  // live query tokens in this tile
-    const int qpos0 = p.starts[seq] + t0;
-    const int kv_end = qpos0 + ntok;                       // keys 0..kv_end-1
+    const int ntok = p.w_ntok[item];   // live query tokens in this tile
+    const int kv_end = p.w_kend[item];  // keys 0..kv_end-1
     const int ntiles = (kv_end + kWKeys - 1) / kWKeys;
     const int nblk_ctx = (kv_end + p.bs - 1) / p.bs;
     const int32_t* tbl = p.ids + p.indptr[seq];
@@ -212,7 +217,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
         const int r = 32 * (warp & 3) + lane;
         const int t = r / g, j = r % g;
         const bool live = t < ntok;
-        const float* qp = p.q + (static_cast<size_t>(p.offsets[seq] + t0 + (live ? t : 0)) * p.H + h * g + j) * kWD;
+        const float* qp = p.q + (static_cast<size_t>(p.tok_row[tok0 + (live ? t : 0)]) * p.H + h * g + j) * kWD;
         for (int c = 0; c < 2; ++c)
             for (int u = 0; u < 8; ++u) {
                 float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
@@ -260,8 +265,6 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 for (int b = 0; b < per_tile; ++b) {
                     const int bi = min(jt * per_tile + b, nblk_ctx - 1);  // past the end: a valid block, masked
                     const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(tbl[bi]) * p.bs);
-                    // K: [chunk][key][64] (one copy per 64-dim chunk); V: [block][chunk][token][64]
-                    // (one copy per block: both chunks)
                     for (int c = 0; c < 2; ++c) {
                         tma_load_4d(kd + c * (kWKeys * 128) + b * p.bs * 128, &tmk, 0, slot0, h, c, &full[s]);
                         tma_load_4d(vd + c * (kWKeys * 128) + b * p.bs * 128, &tmv, 0, slot0, h, c, &full[s]);
@@ -315,8 +318,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
                     const uint32_t sbase = static_cast<uint32_t>((jp % kWStages) * kStageBytes);
 #pragma unroll
                     for (int kk = 0; kk < kWKeys / 16; ++kk) {
-                        // A = P in TMEM (16 keys = 8 columns per step); B = V MN-major: keys
-                        // 16kk..16kk+15 lie in block (16kk)/bs, chunks bs*128 bytes apart
+                        // A = P in TMEM (16 keys = 8 columns per step); B = V [key][128 dims] MN-major
                         const int key0 = kk * 16;
                         const uint32_t voff = sbase + key0 * 128;
                         const uint64_t bd = vd0 + (voff >> 4);
@@ -346,7 +348,9 @@ __global__ void __launch_bounds__(kWThreads, 1)
         const int r = 32 * q4 + lane;
         const int t = r / g, jh = r % g;
         const bool live = t < ntok;
-        const int qpos = qpos0 + t;
+        const int orow = p.tok_row[tok0 + (live ? t : 0)];
+        // last visible key: the row's own position, and never past the item's key range
+        const int qlim = live ? min(p.tok_pos[tok0 + t], kv_end - 1) : -1;
         const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16);
         float m = -INFINITY, l = 0.f;
         bool ok = true;
@@ -375,10 +379,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
             if (lane == 0) mbar_arrive(&sfree[jt & 1]);
             // mask by absolute position, only on tiles that reach past this row's position
             // (earlier tiles are fully visible; dead rows mask everything)
-            if (!(live && kbase + kWKeys - 1 <= qpos)) {
+            if (kbase + kWKeys - 1 > qlim) {
 #pragma unroll
                 for (int i = 0; i < 64; ++i)
-                    if (!(live && kbase + i <= qpos)) sv[i] = -INFINITY;
+                    if (kbase + i > qlim) sv[i] = -INFINITY;
             }
             // row max and sum as 8 independent chains (the serial chains were the slow part)
             float mx8[8];
@@ -478,18 +482,40 @@ __global__ void __launch_bounds__(kWThreads, 1)
             if (lane == 0) atomicExch(p.err, kErrTimeout);
         } else {
             tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            float* op = p.out + (static_cast<size_t>(p.offsets[seq] + t0 + (live ? t : 0)) * p.H + h * g + jh) * kWD;
+            const size_t oidx = static_cast<size_t>(orow) * p.H + h * g + jh;
+            float* op = p.out + oidx * kWD;
+            // This partial is o / l with log-sum-exp m + log2(l). Shared-prefix pass: the row
+            // already holds the rest of the sequence's keys, normalised, with log-sum-exp
+            // lse_s; the merged row is (o * 2^(m-M) + out * 2^(lse_s-M)) / (l * 2^(m-M) + 2^(lse_s-M)).
+            float wo = l > 0.f ? 1.f / l : 0.f, wr = 0.f;
+            if (p.lse != nullptr && live) {
+                const float ls = p.lse[oidx];
+                const float mm = fmaxf(l > 0.f ? m : -INFINITY, ls);
+                const float a = l > 0.f ? exp2f(m - mm) : 0.f;
+                const float b = exp2f(ls - mm);
+                const float inv = 1.f / (l * a + b);
+                wo = a * inv;
+                wr = b * inv;
+            }
 #pragma unroll 1
             for (int c = 0; c < kWD / 32; ++c) {
                 float o[32];
                 tmem_ld32(trow + kColO + c * 32, o);
                 tmem_wait_ld();
-                if (live)
+                if (live) {
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4*>(op + c * 32 + i) =
-                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                    for (int i = 0; i < 32; i += 4) {
+                        float4 x = make_float4(o[i] * wo, o[i + 1] * wo, o[i + 2] * wo, o[i + 3] * wo);
+                        if (p.lse != nullptr) {
+                            const float4 y = *reinterpret_cast<const float4*>(op + c * 32 + i);
+                            x.x += y.x * wr;
+                            x.y += y.y * wr;
+                            x.z += y.z * wr;
+                            x.w += y.w * wr;
+                        }
+                        *reinterpret_cast<float4*>(op + c * 32 + i) = x;
+                    }
+                }
             }
         }
     }

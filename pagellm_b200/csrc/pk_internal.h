@@ -31,6 +31,12 @@ struct TcParams {
     const int32_t* u_t0;    // [nu] first query token of the unit within its sequence
     const int32_t* u_n;     // [nu] query tokens in the unit
     const int32_t* u_blk;   // [nu+1] prefix sum of the units' block counts
+    // [nu] first block of the sequence the unit reads (blocks before it - a prefix shared
+    // with other sequences - are attended by the wide-tile kernel); NULL = all 0.
+    const int32_t* u_kb0;
+    // [rows][H] log2-domain log-sum-exp of each output row (max + log2(sum)); NULL = not
+    // written. The shared-prefix pass merges its partial with the row through it.
+    float* lse;
     int nu;
     int total_blocks;
     int ncta;
@@ -98,10 +104,15 @@ struct WideParams {
     int* err;
     const int32_t* indptr;
     const int32_t* ids;
-    const int32_t* starts;
-    const int32_t* offsets;
-    const int32_t* w_seq;  // [nitems] sequence of each work item
-    const int32_t* w_t0;   // [nitems] first query token of the item within its sequence
+    const int32_t* w_seq;   // [nitems] sequence whose block table the item reads
+    const int32_t* w_tok0;  // [nitems] first entry of the item's query tokens in tok_row/tok_pos
+    const int32_t* w_ntok;  // [nitems] query tokens in the item (<= 128/g)
+    const int32_t* w_kend;  // [nitems] keys 0..kend-1 of the table are attended
+    const int32_t* tok_row; // query/output row of each token
+    const int32_t* tok_pos; // absolute position of each token (causal limit)
+    // Shared-prefix pass: NULL = write the normalised output; else merge this partial with
+    // the output row already written (and its log2-domain log-sum-exp [rows][H] here).
+    const float* lse;
     int nitems;
     int H;
     int kvh;

@@ -44,21 +44,24 @@ def test_pool_create_rejects_bad_arguments_before_touching_cuda():
 
 
 @pytest.mark.parametrize("blocks,ctas", [([3, 1, 7, 2], 148), ([100] * 64, 148), ([144, 230, 31], 5),
-                                         ([1], 148), (list(range(1, 300)), 148)])
+                                         ([1], 148), (list(range(1, 300)), 148), ([2, 1] * 256, 148)])
 def test_split_kv_partition_is_balanced_and_complete(blocks, ctas):
     """CTA c owns blocks [c*T/n, (c+1)*T/n): every block once, sizes differ by at most 1,
-    n = max(1, min(max_ctas, T // 16)) so no CTA is empty or tiny."""
+    n = max(1, min(max_ctas, T, max(T // 16, ceil(units / 3)))) so no CTA is empty, and a
+    CTA gets 16 blocks or more unless the units are many and short."""
     lib = _lib.load()
     b = np.asarray(blocks, dtype=np.int64)
     T = int(b.sum())
-    n = max(1, min(ctas, T // 16))
+    n = max(1, min(ctas, T, max(T // 16, -(-len(b) // 3))))
     first = np.zeros(n + 1, dtype=np.int64)
     got = C.c_int()
     assert lib.pk_plan_partition(b.ctypes.data_as(C.POINTER(C.c_int64)), len(b), ctas,
                                  first.ctypes.data_as(C.POINTER(C.c_int64)), C.byref(got)) == 0
     assert got.value == n and first[0] == 0 and first[-1] == T
     sizes = np.diff(first)
-    assert sizes.min() >= min(T, 16) and sizes.max() - sizes.min() <= 1
+    assert sizes.min() == T // n and sizes.max() - sizes.min() <= 1
+    if T // 16 >= -(-len(b) // 3):  # block-driven count
+        assert sizes.min() >= min(T, 16)
 
 
 def test_partition_rejects_empty_units():

@@ -426,6 +426,99 @@ def test_wide_tile_chunks_match_oracle(H, KVH, bs):
                           po.bf16_bits(k.cpu().numpy()).reshape(k.shape))
 
 
+@pytest.mark.parametrize("mode", ["auto", "always", "off"])
+def test_shared_prefix_forks_match_oracle(mode):
+    """C4's shape at 4 requests: 16 forks over one ref-counted 2048-token prefix, CoW'd
+    partial blocks, 5 verify tokens each. With prefix sharing the shared blocks are
+    attended once per 128 rows (tcgen05 kernel) and merged with the split-KV result for the
+    rest of each fork; every mode matches the oracle."""
+    torch = torch_cuda()
+    from pagellm_b200 import workloads
+    from pagellm_b200.cache import PagedBatch
+
+    w = workloads.c4(2, requests=4)
+    pool = make_pool(w, 0)
+    pool.copy_blocks(w.cow_pairs)
+    b = PagedBatch(pool, w.tables, w.starts, w.n_new)
+    b.prefix_sharing = mode
+    assert b.prefix_sharing == mode
+    q, k, v = dev_inputs(w, 1)
+    out = b.write_and_attend(0, q, k, v)
+    b.check()
+    ps = b.prefix_stats()
+    if mode == "off":
+        assert ps == {"groups": 0, "items": 0, "shared_keys": 0}
+    else:
+        # 16 forks x 5 tokens x g=4 rows = 320 rows -> 3 items of 128 rows
+        assert ps == {"groups": 1, "items": 3, "shared_keys": 2048}, ps
+    got, qh = out.cpu().numpy(), q.cpu().numpy()
+    for i, (rows, ref) in oracle_rows(pool, w, range(w.nseq), qh).items():
+        _close(got[rows], ref, True)
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("H,KVH,bs", [(32, 8, 16), (64, 8, 16), (16, 4, 32)])
+def test_shared_prefix_groups_mixed_step(H, KVH, bs):
+    """Several prefix groups in one step beside unshared decode rows and a prefill chunk:
+    prefixes off block boundaries, one member whose first new token lies inside the shared
+    blocks (so the group's prefix is cut there, and its append writes a block the others
+    read), members with 1..7 new tokens; compared with the oracle and with sharing off."""
+    torch = torch_cuda()
+    from pagellm_b200.cache import PagedBatch, PagedKVPool
+
+    rng = np.random.default_rng(H * 7 + bs)
+    # (shared prefix tokens, [(start, n_new), ...]); solo sequences have prefix 0
+    spec = [(700, [(705, 1), (709, 5), (700 + bs, 3), (701, 1), (760, 7)]),
+            (4 * bs, [(4 * bs + 3, 2), (4 * bs, 4)]),
+            (300, [(320, 1), (330, 1), (100, 2)]),
+            (0, [(499, 1)]), (0, [(1000, 200)]), (0, [(37, 3)])]
+    tables, starts, n_new, need = [], [], [], 0
+    for pre, mem in spec:
+        need += pre // bs + sum(-(-(st + n) // bs) for st, n in mem)
+    nb = need + 16
+    perm = iter(rng.permutation(nb).tolist())
+    for pre, mem in spec:
+        shared = [next(perm) for _ in range(pre // bs)]
+        for st, n in mem:
+            own = -(-(st + n) // bs) - len(shared)
+            tables.append(shared + [next(perm) for _ in range(max(own, 0))])
+            starts.append(st)
+            n_new.append(n)
+    pool = PagedKVPool(Shape(1, KVH, 128), nb, bs, "bfloat16")
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    pool.k.copy_(torch.randn(pool.k.shape, generator=gen, device="cuda").to(pool.k.dtype))
+    pool.v.copy_(torch.randn(pool.v.shape, generator=gen, device="cuda").to(pool.v.dtype))
+    k0, v0 = pool.k.clone(), pool.v.clone()
+    rows = sum(n_new)
+    q = torch.randn((rows, H, 128), generator=gen, device="cuda")
+    k = torch.randn((rows, KVH, 128), generator=gen, device="cuda")
+    v = torch.randn((rows, KVH, 128), generator=gen, device="cuda")
+    outs = {}
+    for mode in ("always", "off"):
+        pool.k.copy_(k0)
+        pool.v.copy_(v0)
+        b = PagedBatch(pool, tables, starts, n_new)
+        b.prefix_sharing = mode
+        outs[mode] = b.write_and_attend(0, q, k, v).cpu().numpy()
+        b.check()
+        ps = b.prefix_stats()
+        if mode == "always":
+            # group 3 is cut to the blocks before its member starting at 100
+            keys = 700 // bs * bs + 4 * bs + 100 // bs * bs
+            assert ps["groups"] == 3 and ps["shared_keys"] == keys, ps
+            assert b.stats()["wide_items"] > 0
+    qh = q.cpu().numpy()
+    meta = po.StepMeta(tables, starts, n_new, bs)
+    for i in range(len(tables)):
+        kc, vc = gather_rows(pool, 0, meta.ctx_slots[i])
+        a, z = meta.offsets[i], meta.offsets[i + 1]
+        ref = po.attention_dense(qh[a:z], kc, vc, starts[i])
+        _close(outs["always"][a:z], ref, True)
+        _close(outs["off"][a:z], ref, True)
+    # both schedules agree far more closely than the bf16 tolerance
+    assert float(np.max(np.abs(outs["always"] - outs["off"]))) < 5e-3
+
+
 def test_bounded_wait_gives_up_and_context_survives():
     """Failure detection without a GPU fault: a wait on a barrier phase that nothing
     completes returns after its limit with an error status the host reads; the context
