@@ -347,9 +347,9 @@ void setup_tc(pk_pool* P) {
     P->tc_smem = pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages);
     P->tc_ok = true;
     P->tc_why.clear();
-    // wide tiles: head_dim 128, 64-key tiles made of whole blocks, the layout-0 view
+    // wide tiles: head_dim 128, 128-key tiles made of whole blocks, the layout-0 view
     std::string why2;
-    P->wide_ok = P->d == 128 && 64 % P->block_size == 0 && P->tc_per_head == 0 &&
+    P->wide_ok = P->d == 128 && pk::kWideKeys % P->block_size == 0 && P->tc_per_head == 0 &&
                  static_cast<size_t>(optin) >= pk::wide_smem_bytes() && encode_chunk_maps(P, &why2);
 }
 

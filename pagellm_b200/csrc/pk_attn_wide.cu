@@ -6,7 +6,7 @@
 //
 // One CTA per (work item, KV head h). A work item is up to 128/g query tokens read through
 // one block table: rows are (token, head-in-group) pairs, row r = t*g + j, so the g heads
-// of a token share every K/V tile. Keys 0..kend-1 stream in tiles of 64 (64/bs blocks).
+// of a token share every K/V tile. Keys 0..kend-1 stream in tiles of 128 (128/bs blocks).
 // Two kinds of item:
 //   chunk   consecutive tokens of one sequence (a prefill chunk or a wide verify window);
 //           causal by absolute position.
@@ -16,19 +16,21 @@
 //           per sequence; the partial is merged into the row that the split-KV kernel wrote
 //           for the rest of the sequence (cascade attention).
 //
-// Warp roles (192 threads):
-//   warp 0  producer: one lane issues TMA loads (no multicast) of each block's K and V,
-//           one 64-dim chunk per copy (tiles [chunk][key][64]), into a 5-stage ring;
-//           mbarrier completion. (One copy per block for both chunks measured slower.)
+// Warp roles (224 threads):
+//   warps 0, 6  producers: one lane each issues TMA loads (no multicast), one copy per
+//           (block, 64-dim chunk), tiles [chunk][key][64]: warp 0 fills a 3-slot K ring
+//           (a slot frees as soon as S_j has completed), warp 6 a 2-slot V ring (freed by
+//           P_j.V_j); mbarrier completion. Separate rings keep K loads two tiles ahead.
 //   warp 1  TMEM owner (alloc/dealloc, 512 columns) and, on one lane, the MMA issuer:
-//           S_j = Q . K_j^T   (M=128, N=64,  K=128, bf16 -> fp32 TMEM, Q as bf16 hi + lo)
-//           O  += P_j . V_j   (M=128, N=128, K=64;  P from TMEM, V MN-major from smem)
+//           S_j = Q . K_j^T   (M=128, N=128, K=128, bf16 -> fp32 TMEM, Q as bf16 hi + lo)
+//           O  += P_j . V_j   (M=128, N=128, K=128; P from TMEM, V MN-major from smem)
+//           (N=128 key tiles: an MMA instruction costs about as much at N=64 as at N=128)
 //   warps 2-5 softmax warpgroup: thread = row. Loads S_j from TMEM, masks by absolute
 //           position, online max/sum in the exp2 domain (the base moves only when a tile's
 //           max exceeds it by 2^8, and only then is O in TMEM rescaled), writes P_j (bf16)
 //           into TMEM, and finally O / l to global.
-// S is double-buffered in TMEM (columns 0-63, 64-127), O lives in columns 128-255, and P
-// (bf16) is double-buffered in columns 256-319 as the A operand of the P.V MMA.
+// S is double-buffered in TMEM (columns 0-127, 128-255), O lives in columns 256-383, and P
+// (bf16) is double-buffered in columns 384-511 as the A operand of the P.V MMA.
 // Every wait is bounded; on a timeout the CTA records the error, unwinds and frees TMEM.
 
 #include "pk_device.cuh"
@@ -39,24 +41,26 @@ namespace pk {
 namespace {
 
 constexpr int kWRows = 128;       // query rows per CTA (UMMA M)
-constexpr int kWKeys = 64;        // keys per tile (UMMA N of S, K of P.V)
+constexpr int kWKeys = kWideKeys;  // keys per tile (UMMA N of S, K of P.V)
 constexpr int kWD = 128;          // head dim
-constexpr int kWStages = 5;
-constexpr int kWThreads = 192;
+constexpr int kKStages = 3;        // K ring: a slot frees when S_j completes
+constexpr int kVStages = 2;        // V ring: a slot frees when P_j.V_j completes
+constexpr int kWThreads = 224;
 constexpr uint32_t kTmemCols = 512;
-// TMEM columns: S double buffer [0,64) [64,128); O [128,256); P double buffer (bf16 pairs)
-// [256,288) [288,320).
-constexpr uint32_t kColO = 128;
-constexpr uint32_t kColP = 256;
+// TMEM columns: S double buffer [0,128) [128,256); O [256,384); P double buffer (bf16
+// pairs) [384,448) [448,512).
+constexpr uint32_t kColO = 2 * kWKeys;
+constexpr uint32_t kColP = kColO + kWD;
+static_assert(kColP + kWKeys <= kTmemCols, "TMEM budget");
 
 // shared memory carve-up (bytes from a 1024-aligned base)
 constexpr int kQBytes = kWRows * kWD * 2;            // 32 KB per Q half (hi, lo): [chunk][row][64]
-constexpr int kKVBytes = kWKeys * kWD * 2;           // 16 KB per K or V tile
-constexpr int kStageBytes = 2 * kKVBytes;
+constexpr int kKVBytes = kWKeys * kWD * 2;           // 32 KB per K or V tile
 constexpr int kOffQhi = 0;
 constexpr int kOffQlo = kOffQhi + kQBytes;
-constexpr int kOffStage = kOffQlo + kQBytes;
-constexpr int kOffBar = kOffStage + kWStages * kStageBytes;
+constexpr int kOffK = kOffQlo + kQBytes;
+constexpr int kOffV = kOffK + kKStages * kKVBytes;
+constexpr int kOffBar = kOffV + kVStages * kKVBytes;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 
 // ---------------------------------------------------------------- tcgen05 wrappers
@@ -98,7 +102,7 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                      smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     uint32_t r[32];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -112,7 +116,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
         "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
@@ -120,6 +124,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]),
         "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]),
         "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -169,9 +183,11 @@ __global__ void __launch_bounds__(kWThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
-    uint64_t* empty = full + kWStages;
-    uint64_t* sfull = empty + kWStages;  // [2]
+    uint64_t* kfull = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* kempty = kfull + kKStages;
+    uint64_t* vfull = kempty + kKStages;
+    uint64_t* vempty = vfull + kVStages;
+    uint64_t* sfull = vempty + kVStages;  // [2]
     uint64_t* sfree = sfull + 2;         // [2]
     uint64_t* pfull = sfree + 2;         // [2] per P buffer
     uint64_t* pvdone = pfull + 2;        // [2] per P buffer
@@ -192,9 +208,13 @@ __global__ void __launch_bounds__(kWThreads, 1)
     const int32_t* tbl = p.ids + p.indptr[seq];
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kWStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+        for (int s = 0; s < kKStages; ++s) {
+            mbar_init(&kfull[s], 1);
+            mbar_init(&kempty[s], 1);
+        }
+        for (int s = 0; s < kVStages; ++s) {
+            mbar_init(&vfull[s], 1);
+            mbar_init(&vempty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&sfull[b], 1);
@@ -213,7 +233,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
     }
 
     // ---- Q tile -> shared memory (softmax warps): scale into the exp2 domain, bf16 hi + lo
-    if (warp >= 2) {
+    if (warp >= 2 && warp < 6) {
         const int r = 32 * (warp & 3) + lane;
         const int t = r / g, j = r % g;
         const bool live = t < ntok;
@@ -245,35 +265,41 @@ __global__ void __launch_bounds__(kWThreads, 1)
     const uint32_t tmem = *tmem_slot;
     const uint32_t smem_base = smem_u32(smem);
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer
+    if (warp == 0 || warp == 6) {
+        // ------------------------------------------------------------ producers
+        // warp 0: K tiles into the K ring; warp 6: V tiles into the V ring. Each tile is one
+        // copy per (block, 64-dim chunk); blocks past the context repeat the last valid one
+        // (masked, and V zeroed there).
         if (lane == 0) {
-            prefetch_tensormap(&tmk);
-            prefetch_tensormap(&tmv);
+            const bool is_k = warp == 0;
+            const CUtensorMap* map = is_k ? &tmk : &tmv;
+            const int nst = is_k ? kKStages : kVStages;
+            uint64_t* fullb = is_k ? kfull : vfull;
+            uint64_t* emptyb = is_k ? kempty : vempty;
+            uint8_t* ring = smem + (is_k ? kOffK : kOffV);
+            prefetch_tensormap(map);
             const int per_tile = kWKeys / p.bs;
             int issued = 0;
             for (int jt = 0; jt < ntiles; ++jt) {
-                const int s = jt % kWStages;
-                if (!mbar_wait_bounded(&empty[s], ((jt / kWStages) & 1u) ^ 1u) || *abort_flag) {
+                const int s = jt % nst;
+                if (!mbar_wait_bounded(&emptyb[s], ((jt / nst) & 1u) ^ 1u) || *abort_flag) {
                     *abort_flag = 1;
                     atomicExch(p.err, kErrTimeout);
                     break;
                 }
-                uint8_t* kd = smem + kOffStage + s * kStageBytes;
-                uint8_t* vd = kd + kKVBytes;
-                mbar_arrive_expect_tx(&full[s], kStageBytes);
+                uint8_t* dst = ring + s * kKVBytes;
+                mbar_arrive_expect_tx(&fullb[s], kKVBytes);
                 for (int b = 0; b < per_tile; ++b) {
-                    const int bi = min(jt * per_tile + b, nblk_ctx - 1);  // past the end: a valid block, masked
+                    const int bi = min(jt * per_tile + b, nblk_ctx - 1);
                     const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(tbl[bi]) * p.bs);
-                    for (int c = 0; c < 2; ++c) {
-                        tma_load_4d(kd + c * (kWKeys * 128) + b * p.bs * 128, &tmk, 0, slot0, h, c, &full[s]);
-                        tma_load_4d(vd + c * (kWKeys * 128) + b * p.bs * 128, &tmv, 0, slot0, h, c, &full[s]);
-                    }
+                    for (int c = 0; c < 2; ++c)
+                        tma_load_4d(dst + c * (kWKeys * 128) + b * p.bs * 128, map, 0, slot0, h, c, &fullb[s]);
                 }
                 ++issued;
             }
-            for (int t = max(0, issued - kWStages); t < issued; ++t)
-                mbar_wait_bounded(&full[t % kWStages], static_cast<uint32_t>(t / kWStages) & 1u);
+            // never leave the CTA with copies still landing in its shared memory
+            for (int t = max(0, issued - nst); t < issued; ++t)
+                mbar_wait_bounded(&fullb[t % nst], static_cast<uint32_t>(t / nst) & 1u);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -289,44 +315,46 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 qd_hi[kk] = smem_desc(smem_base + kOffQhi + qoff, 16, 1024);
                 qd_lo[kk] = smem_desc(smem_base + kOffQlo + qoff, 16, 1024);
             }
-            const uint64_t kd0 = smem_desc(smem_base + kOffStage, 16, 1024);
-            const uint64_t vd0 = smem_desc(smem_base + kOffStage + kKVBytes, kWKeys * 128, 1024);
+            const uint64_t kd0 = smem_desc(smem_base + kOffK, 16, 1024);
+            const uint64_t vd0 = smem_desc(smem_base + kOffV, kWKeys * 128, 1024);
             int js = 0, jp = 0;  // next S tile / next P.V tile to issue
             unsigned long long idle_since = global_ns();
             bool ok = true;
             while (jp < ntiles) {
                 bool progressed = false;
-                if (js < ntiles && mbar_test_wait(&full[js % kWStages], static_cast<uint32_t>(js / kWStages) & 1u) &&
+                if (js < ntiles && mbar_test_wait(&kfull[js % kKStages], static_cast<uint32_t>(js / kKStages) & 1u) &&
                     (js < 2 || mbar_test_wait(&sfree[js & 1], static_cast<uint32_t>((js - 2) / 2) & 1u))) {
                     tc_fence_after();
-                    const uint32_t sbase = static_cast<uint32_t>((js % kWStages) * kStageBytes);
+                    const uint32_t sbase = static_cast<uint32_t>((js % kKStages) * kKVBytes);
                     const uint32_t sd = tmem + (js & 1) * kWKeys;
 #pragma unroll
                     for (int kk = 0; kk < kWD / 16; ++kk) {
-                        // A = Q [128 rows][128 dims] K-major, B = K [64 keys][128 dims] K-major
+                        // A = Q [128 rows][128 dims] K-major, B = K [128 keys][128 dims] K-major
                         const uint32_t koff = sbase + (kk >> 2) * (kWKeys * 128) + (kk & 3) * 32;
                         const uint64_t bd = kd0 + (koff >> 4);
                         umma_bf16(sd, qd_hi[kk], bd, kIdescS, kk > 0 ? 1u : 0u);
                         umma_bf16(sd, qd_lo[kk], bd, kIdescS, 1u);
                     }
                     umma_commit(&sfull[js & 1]);
+                    umma_commit(&kempty[js % kKStages]);
                     ++js;
                     progressed = true;
                 }
-                if (jp < js && mbar_test_wait(&pfull[jp & 1], static_cast<uint32_t>(jp / 2) & 1u)) {
+                if (jp < js && mbar_test_wait(&pfull[jp & 1], static_cast<uint32_t>(jp / 2) & 1u) &&
+                    mbar_test_wait(&vfull[jp % kVStages], static_cast<uint32_t>(jp / kVStages) & 1u)) {
                     tc_fence_after();
-                    const uint32_t sbase = static_cast<uint32_t>((jp % kWStages) * kStageBytes);
+                    const uint32_t sbase = static_cast<uint32_t>((jp % kVStages) * kKVBytes);
 #pragma unroll
                     for (int kk = 0; kk < kWKeys / 16; ++kk) {
                         // A = P in TMEM (16 keys = 8 columns per step); B = V [key][128 dims] MN-major
                         const int key0 = kk * 16;
                         const uint32_t voff = sbase + key0 * 128;
                         const uint64_t bd = vd0 + (voff >> 4);
-                        umma_bf16_ts(tmem + kColO, tmem + kColP + (jp & 1) * 32 + kk * 8, bd, kIdescO,
+                        umma_bf16_ts(tmem + kColO, tmem + kColP + (jp & 1) * (kWKeys / 2) + kk * 8, bd, kIdescO,
                                      (jp > 0 || kk > 0) ? 1u : 0u);
                     }
                     umma_commit(&pvdone[jp & 1]);
-                    umma_commit(&empty[jp % kWStages]);
+                    umma_commit(&vempty[jp % kVStages]);
                     ++jp;
                     progressed = true;
                 }
@@ -362,18 +390,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 break;
             }
             tc_fence_after();
-            float sv[64];
-            {
-                float a[32], b[32];
-                tmem_ld32(trow + (jt & 1) * kWKeys, a);
-                tmem_ld32(trow + (jt & 1) * kWKeys + 32, b);
-                tmem_wait_ld();
+            float sv[kWKeys];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    sv[i] = a[i];
-                    sv[32 + i] = b[i];
-                }
-            }
+            for (int c = 0; c < kWKeys / 32; ++c) tmem_ld32(trow + (jt & 1) * kWKeys + c * 32, sv + c * 32);
+            tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sfree[jt & 1]);
@@ -381,7 +401,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
             // (earlier tiles are fully visible; dead rows mask everything)
             if (kbase + kWKeys - 1 > qlim) {
 #pragma unroll
-                for (int i = 0; i < 64; ++i)
+                for (int i = 0; i < kWKeys; ++i)
                     if (kbase + i > qlim) sv[i] = -INFINITY;
             }
             // row max and sum as 8 independent chains (the serial chains were the slow part)
@@ -390,7 +410,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
             for (int k = 0; k < 8; ++k) {
                 mx8[k] = sv[k];
 #pragma unroll
-                for (int i = k + 8; i < 64; i += 8) mx8[k] = fmaxf(mx8[k], sv[i]);
+                for (int i = k + 8; i < kWKeys; i += 8) mx8[k] = fmaxf(mx8[k], sv[i]);
             }
             const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                    fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
@@ -403,9 +423,9 @@ __global__ void __launch_bounds__(kWThreads, 1)
             float sum8[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) sum8[k] = 0.f;
-            uint32_t pk[32];
+            uint32_t pk[kWKeys / 2];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            for (int i = 0; i < kWKeys / 2; ++i) {
                 const float a = ex2_approx(sv[2 * i] - base), b = ex2_approx(sv[2 * i + 1] - base);
                 sum8[i & 7] += a + b;
                 pk[i] = pack_bf16(a, b);
@@ -444,13 +464,13 @@ __global__ void __launch_bounds__(kWThreads, 1)
             }
             if (jt == ntiles - 1 && kv_end < kbase + kWKeys) {
                 // keys past the context in the last tile: zero their V rows so P = 0 meets 0
-                const int s = jt % kWStages;
-                const bool landed = mbar_wait_bounded(&full[s], static_cast<uint32_t>(jt / kWStages) & 1u);
+                const int s = jt % kVStages;
+                const bool landed = mbar_wait_bounded(&vfull[s], static_cast<uint32_t>(jt / kVStages) & 1u);
                 if (!__all_sync(0xffffffffu, landed)) {
                     ok = false;
                     break;
                 }
-                uint8_t* vd = smem + kOffStage + s * kStageBytes + kKVBytes;
+                uint8_t* vd = smem + kOffV + s * kKVBytes;
                 const int first = kv_end - kbase;
                 const int units = (kWKeys - first) * 2 * 8;
                 for (int x = threadIdx.x - 64; x < units; x += 128) {
@@ -460,13 +480,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 }
             }
             // P row -> TMEM (A operand of P.V), bf16 pairs along the columns
-            {
-                float pf[32];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) pf[i] = __uint_as_float(pk[i]);
-                tmem_st32(trow + kColP + (jt & 1) * 32, pf);
-                tmem_wait_st();
-            }
+            for (int c = 0; c < kWKeys / 64; ++c)
+                tmem_st32u(trow + kColP + (jt & 1) * (kWKeys / 2) + c * 32, pk + c * 32);
+            tmem_wait_st();
             fence_proxy_async_smem();  // the zeroed V rows (generic writes) before the MMA reads them
             tc_fence_before();
             // one arrival per warp (count 4): the MMA starts once all rows of P are written

@@ -12,6 +12,7 @@ namespace pk {
 constexpr int kMaxCols = 16;
 // Largest number of KV heads the tensor-core kernel maps to warps of one CTA.
 constexpr int kTcMaxKvHeads = 8;
+constexpr int kWideKeys = 128;  // keys per tile of the wide-tile kernel (a multiple of block_size)
 
 // Parameters of the split-KV tensor-core attention kernel (bf16 pool).
 // A "unit" is a window of at most kMaxCols / g query tokens of one sequence; every unit
