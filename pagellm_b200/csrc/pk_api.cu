@@ -221,11 +221,15 @@ struct pk_batch {
     int prefix_sharing = 1;   // 0 off, 1 where the cost estimate favours it, 2 always
     std::vector<int32_t> w_seq, w_tok0, w_ntok, w_kend, tok_row, tok_pos;
     std::vector<int32_t> w_rows;   // rows of chunk items (appended separately)
+    std::vector<int32_t> w_pair;   // items of each wide CTA: chunk pairs, then prefix pairs
+    int npair_chunk = 0, npair_prefix = 0;
     std::vector<int32_t> u_kb0;    // per unit: first block read (after a shared prefix)
     std::vector<int32_t> seq_kb0;  // scratch: per sequence
+    int tc_max_new = 0;            // most new tokens of a sequence on the split-KV kernel
     DevBuf lse;                    // [rows][H] when shared-prefix items exist
     Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows 8 w_seq
                     // 9 w_tok0 10 w_rows 11 w_ntok 12 w_kend 13 tok_row 14 tok_pos 15 u_kb0
+                    // 16 w_pair
     DevBuf ws;
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
@@ -361,6 +365,7 @@ int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 // CTAs than blocks.
 constexpr int64_t kMinBlocksPerCta = 16;
 constexpr int64_t kUnitsPerCta = 3;
+constexpr int kFuseMaxNew = 1;  // fuse the append only when split-KV sequences add <= 1 token
 
 int64_t split_kv_ctas(int64_t T, int64_t nu, int64_t max_ctas) {
     if (T <= 0) return 0;
@@ -392,7 +397,7 @@ int cta_of_block(int64_t j, int64_t T, int64_t n) {
 // In mode 1 it is taken only where a cost estimate says reading the prefix once per
 // sequence (the split-KV path) would take longer than the wide-tile CTAs over it.
 constexpr int64_t kPrefixMinKeys = 64;
-constexpr double kWideUsPerKeyTile = 0.8;     // one 128-row x 64-key tile on one SM
+constexpr double kWideUsPerKeyTile = 2.0;     // one CTA (256 rows) over one 128-key tile
 constexpr double kSplitKvBytesPerUs = 6.0e6;  // split-KV streaming rate (HBM / L2)
 
 void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>& tc_seqs) {
@@ -424,9 +429,9 @@ void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>
             }
             const int64_t keys = pb * P->block_size;
             if (keys >= kPrefixMinKeys) {
-                const int64_t tiles = ceil_div(toks, tpt);
-                const double waves = static_cast<double>(ceil_div(tiles * P->kvh, std::max(1, P->num_sms)));
-                const double est_wide = waves * static_cast<double>(ceil_div(keys, 64)) * kWideUsPerKeyTile;
+                const int64_t ctas = ceil_div(ceil_div(toks, tpt), 2) * P->kvh;
+                const double waves = static_cast<double>(ceil_div(ctas, std::max(1, P->num_sms)));
+                const double est_wide = waves * static_cast<double>(ceil_div(keys, pk::kWideKeys)) * kWideUsPerKeyTile;
                 const double est_split = static_cast<double>(units) * pb * blk_bytes / kSplitKvBytesPerUs;
                 if (B->prefix_sharing == 2 || est_wide < est_split) {
                     // the group's tokens, member by member, cut into items of tpt tokens
@@ -505,6 +510,8 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         tc_seqs.push_back(i);
     }
     B->nwide = static_cast<int>(B->w_seq.size());
+    B->tc_max_new = 0;
+    for (int i : tc_seqs) B->tc_max_new = std::max(B->tc_max_new, B->nnew[i]);
     if (wide_ok && B->prefix_sharing != 0 && tc_seqs.size() >= 2) plan_shared_prefixes(B, qmax, tpt, tc_seqs);
     B->nprefix = static_cast<int>(B->w_seq.size()) - B->nwide;
     int64_t T = 0;
@@ -524,26 +531,35 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         }
     }
     if (T >= (int64_t(1) << 31)) return fail(PK_ERR_UNSUPPORTED, "step reads 2^31 blocks or more");
-    // within each kind, the items with the most keys first, so the longest CTAs start in
-    // the first wave
-    auto sort_items = [&](int a0, int a1) {
-        std::vector<int> order;
-        for (int x = a0; x < a1; ++x) order.push_back(x);
-        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return B->w_kend[a] > B->w_kend[b]; });
-        std::vector<int32_t> ws(order.size()), w0(order.size()), wn(order.size()), wk(order.size());
-        for (size_t x = 0; x < order.size(); ++x) {
-            ws[x] = B->w_seq[order[x]];
-            w0[x] = B->w_tok0[order[x]];
-            wn[x] = B->w_ntok[order[x]];
-            wk[x] = B->w_kend[order[x]];
+    // Wide CTAs take two items each: neighbouring items of one sequence (chunk) or of one
+    // prefix group, which read the same block table. Within each kind the pairs with the
+    // most keys go first, so the longest CTAs start in the first wave.
+    B->w_pair.clear();
+    auto make_pairs = [&](int a0, int a1) {
+        std::vector<std::pair<int32_t, int32_t>> pr;
+        for (int x = a0; x < a1;) {
+            if (x + 1 < a1 && B->w_seq[x + 1] == B->w_seq[x]) {
+                pr.emplace_back(x, x + 1);
+                x += 2;
+            } else {
+                pr.emplace_back(x, -1);
+                x += 1;
+            }
         }
-        std::copy(ws.begin(), ws.end(), B->w_seq.begin() + a0);
-        std::copy(w0.begin(), w0.end(), B->w_tok0.begin() + a0);
-        std::copy(wn.begin(), wn.end(), B->w_ntok.begin() + a0);
-        std::copy(wk.begin(), wk.end(), B->w_kend.begin() + a0);
+        auto keys = [&](const std::pair<int32_t, int32_t>& q) {
+            return std::max(B->w_kend[q.first], q.second >= 0 ? B->w_kend[q.second] : 0);
+        };
+        std::stable_sort(pr.begin(), pr.end(), [&](const std::pair<int32_t, int32_t>& x, const std::pair<int32_t, int32_t>& y) {
+            return keys(x) > keys(y);
+        });
+        for (const auto& q : pr) {
+            B->w_pair.push_back(q.first);
+            B->w_pair.push_back(q.second);
+        }
+        return static_cast<int>(pr.size());
     };
-    sort_items(0, B->nwide);
-    sort_items(B->nwide, B->nwide + B->nprefix);
+    B->npair_chunk = make_pairs(0, B->nwide);
+    B->npair_prefix = make_pairs(B->nwide, B->nwide + B->nprefix);
     B->nu = static_cast<int>(B->u_seq.size());
     B->ngeneric = static_cast<int>(B->gen_rows.size());
     if (B->nu > 0) {
@@ -587,6 +603,7 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan.add(B->tok_row.data(), B->tok_row.size() * 4);
     B->plan.add(B->tok_pos.data(), B->tok_pos.size() * 4);
     B->plan.add(B->u_kb0.data(), B->u_kb0.size() * 4);
+    B->plan.add(B->w_pair.data(), B->w_pair.size() * 4);
     if (B->nprefix > 0) PK_CUDA(B->lse.reserve(static_cast<size_t>(B->nrows) * H * sizeof(float)));
     int rc = B->plan.commit(st);
     if (rc != PK_OK) return rc;
@@ -630,7 +647,7 @@ int check_heads(const pk_batch* B, int H) {
     return PK_OK;
 }
 
-// Wide-tile launch parameters for items [first, first + n) of the plan.
+// Wide-tile launch parameters for CTAs (item pairs) [first, first + n) of the plan.
 pk::WideParams wide_params(pk_batch* B, int layer, int H, const float* q, float* out, int first, int n,
                            const float* lse) {
     pk_pool* P = B->pool;
@@ -640,14 +657,15 @@ pk::WideParams wide_params(pk_batch* B, int layer, int H, const float* q, float*
     w.err = static_cast<int*>(B->err.ptr);
     w.indptr = B->meta.at<int32_t>(0);
     w.ids = B->meta.at<int32_t>(1);
-    w.w_seq = B->plan.at<int32_t>(8) + first;
-    w.w_tok0 = B->plan.at<int32_t>(9) + first;
-    w.w_ntok = B->plan.at<int32_t>(11) + first;
-    w.w_kend = B->plan.at<int32_t>(12) + first;
+    w.w_seq = B->plan.at<int32_t>(8);
+    w.w_tok0 = B->plan.at<int32_t>(9);
+    w.w_ntok = B->plan.at<int32_t>(11);
+    w.w_kend = B->plan.at<int32_t>(12);
+    w.w_pair = B->plan.at<int32_t>(16) + 2 * first;
     w.tok_row = B->plan.at<int32_t>(13);
     w.tok_pos = B->plan.at<int32_t>(14);
     w.lse = lse;
-    w.nitems = n;
+    w.npairs = n;
     w.H = H;
     w.kvh = P->kvh;
     w.g = H / P->kvh;
@@ -687,7 +705,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
             PK_CUDA(prof_end(B, kProfAppend, ws));
             B->launches++;
         }
-        const pk::WideParams w = wide_params(B, layer, H, q, out, 0, B->nwide, nullptr);
+        const pk::WideParams w = wide_params(B, layer, H, q, out, 0, B->npair_chunk, nullptr);
         PK_CUDA(prof_begin(B, ws));
         PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, ws));
         PK_CUDA(prof_end(B, kProfWide, ws));
@@ -754,7 +772,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
     }
     if (B->nprefix > 0) {
         // shared-prefix items: after the split-KV kernel has written the rows they merge into
-        const pk::WideParams w = wide_params(B, layer, H, q, out, B->nwide, B->nprefix,
+        const pk::WideParams w = wide_params(B, layer, H, q, out, B->npair_chunk, B->npair_prefix,
                                              static_cast<const float*>(B->lse.ptr));
         PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, st));
@@ -1163,7 +1181,10 @@ int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* 
         rc = build_attention_plan(B, n_heads, st);
         if (rc != PK_OK) return rc;
     }
-    if (B->ngeneric == 0 && B->fuse_append_ok && (B->use_tc || B->nwide > 0))
+    // Fused append (rows patched into the attention kernels' shared memory) pays off for
+    // decode steps; with several new tokens per sequence one scatter kernel first is faster
+    // than each unit fetching its rows on its critical path.
+    if (B->ngeneric == 0 && B->fuse_append_ok && (B->use_tc || B->nwide > 0) && B->tc_max_new <= kFuseMaxNew)
         return attend_impl(B, layer, n_heads, q_dev, out_dev, st, k_dev, v_dev);
     if (B->nrows > 0) {
         const bool listed = !B->app_rows.empty();

@@ -4,33 +4,31 @@
 // Semantics: pagellm cache/paged.py:454-463 -> model/transformer.py:116-146: the query at
 // absolute position p sees keys 0..p of its sequence, keys read through the block table.
 //
-// One CTA per (work item, KV head h). A work item is up to 128/g query tokens read through
-// one block table: rows are (token, head-in-group) pairs, row r = t*g + j, so the g heads
-// of a token share every K/V tile. Keys 0..kend-1 stream in tiles of 128 (128/bs blocks).
-// Two kinds of item:
+// One CTA per (pair of work items, KV head h). A work item is one query tile: up to 128/g
+// query tokens read through one block table; rows are (token, head-in-group) pairs,
+// row r = t*g + j, so the g heads of a token share every K/V tile. The two items of a CTA
+// read the same block table, so every K/V tile brought into shared memory serves 256 query
+// rows (half the L2 -> SM traffic of one tile per CTA, which is what bounded that design).
+// Keys 0..kend-1 stream in tiles of 128 (128/bs blocks). Two kinds of item:
 //   chunk   consecutive tokens of one sequence (a prefill chunk or a wide verify window);
 //           causal by absolute position.
 //   prefix  tokens of several sequences whose block tables begin with the same blocks
 //           (forks / prefix-cache hits); kend = the shared blocks' keys, all before every
-//           token's position. Each such K/V tile is read once for 128 rows instead of once
+//           token's position. Each such K/V tile is read once per 256 rows instead of once
 //           per sequence; the partial is merged into the row that the split-KV kernel wrote
 //           for the rest of the sequence (cascade attention).
 //
-// Warp roles (224 threads):
-//   warps 0, 6  producers: one lane each issues TMA loads (no multicast), one copy per
-//           (block, 64-dim chunk), tiles [chunk][key][64]: warp 0 fills a 3-slot K ring
-//           (a slot frees as soon as S_j has completed), warp 6 a 2-slot V ring (freed by
-//           P_j.V_j); mbarrier completion. Separate rings keep K loads two tiles ahead.
+// Warp roles (320 threads):
+//   warp 0  producer: one lane fills a 3-slot K ring and a 2-slot V ring with TMA loads (no
+//           multicast), one copy per (block, 64-dim chunk); mbarrier completion.
 //   warp 1  TMEM owner (alloc/dealloc, 512 columns) and, on one lane, the MMA issuer:
-//           S_j = Q . K_j^T   (M=128, N=128, K=128, bf16 -> fp32 TMEM, Q as bf16 hi + lo)
-//           O  += P_j . V_j   (M=128, N=128, K=128; P from TMEM, V MN-major from smem)
-//           (N=128 key tiles: an MMA instruction costs about as much at N=64 as at N=128)
-//   warps 2-5 softmax warpgroup: thread = row. Loads S_j from TMEM, masks by absolute
-//           position, online max/sum in the exp2 domain (the base moves only when a tile's
-//           max exceeds it by 2^8, and only then is O in TMEM rescaled), writes P_j (bf16)
-//           into TMEM, and finally O / l to global.
-// S is double-buffered in TMEM (columns 0-127, 128-255), O lives in columns 256-383, and P
-// (bf16) is double-buffered in columns 384-511 as the A operand of the P.V MMA.
+//           S_t = Q_t . K^T  (M=128, N=128, K=128; bf16 -> fp32 in TMEM)
+//           O_t += P_t . V   (M=128, N=128, K=128; P_t from TMEM, V MN-major from smem)
+//   warps 2-5 / 6-9  softmax of query tile 0 / 1: thread = row. Loads S_t from TMEM, masks
+//           by absolute position, online max/sum in the exp2 domain (the base moves only
+//           when a tile's max exceeds it by 2^8, and only then is O_t in TMEM rescaled),
+//           writes P_t (bf16) over S_t's columns, and finally O_t / l to global.
+// Q is rounded to bf16 once (scaled by log2(e)/sqrt(d)); P to bf16; accumulation is fp32.
 // Every wait is bounded; on a timeout the CTA records the error, unwinds and frees TMEM.
 
 #include "pk_device.cuh"
@@ -40,25 +38,23 @@ namespace pk {
 
 namespace {
 
-constexpr int kWRows = 128;       // query rows per CTA (UMMA M)
+constexpr int kWRows = 128;        // query rows per tile (UMMA M); two tiles per CTA
 constexpr int kWKeys = kWideKeys;  // keys per tile (UMMA N of S, K of P.V)
-constexpr int kWD = 128;          // head dim
-constexpr int kKStages = 3;        // K ring: a slot frees when S_j completes
-constexpr int kVStages = 2;        // V ring: a slot frees when P_j.V_j completes
-constexpr int kWThreads = 224;
+constexpr int kWD = 128;           // head dim
+constexpr int kKStages = 3;        // K ring: a slot frees when S of both query tiles completes
+constexpr int kVStages = 2;        // V ring: a slot frees when P.V of both query tiles completes
+constexpr int kWThreads = 320;
 constexpr uint32_t kTmemCols = 512;
-// TMEM columns: S double buffer [0,128) [128,256); O [256,384); P double buffer (bf16
-// pairs) [384,448) [448,512).
+// TMEM columns: S_0 [0,128), S_1 [128,256) (P_t written over the first 64 columns of S_t),
+// O_0 [256,384), O_1 [384,512).
 constexpr uint32_t kColO = 2 * kWKeys;
-constexpr uint32_t kColP = kColO + kWD;
-static_assert(kColP + kWKeys <= kTmemCols, "TMEM budget");
+static_assert(kColO + 2 * kWD <= kTmemCols, "TMEM budget");
 
 // shared memory carve-up (bytes from a 1024-aligned base)
-constexpr int kQBytes = kWRows * kWD * 2;            // 32 KB per Q half (hi, lo): [chunk][row][64]
-constexpr int kKVBytes = kWKeys * kWD * 2;           // 32 KB per K or V tile
-constexpr int kOffQhi = 0;
-constexpr int kOffQlo = kOffQhi + kQBytes;
-constexpr int kOffK = kOffQlo + kQBytes;
+constexpr int kQBytes = kWRows * kWD * 2;   // 32 KB per query tile (bf16): [chunk][row][64]
+constexpr int kKVBytes = kWKeys * kWD * 2;  // 32 KB per K or V tile: [chunk][key][64]
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + 2 * kQBytes;
 constexpr int kOffV = kOffK + kKStages * kKVBytes;
 constexpr int kOffBar = kOffV + kVStages * kKVBytes;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
@@ -187,22 +183,22 @@ __global__ void __launch_bounds__(kWThreads, 1)
     uint64_t* kempty = kfull + kKStages;
     uint64_t* vfull = kempty + kKStages;
     uint64_t* vempty = vfull + kVStages;
-    uint64_t* sfull = vempty + kVStages;  // [2]
-    uint64_t* sfree = sfull + 2;         // [2]
-    uint64_t* pfull = sfree + 2;         // [2] per P buffer
-    uint64_t* pvdone = pfull + 2;        // [2] per P buffer
+    uint64_t* sfull = vempty + kVStages;  // [tile]
+    uint64_t* pfull = sfull + 2;          // [tile], one arrival per softmax warp
+    uint64_t* pvdone = pfull + 2;         // [tile]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pvdone + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int item = blockIdx.x;
     const int h = blockIdx.y;
-    const int seq = p.w_seq[item];
-    const int tok0 = p.w_tok0[item];
     const int g = p.g;
-    const int ntok = p.w_ntok[item];   // live query tokens in this tile
-    const int kv_end = p.w_kend[item];  // keys 0..kv_end-1
+    // the pair of items (query tiles) this CTA owns; both read the same block table
+    int it_of[2] = {p.w_pair[2 * blockIdx.x], p.w_pair[2 * blockIdx.x + 1]};
+    const int seq = p.w_seq[it_of[0]];
+    const int kend0 = p.w_kend[it_of[0]];
+    const int kend1 = it_of[1] >= 0 ? p.w_kend[it_of[1]] : 0;
+    const int kv_end = max(kend0, kend1);  // keys 0..kv_end-1 are streamed
     const int ntiles = (kv_end + kWKeys - 1) / kWKeys;
     const int nblk_ctx = (kv_end + p.bs - 1) / p.bs;
     const int32_t* tbl = p.ids + p.indptr[seq];
@@ -216,13 +212,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
             mbar_init(&vfull[s], 1);
             mbar_init(&vempty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&sfull[b], 1);
-            mbar_init(&sfree[b], 4);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&pfull[b], 4);
-            mbar_init(&pvdone[b], 1);
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(&sfull[t], 1);
+            mbar_init(&pfull[t], 4);
+            mbar_init(&pvdone[t], 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -232,12 +225,21 @@ __global__ void __launch_bounds__(kWThreads, 1)
         tmem_relinquish();
     }
 
-    // ---- Q tile -> shared memory (softmax warps): scale into the exp2 domain, bf16 hi + lo
-    if (warp >= 2 && warp < 6) {
-        const int r = 32 * (warp & 3) + lane;
-        const int t = r / g, j = r % g;
-        const bool live = t < ntok;
-        const float* qp = p.q + (static_cast<size_t>(p.tok_row[tok0 + (live ? t : 0)]) * p.H + h * g + j) * kWD;
+    // softmax warps: tile = which query tile, row = thread's TMEM lane / Q row
+    const int tile = warp >= 6 ? 1 : 0;
+    const int q4 = warp & 3;
+    const int r = 32 * q4 + lane;
+    const int item = it_of[tile];
+    const int ntok = (warp >= 2 && item >= 0) ? p.w_ntok[item] : 0;
+    const int tok0 = item >= 0 ? p.w_tok0[item] : 0;
+    const int kend_t = tile ? kend1 : kend0;
+    const int t_row = r / g, jh = r % g;
+    const bool live = t_row < ntok;
+
+    // ---- Q tiles -> shared memory: scaled into the exp2 domain, bf16, [chunk][row][64] SW128
+    if (warp >= 2) {
+        const float* qp = p.q + (static_cast<size_t>(p.tok_row[tok0 + (live ? t_row : 0)]) * p.H + h * g + jh) * kWD;
+        uint8_t* qs = smem + kOffQ + tile * kQBytes;
         for (int c = 0; c < 2; ++c)
             for (int u = 0; u < 8; ++u) {
                 float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
@@ -245,17 +247,9 @@ __global__ void __launch_bounds__(kWThreads, 1)
                     a = *reinterpret_cast<const float4*>(qp + c * 64 + u * 8);
                     b = *reinterpret_cast<const float4*>(qp + c * 64 + u * 8 + 4);
                 }
-                const float x[8] = {a.x * p.qscale, a.y * p.qscale, a.z * p.qscale, a.w * p.qscale,
-                                    b.x * p.qscale, b.y * p.qscale, b.z * p.qscale, b.w * p.qscale};
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    hi[e] = pack_bf16(x[2 * e], x[2 * e + 1]);
-                    lo[e] = pack_bf16(x[2 * e] - bf16_lo_f(hi[e]), x[2 * e + 1] - bf16_hi_f(hi[e]));
-                }
-                const uint32_t off = c * (kWRows * 128) + sw128(r, u);
-                *reinterpret_cast<uint4*>(smem + kOffQhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(smem + kOffQlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                const uint4 v = make_uint4(pack_bf16(a.x * p.qscale, a.y * p.qscale), pack_bf16(a.z * p.qscale, a.w * p.qscale),
+                                           pack_bf16(b.x * p.qscale, b.y * p.qscale), pack_bf16(b.z * p.qscale, b.w * p.qscale));
+                *reinterpret_cast<uint4*>(qs + c * (kWRows * 128) + sw128(r, u)) = v;
             }
         fence_proxy_async_smem();
     }
@@ -265,104 +259,125 @@ __global__ void __launch_bounds__(kWThreads, 1)
     const uint32_t tmem = *tmem_slot;
     const uint32_t smem_base = smem_u32(smem);
 
-    if (warp == 0 || warp == 6) {
-        // ------------------------------------------------------------ producers
-        // warp 0: K tiles into the K ring; warp 6: V tiles into the V ring. Each tile is one
-        // copy per (block, 64-dim chunk); blocks past the context repeat the last valid one
-        // (masked, and V zeroed there).
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        // One lane fills both rings, polling without blocking: K tile j as soon as its slot
+        // is free (S of both query tiles done with the slot's previous tile), V tile j once
+        // K tile j is issued and its slot is free (P.V of both tiles done).
         if (lane == 0) {
-            const bool is_k = warp == 0;
-            const CUtensorMap* map = is_k ? &tmk : &tmv;
-            const int nst = is_k ? kKStages : kVStages;
-            uint64_t* fullb = is_k ? kfull : vfull;
-            uint64_t* emptyb = is_k ? kempty : vempty;
-            uint8_t* ring = smem + (is_k ? kOffK : kOffV);
-            prefetch_tensormap(map);
+            prefetch_tensormap(&tmk);
+            prefetch_tensormap(&tmv);
             const int per_tile = kWKeys / p.bs;
-            int issued = 0;
-            for (int jt = 0; jt < ntiles; ++jt) {
-                const int s = jt % nst;
-                if (!mbar_wait_bounded(&emptyb[s], ((jt / nst) & 1u) ^ 1u) || *abort_flag) {
-                    *abort_flag = 1;
-                    atomicExch(p.err, kErrTimeout);
-                    break;
-                }
-                uint8_t* dst = ring + s * kKVBytes;
-                mbar_arrive_expect_tx(&fullb[s], kKVBytes);
-                for (int b = 0; b < per_tile; ++b) {
-                    const int bi = min(jt * per_tile + b, nblk_ctx - 1);
-                    const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(tbl[bi]) * p.bs);
-                    for (int c = 0; c < 2; ++c)
-                        tma_load_4d(dst + c * (kWKeys * 128) + b * p.bs * 128, map, 0, slot0, h, c, &fullb[s]);
-                }
-                ++issued;
-            }
-            // never leave the CTA with copies still landing in its shared memory
-            for (int t = max(0, issued - nst); t < issued; ++t)
-                mbar_wait_bounded(&fullb[t % nst], static_cast<uint32_t>(t / nst) & 1u);
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        // Issues S_j and PV_{j-1} in whichever order their inputs become ready (polling
-        // both barriers without blocking), so P.V never waits behind the next K/V load.
-        if (lane == 0) {
-            // Descriptors: Q's are loop invariant; K's and V's are a base plus the 16-byte
-            // units of the stage / k-step offset (the start-address field is the low 14 bits).
-            uint64_t qd_hi[kWD / 16], qd_lo[kWD / 16];
-#pragma unroll
-            for (int kk = 0; kk < kWD / 16; ++kk) {
-                const uint32_t qoff = (kk >> 2) * (kWRows * 128) + (kk & 3) * 32;
-                qd_hi[kk] = smem_desc(smem_base + kOffQhi + qoff, 16, 1024);
-                qd_lo[kk] = smem_desc(smem_base + kOffQlo + qoff, 16, 1024);
-            }
-            const uint64_t kd0 = smem_desc(smem_base + kOffK, 16, 1024);
-            const uint64_t vd0 = smem_desc(smem_base + kOffV, kWKeys * 128, 1024);
-            int js = 0, jp = 0;  // next S tile / next P.V tile to issue
+            int jk = 0, jv = 0;
             unsigned long long idle_since = global_ns();
-            bool ok = true;
-            while (jp < ntiles) {
-                bool progressed = false;
-                if (js < ntiles && mbar_test_wait(&kfull[js % kKStages], static_cast<uint32_t>(js / kKStages) & 1u) &&
-                    (js < 2 || mbar_test_wait(&sfree[js & 1], static_cast<uint32_t>((js - 2) / 2) & 1u))) {
-                    tc_fence_after();
-                    const uint32_t sbase = static_cast<uint32_t>((js % kKStages) * kKVBytes);
-                    const uint32_t sd = tmem + (js & 1) * kWKeys;
+            auto issue = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* bar, int jt) {
+                // the tile's block ids first, as independent loads: one load latency per tile
+                // instead of one per block (each copy below is ordered after the loads)
+                int idv[kWKeys / 16];
 #pragma unroll
-                    for (int kk = 0; kk < kWD / 16; ++kk) {
-                        // A = Q [128 rows][128 dims] K-major, B = K [128 keys][128 dims] K-major
-                        const uint32_t koff = sbase + (kk >> 2) * (kWKeys * 128) + (kk & 3) * 32;
-                        const uint64_t bd = kd0 + (koff >> 4);
-                        umma_bf16(sd, qd_hi[kk], bd, kIdescS, kk > 0 ? 1u : 0u);
-                        umma_bf16(sd, qd_lo[kk], bd, kIdescS, 1u);
-                    }
-                    umma_commit(&sfull[js & 1]);
-                    umma_commit(&kempty[js % kKStages]);
-                    ++js;
+                for (int b = 0; b < kWKeys / 16; ++b)
+                    if (b < per_tile) idv[b] = __ldg(tbl + min(jt * per_tile + b, nblk_ctx - 1));  // past the end: valid, masked
+                mbar_arrive_expect_tx(bar, kKVBytes);
+#pragma unroll
+                for (int b = 0; b < kWKeys / 16; ++b) {
+                    if (b >= per_tile) break;
+                    const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(idv[b]) * p.bs);
+                    for (int c = 0; c < 2; ++c)
+                        tma_load_4d(dst + c * (kWKeys * 128) + b * p.bs * 128, map, 0, slot0, h, c, bar);
+                }
+            };
+            while (jv < ntiles) {
+                bool progressed = false;
+                if (jk < ntiles && mbar_test_wait(&kempty[jk % kKStages], ((jk / kKStages) & 1u) ^ 1u)) {
+                    issue(&tmk, smem + kOffK + (jk % kKStages) * kKVBytes, &kfull[jk % kKStages], jk);
+                    ++jk;
                     progressed = true;
                 }
-                if (jp < js && mbar_test_wait(&pfull[jp & 1], static_cast<uint32_t>(jp / 2) & 1u) &&
-                    mbar_test_wait(&vfull[jp % kVStages], static_cast<uint32_t>(jp / kVStages) & 1u)) {
-                    tc_fence_after();
-                    const uint32_t sbase = static_cast<uint32_t>((jp % kVStages) * kKVBytes);
-#pragma unroll
-                    for (int kk = 0; kk < kWKeys / 16; ++kk) {
-                        // A = P in TMEM (16 keys = 8 columns per step); B = V [key][128 dims] MN-major
-                        const int key0 = kk * 16;
-                        const uint32_t voff = sbase + key0 * 128;
-                        const uint64_t bd = vd0 + (voff >> 4);
-                        umma_bf16_ts(tmem + kColO, tmem + kColP + (jp & 1) * (kWKeys / 2) + kk * 8, bd, kIdescO,
-                                     (jp > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    umma_commit(&pvdone[jp & 1]);
-                    umma_commit(&vempty[jp % kVStages]);
-                    ++jp;
+                if (jv < jk && mbar_test_wait(&vempty[jv % kVStages], ((jv / kVStages) & 1u) ^ 1u)) {
+                    issue(&tmv, smem + kOffV + (jv % kVStages) * kKVBytes, &vfull[jv % kVStages], jv);
+                    ++jv;
                     progressed = true;
                 }
                 if (progressed) {
                     idle_since = global_ns();
                 } else if (*abort_flag || global_ns() - idle_since > kWaitLimitNs) {
-                    ok = false;
+                    *abort_flag = 1;
+                    atomicExch(p.err, kErrTimeout);
                     break;
+                }
+            }
+            // never leave the CTA with copies still landing in its shared memory
+            for (int t = max(0, jk - kKStages); t < jk; ++t)
+                mbar_wait_bounded(&kfull[t % kKStages], static_cast<uint32_t>(t / kKStages) & 1u);
+            for (int t = max(0, jv - kVStages); t < jv; ++t)
+                mbar_wait_bounded(&vfull[t % kVStages], static_cast<uint32_t>(t / kVStages) & 1u);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        // Order per key tile j (after S_0(0), S_1(0)): P_0.V(j), S_0(j+1), P_1.V(j), S_1(j+1).
+        // Each query tile's S(j+1) overwrites its P(j) in TMEM, so it is issued right after
+        // that tile's P.V(j) (tcgen05 MMAs of one thread execute in issue order); softmax of
+        // one tile overlaps the other tile's MMAs.
+        if (lane == 0) {
+            uint64_t qd[2][kWD / 16];
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int kk = 0; kk < kWD / 16; ++kk)
+                    qd[t][kk] = smem_desc(smem_base + kOffQ + t * kQBytes + (kk >> 2) * (kWRows * 128) + (kk & 3) * 32,
+                                          16, 1024);
+            const uint64_t kd0 = smem_desc(smem_base + kOffK, 16, 1024);
+            const uint64_t vd0 = smem_desc(smem_base + kOffV, kWKeys * 128, 1024);
+            bool ok = true;
+            auto wait = [&](uint64_t* bar, uint32_t parity) {
+                if (ok && (!mbar_wait_bounded(bar, parity) || *abort_flag)) ok = false;
+                return ok;
+            };
+            auto issue_s = [&](int t, int jt) {
+                const uint32_t kb = static_cast<uint32_t>((jt % kKStages) * kKVBytes);
+#pragma unroll
+                for (int kk = 0; kk < kWD / 16; ++kk) {
+                    // A = Q_t [128 rows][128 dims] K-major, B = K [128 keys][128 dims] K-major
+                    const uint64_t bd = kd0 + ((kb + (kk >> 2) * (kWKeys * 128) + (kk & 3) * 32) >> 4);
+                    umma_bf16(tmem + t * kWKeys, qd[t][kk], bd, kIdescS, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(&sfull[t]);
+            };
+            auto issue_pv = [&](int t, int jt) {
+                const uint32_t vb = static_cast<uint32_t>((jt % kVStages) * kKVBytes);
+#pragma unroll
+                for (int kk = 0; kk < kWKeys / 16; ++kk) {
+                    // A = P_t in TMEM (16 keys = 8 columns per step); B = V [key][128 dims] MN-major
+                    const uint64_t bd = vd0 + ((vb + kk * 16 * 128) >> 4);
+                    umma_bf16_ts(tmem + kColO + t * kWD, tmem + t * kWKeys + kk * 8, bd, kIdescO,
+                                 (jt > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(&pvdone[t]);
+            };
+            if (ntiles > 0 && wait(&kfull[0], 0)) {
+                tc_fence_after();
+                issue_s(0, 0);
+                issue_s(1, 0);
+                umma_commit(&kempty[0]);
+            }
+            for (int jt = 0; jt < ntiles && ok; ++jt) {
+                const bool more = jt + 1 < ntiles;
+                if (!wait(&vfull[jt % kVStages], static_cast<uint32_t>(jt / kVStages) & 1u)) break;
+                if (!wait(&pfull[0], static_cast<uint32_t>(jt & 1))) break;
+                tc_fence_after();
+                issue_pv(0, jt);
+                if (more) {
+                    if (!wait(&kfull[(jt + 1) % kKStages], static_cast<uint32_t>((jt + 1) / kKStages) & 1u)) break;
+                    tc_fence_after();
+                    issue_s(0, jt + 1);
+                }
+                if (!wait(&pfull[1], static_cast<uint32_t>(jt & 1))) break;
+                tc_fence_after();
+                issue_pv(1, jt);
+                umma_commit(&vempty[jt % kVStages]);
+                if (more) {
+                    issue_s(1, jt + 1);
+                    umma_commit(&kempty[(jt + 1) % kKStages]);
                 }
             }
             if (!ok) {
@@ -371,20 +386,18 @@ __global__ void __launch_bounds__(kWThreads, 1)
             }
         }
     } else {
-        // ------------------------------------------------------------ softmax warpgroup
-        const int q4 = warp & 3;
-        const int r = 32 * q4 + lane;
-        const int t = r / g, jh = r % g;
-        const bool live = t < ntok;
-        const int orow = p.tok_row[tok0 + (live ? t : 0)];
-        // last visible key: the row's own position, and never past the item's key range
-        const int qlim = live ? min(p.tok_pos[tok0 + t], kv_end - 1) : -1;
+        // ------------------------------------------------------------ softmax warpgroups
+        // warps 2-5: query tile 0, warps 6-9: query tile 1; thread = row (TMEM lane).
+        // last visible key: the row's own position, and never past its item's key range
+        const int qlim = live ? min(p.tok_pos[tok0 + t_row], kend_t - 1) : -1;
         const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+        const uint32_t tS = trow + tile * kWKeys;      // S_t, and P_t in its first 64 columns
+        const uint32_t tO = trow + kColO + tile * kWD;  // O_t
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int jt = 0; jt < ntiles; ++jt) {
             const int kbase = jt * kWKeys;
-            const bool got = mbar_wait_bounded(&sfull[jt & 1], static_cast<uint32_t>(jt / 2) & 1u);
+            const bool got = mbar_wait_bounded(&sfull[tile], static_cast<uint32_t>(jt & 1));
             if (!__all_sync(0xffffffffu, got) || *abort_flag) {
                 ok = false;
                 break;
@@ -392,19 +405,16 @@ __global__ void __launch_bounds__(kWThreads, 1)
             tc_fence_after();
             float sv[kWKeys];
 #pragma unroll
-            for (int c = 0; c < kWKeys / 32; ++c) tmem_ld32(trow + (jt & 1) * kWKeys + c * 32, sv + c * 32);
+            for (int c = 0; c < kWKeys / 32; ++c) tmem_ld32(tS + c * 32, sv + c * 32);
             tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sfree[jt & 1]);
-            // mask by absolute position, only on tiles that reach past this row's position
+            // mask by absolute position, only on tiles that reach past this row's limit
             // (earlier tiles are fully visible; dead rows mask everything)
             if (kbase + kWKeys - 1 > qlim) {
 #pragma unroll
                 for (int i = 0; i < kWKeys; ++i)
                     if (kbase + i > qlim) sv[i] = -INFINITY;
             }
-            // row max and sum as 8 independent chains (the serial chains were the slow part)
+            // row max as 8 independent chains
             float mx8[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
@@ -420,50 +430,48 @@ __global__ void __launch_bounds__(kWThreads, 1)
             const float mnew = (m == -INFINITY || mx > m + 8.f) ? mx : m;
             const float base = mnew == -INFINITY ? 0.f : mnew;
             const float corr = m == -INFINITY ? 0.f : ex2_approx(m - base);
-            float sum8[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) sum8[k] = 0.f;
-            uint32_t pk[kWKeys / 2];
-#pragma unroll
-            for (int i = 0; i < kWKeys / 2; ++i) {
-                const float a = ex2_approx(sv[2 * i] - base), b = ex2_approx(sv[2 * i + 1] - base);
-                sum8[i & 7] += a + b;
-                pk[i] = pack_bf16(a, b);
-            }
-            const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
-            l = l * corr + sum;
-            m = mnew;
-            // P_j goes to TMEM buffer jt&1, last read by PV(jt-2)
-            if (jt >= 2) {
-                const bool done = mbar_wait_bounded(&pvdone[jt & 1], static_cast<uint32_t>((jt - 2) / 2) & 1u);
-                if (!__all_sync(0xffffffffu, done) || *abort_flag) {
-                    ok = false;
-                    break;
-                }
-            }
             if (jt >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
-                // O must include PV(jt-1) before it is rescaled
-                const bool done = mbar_wait_bounded(&pvdone[(jt - 1) & 1], static_cast<uint32_t>((jt - 1) / 2) & 1u);
+                // O must include P.V(jt-1) before it is rescaled
+                const bool done = mbar_wait_bounded(&pvdone[tile], static_cast<uint32_t>((jt - 1) & 1));
                 if (!__all_sync(0xffffffffu, done) || *abort_flag) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                {
 #pragma unroll 1
-                    for (int c = 0; c < kWD / 32; ++c) {
-                        float o[32];
-                        tmem_ld32(trow + kColO + c * 32, o);
-                        tmem_wait_ld();
+                for (int c = 0; c < kWD / 32; ++c) {
+                    float o[32];
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= corr;
-                        tmem_st32(trow + kColO + c * 32, o);
-                    }
-                    tmem_wait_st();
+                    for (int i = 0; i < 32; ++i) o[i] *= corr;
+                    tmem_st32(tO + c * 32, o);
                 }
+                tmem_wait_st();
             }
-            if (jt == ntiles - 1 && kv_end < kbase + kWKeys) {
+            // P = 2^(S - base) as bf16 pairs over S's first 64 columns (all of S is in
+            // registers already), 64 keys at a time
+            float sum8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) sum8[k] = 0.f;
+#pragma unroll
+            for (int half = 0; half < kWKeys / 64; ++half) {
+                uint32_t pk[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float a = ex2_approx(sv[half * 64 + 2 * i] - base);
+                    const float b = ex2_approx(sv[half * 64 + 2 * i + 1] - base);
+                    sum8[i & 7] += a + b;
+                    pk[i] = pack_bf16(a, b);
+                }
+                tmem_st32u(tS + half * 32, pk);
+            }
+            tmem_wait_st();
+            l = l * corr + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
+            m = mnew;
+            if (tile == 0 && jt == ntiles - 1 && kv_end < kbase + kWKeys) {
                 // keys past the context in the last tile: zero their V rows so P = 0 meets 0
+                // (tile 0's P.V is issued first, so tile 1's sees the zeros too)
                 const int s = jt % kVStages;
                 const bool landed = mbar_wait_bounded(&vfull[s], static_cast<uint32_t>(jt / kVStages) & 1u);
                 if (!__all_sync(0xffffffffu, landed)) {
@@ -478,27 +486,23 @@ __global__ void __launch_bounds__(kWThreads, 1)
                     const int c = (x / 8) & 1;
                     *reinterpret_cast<uint4*>(vd + c * (kWKeys * 128) + sw128(key, x & 7)) = make_uint4(0, 0, 0, 0);
                 }
+                fence_proxy_async_smem();  // the zeroed V rows (generic writes) before the MMA reads them
             }
-            // P row -> TMEM (A operand of P.V), bf16 pairs along the columns
-#pragma unroll
-            for (int c = 0; c < kWKeys / 64; ++c)
-                tmem_st32u(trow + kColP + (jt & 1) * (kWKeys / 2) + c * 32, pk + c * 32);
-            tmem_wait_st();
-            fence_proxy_async_smem();  // the zeroed V rows (generic writes) before the MMA reads them
             tc_fence_before();
-            // one arrival per warp (count 4): the MMA starts once all rows of P are written
+            // one arrival per warp (count 4): the MMA starts once all rows of P_t are written
             __syncwarp();
-            if (lane == 0) mbar_arrive(&pfull[jt & 1]);
+            if (lane == 0) mbar_arrive(&pfull[tile]);
         }
         if (ok && ntiles > 0) {
-            const bool done = mbar_wait_bounded(&pvdone[(ntiles - 1) & 1], static_cast<uint32_t>((ntiles - 1) / 2) & 1u);
+            const bool done = mbar_wait_bounded(&pvdone[tile], static_cast<uint32_t>((ntiles - 1) & 1));
             ok = __all_sync(0xffffffffu, done) && !*abort_flag;
         }
         if (!ok) {
             *abort_flag = 1;
             if (lane == 0) atomicExch(p.err, kErrTimeout);
-        } else {
+        } else if (ntok > 0) {
             tc_fence_after();
+            const int orow = p.tok_row[tok0 + (live ? t_row : 0)];
             const size_t oidx = static_cast<size_t>(orow) * p.H + h * g + jh;
             float* op = p.out + oidx * kWD;
             // This partial is o / l with log-sum-exp m + log2(l). Shared-prefix pass: the row
@@ -517,7 +521,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
 #pragma unroll 1
             for (int c = 0; c < kWD / 32; ++c) {
                 float o[32];
-                tmem_ld32(trow + kColO + c * 32, o);
+                tmem_ld32(tO + c * 32, o);
                 tmem_wait_ld();
                 if (live) {
 #pragma unroll
@@ -550,10 +554,10 @@ size_t wide_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tmv1, const WideParams& p,
                                   cudaStream_t st) {
-    if (p.nitems <= 0) return cudaSuccess;
+    if (p.npairs <= 0) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(wide_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    wide_attn_kernel<<<dim3(p.nitems, p.kvh), kWThreads, kSmemBytes, st>>>(*tmk1, *tmv1, p);
+    wide_attn_kernel<<<dim3(p.npairs, p.kvh), kWThreads, kSmemBytes, st>>>(*tmk1, *tmv1, p);
     return cudaGetLastError();
 }
 

@@ -114,7 +114,8 @@ struct WideParams {
     // Shared-prefix pass: NULL = write the normalised output; else merge this partial with
     // the output row already written (and its log2-domain log-sum-exp [rows][H] here).
     const float* lse;
-    int nitems;
+    const int32_t* w_pair;  // [npairs][2] items of each CTA (second = -1: none), same table
+    int npairs;
     int H;
     int kvh;
     int g;
