@@ -221,15 +221,19 @@ struct pk_batch {
     int prefix_sharing = 1;   // 0 off, 1 where the cost estimate favours it, 2 always
     std::vector<int32_t> w_seq, w_tok0, w_ntok, w_kend, tok_row, tok_pos;
     std::vector<int32_t> w_rows;   // rows of chunk items (appended separately)
-    std::vector<int32_t> w_pair;   // items of each wide CTA: chunk pairs, then prefix pairs
+    std::vector<int32_t> w_pair;   // item pairs: chunk pairs, then prefix pairs
     int npair_chunk = 0, npair_prefix = 0;
+    // wide-kernel schedule: per CTA a range of segments (pair, head, key tiles, slot, ph)
+    std::vector<int32_t> pair_kend, cta_seg, seg, ph_info, split;
+    int ncta_chunk = 0, ncta_prefix = 0, nslots = 0, nph = 0, nwsplit = 0;
+    DevBuf wpart;  // partial O and (max, sum) of pair-heads cut between CTAs
     std::vector<int32_t> u_kb0;    // per unit: first block read (after a shared prefix)
     std::vector<int32_t> seq_kb0;  // scratch: per sequence
     int tc_max_new = 0;            // most new tokens of a sequence on the split-KV kernel
     DevBuf lse;                    // [rows][H] when shared-prefix items exist
     Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows 8 w_seq
                     // 9 w_tok0 10 w_rows 11 w_ntok 12 w_kend 13 tok_row 14 tok_pos 15 u_kb0
-                    // 16 w_pair
+                    // 16 w_pair 17 pair_kend 18 cta_seg 19 seg 20 split
     DevBuf ws;
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
@@ -397,7 +401,9 @@ int cta_of_block(int64_t j, int64_t T, int64_t n) {
 // In mode 1 it is taken only where a cost estimate says reading the prefix once per
 // sequence (the split-KV path) would take longer than the wide-tile CTAs over it.
 constexpr int64_t kPrefixMinKeys = 64;
-constexpr double kWideUsPerKeyTile = 2.0;     // one CTA (256 rows) over one 128-key tile
+constexpr double kWideUsPerKeyTile = 2.5;     // one CTA (256 rows) over one 128-key tile
+constexpr double kWideFixedUs = 5.0;          // launch, Q load, epilogue
+constexpr int64_t kWideMinTilesPerCta = 4;    // stream-K shares smaller than this cost more than they save
 constexpr double kSplitKvBytesPerUs = 6.0e6;  // split-KV streaming rate (HBM / L2)
 
 void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>& tc_seqs) {
@@ -429,9 +435,10 @@ void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>
             }
             const int64_t keys = pb * P->block_size;
             if (keys >= kPrefixMinKeys) {
-                const int64_t ctas = ceil_div(ceil_div(toks, tpt), 2) * P->kvh;
-                const double waves = static_cast<double>(ceil_div(ctas, std::max(1, P->num_sms)));
-                const double est_wide = waves * static_cast<double>(ceil_div(keys, pk::kWideKeys)) * kWideUsPerKeyTile;
+                // stream-K over (pair-head, key tile): the work W in equal shares over <= one wave
+                const int64_t work = ceil_div(ceil_div(toks, tpt), 2) * P->kvh * ceil_div(keys, pk::kWideKeys);
+                const int64_t g = std::max<int64_t>(1, std::min<int64_t>(P->num_sms, work / kWideMinTilesPerCta));
+                const double est_wide = static_cast<double>(ceil_div(work, g)) * kWideUsPerKeyTile + kWideFixedUs;
                 const double est_split = static_cast<double>(units) * pb * blk_bytes / kSplitKvBytesPerUs;
                 if (B->prefix_sharing == 2 || est_wide < est_split) {
                     // the group's tokens, member by member, cut into items of tpt tokens
@@ -460,6 +467,92 @@ void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>
         }
         a = b;
     }
+}
+
+// Wide-kernel schedule. Chunk pairs: one CTA per (pair, KV head), whole key range. Prefix
+// pairs: the (pair-head, key tile) space, pair-heads in order, cut into G equal shares (G =
+// SMs, fewer when shares would be under kWideMinTilesPerCta tiles); a CTA's share is its
+// segment list; a pair-head met by several CTAs gets one partial slot per CTA.
+void build_wide_schedule(pk_batch* B) {
+    pk_pool* P = B->pool;
+    const int kvh = P->kvh;
+    const int npairs = B->npair_chunk + B->npair_prefix;
+    B->pair_kend.resize(npairs);
+    for (int x = 0; x < npairs; ++x) {
+        const int i0 = B->w_pair[2 * x], i1 = B->w_pair[2 * x + 1];
+        B->pair_kend[x] = std::max(B->w_kend[i0], i1 >= 0 ? B->w_kend[i1] : 0);
+    }
+    B->cta_seg.assign(1, 0);
+    B->seg.clear();
+    B->ph_info.clear();
+    B->split.clear();
+    B->nslots = B->nwsplit = 0;
+    auto tiles = [&](int x) { return ceil_div(B->pair_kend[x], pk::kWideKeys); };
+    auto add_seg = [&](int x, int h, int t0, int t1, int slot, int ph) {
+        B->seg.insert(B->seg.end(), {x, h, t0, t1, slot, ph});
+    };
+    for (int x = 0; x < B->npair_chunk; ++x)
+        for (int h = 0; h < kvh; ++h) {
+            const int ph = static_cast<int>(B->ph_info.size() / 2);
+            B->ph_info.insert(B->ph_info.end(), {0, 1});
+            add_seg(x, h, 0, tiles(x), -1, ph);
+            B->cta_seg.push_back(static_cast<int32_t>(B->seg.size() / 6));
+        }
+    B->ncta_chunk = B->npair_chunk * kvh;
+    int64_t W = 0;
+    for (int x = B->npair_chunk; x < npairs; ++x) W += static_cast<int64_t>(tiles(x)) * kvh;
+    B->ncta_prefix = 0;
+    if (W > 0) {
+        const int64_t G = std::max<int64_t>(1, std::min<int64_t>(P->num_sms, W / kWideMinTilesPerCta));
+        const size_t seg0 = B->seg.size() / 6;
+        // pair-heads in order: [base, base + T) of the work axis
+        int x = B->npair_chunk, h = 0;
+        int64_t base = 0;
+        for (int64_t c = 0; c < G; ++c) {
+            const int64_t lo = c * W / G, hi = (c + 1) * W / G;
+            int64_t pos = lo;
+            while (pos < hi) {
+                const int64_t T = tiles(x);
+                const int64_t a = pos - base, b = std::min<int64_t>(hi - base, T);
+                // pair-head index: the chunk pair-heads come first
+                const int ph = B->ncta_chunk + (x - B->npair_chunk) * kvh + h;
+                add_seg(x, h, static_cast<int>(a), static_cast<int>(b), 0, ph);
+                pos = base + b;
+                if (b == T) {
+                    base += T;
+                    if (++h == kvh) {
+                        h = 0;
+                        ++x;
+                    }
+                }
+            }
+            B->cta_seg.push_back(static_cast<int32_t>(B->seg.size() / 6));
+        }
+        B->ncta_prefix = static_cast<int>(G);
+        // slots: a pair-head with several segments gets one slot per segment
+        const int ph_base = static_cast<int>(B->ph_info.size() / 2);
+        const int nph_prefix = B->npair_prefix * kvh;
+        std::vector<int32_t> count(nph_prefix, 0);
+        const size_t nseg = B->seg.size() / 6;
+        for (size_t sidx = seg0; sidx < nseg; ++sidx) count[B->seg[6 * sidx + 5] - ph_base]++;
+        std::vector<int32_t> next(nph_prefix, -1);
+        for (int q = 0; q < nph_prefix; ++q) {
+            if (count[q] > 1) {
+                B->ph_info.insert(B->ph_info.end(), {B->nslots, count[q]});
+                B->split.insert(B->split.end(), {B->npair_chunk + q / kvh, q % kvh, B->nslots, count[q]});
+                next[q] = B->nslots;
+                B->nslots += count[q];
+            } else {
+                B->ph_info.insert(B->ph_info.end(), {0, 1});
+            }
+        }
+        for (size_t sidx = seg0; sidx < nseg; ++sidx) {
+            const int q = B->seg[6 * sidx + 5] - ph_base;
+            B->seg[6 * sidx + 4] = next[q] >= 0 ? next[q]++ : -1;
+        }
+    }
+    B->nph = static_cast<int>(B->ph_info.size() / 2);
+    B->nwsplit = static_cast<int>(B->split.size() / 4);
 }
 
 int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
@@ -560,6 +653,7 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     };
     B->npair_chunk = make_pairs(0, B->nwide);
     B->npair_prefix = make_pairs(B->nwide, B->nwide + B->nprefix);
+    build_wide_schedule(B);
     B->nu = static_cast<int>(B->u_seq.size());
     B->ngeneric = static_cast<int>(B->gen_rows.size());
     if (B->nu > 0) {
@@ -604,6 +698,12 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan.add(B->tok_pos.data(), B->tok_pos.size() * 4);
     B->plan.add(B->u_kb0.data(), B->u_kb0.size() * 4);
     B->plan.add(B->w_pair.data(), B->w_pair.size() * 4);
+    B->plan.add(B->pair_kend.data(), B->pair_kend.size() * 4);
+    B->plan.add(B->cta_seg.data(), B->cta_seg.size() * 4);
+    B->plan.add(B->seg.data(), B->seg.size() * 4);
+    B->plan.add(B->split.data(), B->split.size() * 4);
+    if (B->nslots > 0)
+        PK_CUDA(B->wpart.reserve(static_cast<size_t>(B->nslots) * 2 * 128 * (128 + 2) * sizeof(float)));
     if (B->nprefix > 0) PK_CUDA(B->lse.reserve(static_cast<size_t>(B->nrows) * H * sizeof(float)));
     int rc = B->plan.commit(st);
     if (rc != PK_OK) return rc;
@@ -647,7 +747,7 @@ int check_heads(const pk_batch* B, int H) {
     return PK_OK;
 }
 
-// Wide-tile launch parameters for CTAs (item pairs) [first, first + n) of the plan.
+// Wide-tile launch parameters for CTAs [first, first + n) of the plan's schedule.
 pk::WideParams wide_params(pk_batch* B, int layer, int H, const float* q, float* out, int first, int n,
                            const float* lse) {
     pk_pool* P = B->pool;
@@ -661,11 +761,16 @@ pk::WideParams wide_params(pk_batch* B, int layer, int H, const float* q, float*
     w.w_tok0 = B->plan.at<int32_t>(9);
     w.w_ntok = B->plan.at<int32_t>(11);
     w.w_kend = B->plan.at<int32_t>(12);
-    w.w_pair = B->plan.at<int32_t>(16) + 2 * first;
+    w.w_pair = B->plan.at<int32_t>(16);
+    w.pair_kend = B->plan.at<int32_t>(17);
+    w.cta_seg = B->plan.at<int32_t>(18) + first;
+    w.seg = B->plan.at<int32_t>(19);
+    w.part_o = static_cast<float*>(B->wpart.ptr);
+    w.part_ml = static_cast<float*>(B->wpart.ptr) + static_cast<size_t>(B->nslots) * 2 * 128 * 128;
     w.tok_row = B->plan.at<int32_t>(13);
     w.tok_pos = B->plan.at<int32_t>(14);
     w.lse = lse;
-    w.npairs = n;
+    w.nctas = n;
     w.H = H;
     w.kvh = P->kvh;
     w.g = H / P->kvh;
@@ -705,7 +810,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
             PK_CUDA(prof_end(B, kProfAppend, ws));
             B->launches++;
         }
-        const pk::WideParams w = wide_params(B, layer, H, q, out, 0, B->npair_chunk, nullptr);
+        const pk::WideParams w = wide_params(B, layer, H, q, out, 0, B->ncta_chunk, nullptr);
         PK_CUDA(prof_begin(B, ws));
         PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, ws));
         PK_CUDA(prof_end(B, kProfWide, ws));
@@ -772,10 +877,14 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
     }
     if (B->nprefix > 0) {
         // shared-prefix items: after the split-KV kernel has written the rows they merge into
-        const pk::WideParams w = wide_params(B, layer, H, q, out, B->npair_chunk, B->npair_prefix,
+        const pk::WideParams w = wide_params(B, layer, H, q, out, B->ncta_chunk, B->ncta_prefix,
                                              static_cast<const float*>(B->lse.ptr));
         PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, st));
+        if (B->nwsplit > 0) {
+            PK_CUDA(pk::launch_wide_merge(w, B->plan.at<int32_t>(20), B->nwsplit, st));
+            B->launches++;
+        }
         PK_CUDA(prof_end(B, kProfWide, st));
         B->launches++;
     }

@@ -4,12 +4,12 @@
 // Semantics: pagellm cache/paged.py:454-463 -> model/transformer.py:116-146: the query at
 // absolute position p sees keys 0..p of its sequence, keys read through the block table.
 //
-// One CTA per (pair of work items, KV head h). A work item is one query tile: up to 128/g
-// query tokens read through one block table; rows are (token, head-in-group) pairs,
-// row r = t*g + j, so the g heads of a token share every K/V tile. The two items of a CTA
-// read the same block table, so every K/V tile brought into shared memory serves 256 query
-// rows (half the L2 -> SM traffic of one tile per CTA, which is what bounded that design).
-// Keys 0..kend-1 stream in tiles of 128 (128/bs blocks). Two kinds of item:
+// Work: a work item is one query tile, up to 128/g query tokens read through one block
+// table; rows are (token, head-in-group) pairs, row r = t*g + j, so the g heads of a token
+// share every K/V tile. Items come in pairs that read the same block table, so every K/V
+// tile brought into shared memory serves 256 query rows (half the L2 -> SM traffic of one
+// tile per CTA, which is what bounded that design). Keys 0..kend-1 of a pair stream in tiles
+// of 128 (128/bs blocks). Two kinds of item:
 //   chunk   consecutive tokens of one sequence (a prefill chunk or a wide verify window);
 //           causal by absolute position.
 //   prefix  tokens of several sequences whose block tables begin with the same blocks
@@ -17,6 +17,12 @@
 //           token's position. Each such K/V tile is read once per 256 rows instead of once
 //           per sequence; the partial is merged into the row that the split-KV kernel wrote
 //           for the rest of the sequence (cascade attention).
+// Schedule: each CTA walks a list of segments = key-tile ranges of (item pair, KV head).
+// For chunk items a segment is a whole pair-head; shared-prefix work is cut stream-K style:
+// the launch's (pair-head, key tile) space is split into equal shares, one per CTA (at most
+// one wave), and a pair-head cut between CTAs leaves a partial (un-normalised O, max, sum)
+// per CTA that the last CTA to finish it merges in slot order (per pair-head counters,
+// left at zero).
 //
 // Warp roles (320 threads):
 //   warp 0  producer: one lane fills a 3-slot K ring and a 2-slot V ring with TMA loads (no
@@ -173,6 +179,15 @@ __device__ __forceinline__ uint32_t sw128(int r, int u) {
     return static_cast<uint32_t>(r * 128 + ((u ^ (r & 7)) << 4));
 }
 
+// Per-CTA segment list: a segment is key tiles [t0, t1) of one (item pair, KV head).
+struct Seg {
+    int pair, head, t0, t1, slot, ph;  // slot < 0: the segment covers the whole pair-head
+};
+__device__ __forceinline__ Seg load_seg(const int32_t* s, int i) {
+    const int32_t* e = s + 6 * i;
+    return Seg{e[0], e[1], e[2], e[3], e[4], e[5]};
+}
+
 __global__ void __launch_bounds__(kWThreads, 1)
     wide_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                      const WideParams p) {
@@ -186,22 +201,15 @@ __global__ void __launch_bounds__(kWThreads, 1)
     uint64_t* sfull = vempty + kVStages;  // [tile]
     uint64_t* pfull = sfull + 2;          // [tile], one arrival per softmax warp
     uint64_t* pvdone = pfull + 2;         // [tile]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pvdone + 2);
+    uint64_t* qfull = pvdone + 2;         // [tile], Q of the next segment in shared memory
+    uint64_t* ofree = qfull + 2;          // [tile], O of the last segment read out of TMEM
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ofree + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int h = blockIdx.y;
     const int g = p.g;
-    // the pair of items (query tiles) this CTA owns; both read the same block table
-    int it_of[2] = {p.w_pair[2 * blockIdx.x], p.w_pair[2 * blockIdx.x + 1]};
-    const int seq = p.w_seq[it_of[0]];
-    const int kend0 = p.w_kend[it_of[0]];
-    const int kend1 = it_of[1] >= 0 ? p.w_kend[it_of[1]] : 0;
-    const int kv_end = max(kend0, kend1);  // keys 0..kv_end-1 are streamed
-    const int ntiles = (kv_end + kWKeys - 1) / kWKeys;
-    const int nblk_ctx = (kv_end + p.bs - 1) / p.bs;
-    const int32_t* tbl = p.ids + p.indptr[seq];
+    const int s_begin = p.cta_seg[blockIdx.x], s_end = p.cta_seg[blockIdx.x + 1];
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kKStages; ++s) {
@@ -216,6 +224,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
             mbar_init(&sfull[t], 1);
             mbar_init(&pfull[t], 4);
             mbar_init(&pvdone[t], 1);
+            mbar_init(&qfull[t], 4);
+            mbar_init(&ofree[t], 4);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -223,35 +233,6 @@ __global__ void __launch_bounds__(kWThreads, 1)
     if (warp == 1) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
-    }
-
-    // softmax warps: tile = which query tile, row = thread's TMEM lane / Q row
-    const int tile = warp >= 6 ? 1 : 0;
-    const int q4 = warp & 3;
-    const int r = 32 * q4 + lane;
-    const int item = it_of[tile];
-    const int ntok = (warp >= 2 && item >= 0) ? p.w_ntok[item] : 0;
-    const int tok0 = item >= 0 ? p.w_tok0[item] : 0;
-    const int kend_t = tile ? kend1 : kend0;
-    const int t_row = r / g, jh = r % g;
-    const bool live = t_row < ntok;
-
-    // ---- Q tiles -> shared memory: scaled into the exp2 domain, bf16, [chunk][row][64] SW128
-    if (warp >= 2) {
-        const float* qp = p.q + (static_cast<size_t>(p.tok_row[tok0 + (live ? t_row : 0)]) * p.H + h * g + jh) * kWD;
-        uint8_t* qs = smem + kOffQ + tile * kQBytes;
-        for (int c = 0; c < 2; ++c)
-            for (int u = 0; u < 8; ++u) {
-                float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-                if (live) {
-                    a = *reinterpret_cast<const float4*>(qp + c * 64 + u * 8);
-                    b = *reinterpret_cast<const float4*>(qp + c * 64 + u * 8 + 4);
-                }
-                const uint4 v = make_uint4(pack_bf16(a.x * p.qscale, a.y * p.qscale), pack_bf16(a.z * p.qscale, a.w * p.qscale),
-                                           pack_bf16(b.x * p.qscale, b.y * p.qscale), pack_bf16(b.z * p.qscale, b.w * p.qscale));
-                *reinterpret_cast<uint4*>(qs + c * (kWRows * 128) + sw128(r, u)) = v;
-            }
-        fence_proxy_async_smem();
     }
     tc_fence_before();
     __syncthreads();
@@ -261,41 +242,55 @@ __global__ void __launch_bounds__(kWThreads, 1)
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
-        // One lane fills both rings, polling without blocking: K tile j as soon as its slot
-        // is free (S of both query tiles done with the slot's previous tile), V tile j once
-        // K tile j is issued and its slot is free (P.V of both tiles done).
+        // One lane fills both rings over the CTA's segments in order, polling without
+        // blocking: K tile n as soon as its slot is free (S of both query tiles done with the
+        // slot's previous tile), V tile n once K tile n is issued and its slot is free.
         if (lane == 0) {
             prefetch_tensormap(&tmk);
             prefetch_tensormap(&tmv);
             const int per_tile = kWKeys / p.bs;
-            int jk = 0, jv = 0;
-            unsigned long long idle_since = global_ns();
-            auto issue = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* bar, int jt) {
+            // cursors: segment, tile within the pair's key tiles, running tile count
+            int ks = s_begin, vs = s_begin, nk = 0, nv = 0;
+            Seg sk = ks < s_end ? load_seg(p.seg, ks) : Seg{}, sv = sk;
+            int kt = sk.t0, vt = sv.t0;
+            auto issue = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* bar, const Seg& sg, int jt) {
+                const int i0 = p.w_pair[2 * sg.pair];
+                const int32_t* tbl = p.ids + p.indptr[p.w_seq[i0]];
+                const int kv_end = p.pair_kend[sg.pair];
+                const int nblk = (kv_end + p.bs - 1) / p.bs;
                 // the tile's block ids first, as independent loads: one load latency per tile
-                // instead of one per block (each copy below is ordered after the loads)
                 int idv[kWKeys / 16];
 #pragma unroll
                 for (int b = 0; b < kWKeys / 16; ++b)
-                    if (b < per_tile) idv[b] = __ldg(tbl + min(jt * per_tile + b, nblk_ctx - 1));  // past the end: valid, masked
+                    if (b < per_tile) idv[b] = __ldg(tbl + min(jt * per_tile + b, nblk - 1));  // past the end: valid, masked
                 mbar_arrive_expect_tx(bar, kKVBytes);
 #pragma unroll
                 for (int b = 0; b < kWKeys / 16; ++b) {
                     if (b >= per_tile) break;
                     const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(idv[b]) * p.bs);
                     for (int c = 0; c < 2; ++c)
-                        tma_load_4d(dst + c * (kWKeys * 128) + b * p.bs * 128, map, 0, slot0, h, c, bar);
+                        tma_load_4d(dst + c * (kWKeys * 128) + b * p.bs * 128, map, 0, slot0, sg.head, c, bar);
                 }
             };
-            while (jv < ntiles) {
+            unsigned long long idle_since = global_ns();
+            while (vs < s_end) {
                 bool progressed = false;
-                if (jk < ntiles && mbar_test_wait(&kempty[jk % kKStages], ((jk / kKStages) & 1u) ^ 1u)) {
-                    issue(&tmk, smem + kOffK + (jk % kKStages) * kKVBytes, &kfull[jk % kKStages], jk);
-                    ++jk;
+                if (ks < s_end && mbar_test_wait(&kempty[nk % kKStages], ((nk / kKStages) & 1u) ^ 1u)) {
+                    issue(&tmk, smem + kOffK + (nk % kKStages) * kKVBytes, &kfull[nk % kKStages], sk, kt);
+                    ++nk;
+                    if (++kt == sk.t1 && ++ks < s_end) {
+                        sk = load_seg(p.seg, ks);
+                        kt = sk.t0;
+                    }
                     progressed = true;
                 }
-                if (jv < jk && mbar_test_wait(&vempty[jv % kVStages], ((jv / kVStages) & 1u) ^ 1u)) {
-                    issue(&tmv, smem + kOffV + (jv % kVStages) * kKVBytes, &vfull[jv % kVStages], jv);
-                    ++jv;
+                if (nv < nk && mbar_test_wait(&vempty[nv % kVStages], ((nv / kVStages) & 1u) ^ 1u)) {
+                    issue(&tmv, smem + kOffV + (nv % kVStages) * kKVBytes, &vfull[nv % kVStages], sv, vt);
+                    ++nv;
+                    if (++vt == sv.t1 && ++vs < s_end) {
+                        sv = load_seg(p.seg, vs);
+                        vt = sv.t0;
+                    }
                     progressed = true;
                 }
                 if (progressed) {
@@ -307,17 +302,19 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 }
             }
             // never leave the CTA with copies still landing in its shared memory
-            for (int t = max(0, jk - kKStages); t < jk; ++t)
+            for (int t = max(0, nk - kKStages); t < nk; ++t)
                 mbar_wait_bounded(&kfull[t % kKStages], static_cast<uint32_t>(t / kKStages) & 1u);
-            for (int t = max(0, jv - kVStages); t < jv; ++t)
+            for (int t = max(0, nv - kVStages); t < nv; ++t)
                 mbar_wait_bounded(&vfull[t % kVStages], static_cast<uint32_t>(t / kVStages) & 1u);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        // Order per key tile j (after S_0(0), S_1(0)): P_0.V(j), S_0(j+1), P_1.V(j), S_1(j+1).
-        // Each query tile's S(j+1) overwrites its P(j) in TMEM, so it is issued right after
-        // that tile's P.V(j) (tcgen05 MMAs of one thread execute in issue order); softmax of
-        // one tile overlaps the other tile's MMAs.
+        // Per segment, after S_0(first), S_1(first), for each key tile j:
+        // P_0.V(j), S_0(j+1), P_1.V(j), S_1(j+1). Each query tile's S(j+1) overwrites its P(j)
+        // in TMEM, so it is issued right after that tile's P.V(j) (tcgen05 MMAs of one thread
+        // execute in issue order); softmax of one tile overlaps the other tile's MMAs. A
+        // segment's first S_t waits for its Q_t in shared memory, its first P_t.V for the
+        // previous segment's O_t to have been read out.
         if (lane == 0) {
             uint64_t qd[2][kWD / 16];
 #pragma unroll
@@ -333,8 +330,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 if (ok && (!mbar_wait_bounded(bar, parity) || *abort_flag)) ok = false;
                 return ok;
             };
-            auto issue_s = [&](int t, int jt) {
-                const uint32_t kb = static_cast<uint32_t>((jt % kKStages) * kKVBytes);
+            auto issue_s = [&](int t, int n) {  // n: the CTA's running key-tile count
+                const uint32_t kb = static_cast<uint32_t>((n % kKStages) * kKVBytes);
 #pragma unroll
                 for (int kk = 0; kk < kWD / 16; ++kk) {
                     // A = Q_t [128 rows][128 dims] K-major, B = K [128 keys][128 dims] K-major
@@ -343,41 +340,51 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 }
                 umma_commit(&sfull[t]);
             };
-            auto issue_pv = [&](int t, int jt) {
-                const uint32_t vb = static_cast<uint32_t>((jt % kVStages) * kKVBytes);
+            auto issue_pv = [&](int t, int n, bool first) {
+                const uint32_t vb = static_cast<uint32_t>((n % kVStages) * kKVBytes);
 #pragma unroll
                 for (int kk = 0; kk < kWKeys / 16; ++kk) {
                     // A = P_t in TMEM (16 keys = 8 columns per step); B = V [key][128 dims] MN-major
                     const uint64_t bd = vd0 + ((vb + kk * 16 * 128) >> 4);
                     umma_bf16_ts(tmem + kColO + t * kWD, tmem + t * kWKeys + kk * 8, bd, kIdescO,
-                                 (jt > 0 || kk > 0) ? 1u : 0u);
+                                 (!first || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(&pvdone[t]);
             };
-            if (ntiles > 0 && wait(&kfull[0], 0)) {
+            int n = 0;  // running key-tile count (ring and barrier phases)
+            for (int si = s_begin; si < s_end && ok; ++si) {
+                const Seg sg = load_seg(p.seg, si);
+                const int k = si - s_begin;  // segment count (qfull / ofree phases)
+                const int nt = sg.t1 - sg.t0;
+                if (!wait(&kfull[n % kKStages], static_cast<uint32_t>(n / kKStages) & 1u)) break;
+                if (!wait(&qfull[0], static_cast<uint32_t>(k & 1))) break;
                 tc_fence_after();
-                issue_s(0, 0);
-                issue_s(1, 0);
-                umma_commit(&kempty[0]);
-            }
-            for (int jt = 0; jt < ntiles && ok; ++jt) {
-                const bool more = jt + 1 < ntiles;
-                if (!wait(&vfull[jt % kVStages], static_cast<uint32_t>(jt / kVStages) & 1u)) break;
-                if (!wait(&pfull[0], static_cast<uint32_t>(jt & 1))) break;
+                issue_s(0, n);
+                if (!wait(&qfull[1], static_cast<uint32_t>(k & 1))) break;
                 tc_fence_after();
-                issue_pv(0, jt);
-                if (more) {
-                    if (!wait(&kfull[(jt + 1) % kKStages], static_cast<uint32_t>((jt + 1) / kKStages) & 1u)) break;
+                issue_s(1, n);
+                umma_commit(&kempty[n % kKStages]);
+                for (int j = 0; j < nt && ok; ++j, ++n) {
+                    const bool more = j + 1 < nt;
+                    if (!wait(&vfull[n % kVStages], static_cast<uint32_t>(n / kVStages) & 1u)) break;
+                    if (!wait(&pfull[0], static_cast<uint32_t>(n & 1))) break;
+                    if (j == 0 && k > 0 && !wait(&ofree[0], static_cast<uint32_t>((k - 1) & 1))) break;
                     tc_fence_after();
-                    issue_s(0, jt + 1);
-                }
-                if (!wait(&pfull[1], static_cast<uint32_t>(jt & 1))) break;
-                tc_fence_after();
-                issue_pv(1, jt);
-                umma_commit(&vempty[jt % kVStages]);
-                if (more) {
-                    issue_s(1, jt + 1);
-                    umma_commit(&kempty[(jt + 1) % kKStages]);
+                    issue_pv(0, n, j == 0);
+                    if (more) {
+                        if (!wait(&kfull[(n + 1) % kKStages], static_cast<uint32_t>((n + 1) / kKStages) & 1u)) break;
+                        tc_fence_after();
+                        issue_s(0, n + 1);
+                    }
+                    if (!wait(&pfull[1], static_cast<uint32_t>(n & 1))) break;
+                    if (j == 0 && k > 0 && !wait(&ofree[1], static_cast<uint32_t>((k - 1) & 1))) break;
+                    tc_fence_after();
+                    issue_pv(1, n, j == 0);
+                    umma_commit(&vempty[n % kVStages]);
+                    if (more) {
+                        issue_s(1, n + 1);
+                        umma_commit(&kempty[(n + 1) % kKStages]);
+                    }
                 }
             }
             if (!ok) {
@@ -388,156 +395,227 @@ __global__ void __launch_bounds__(kWThreads, 1)
     } else {
         // ------------------------------------------------------------ softmax warpgroups
         // warps 2-5: query tile 0, warps 6-9: query tile 1; thread = row (TMEM lane).
-        // last visible key: the row's own position, and never past its item's key range
-        const int qlim = live ? min(p.tok_pos[tok0 + t_row], kend_t - 1) : -1;
+        const int tile = warp >= 6 ? 1 : 0;
+        const int q4 = warp & 3;
+        const int r = 32 * q4 + lane;
+        const int t_row = r / g, jh = r % g;
         const uint32_t trow = tmem + (static_cast<uint32_t>(32 * q4) << 16);
         const uint32_t tS = trow + tile * kWKeys;      // S_t, and P_t in its first 64 columns
         const uint32_t tO = trow + kColO + tile * kWD;  // O_t
-        float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int jt = 0; jt < ntiles; ++jt) {
-            const int kbase = jt * kWKeys;
-            const bool got = mbar_wait_bounded(&sfull[tile], static_cast<uint32_t>(jt & 1));
-            if (!__all_sync(0xffffffffu, got) || *abort_flag) {
-                ok = false;
-                break;
+        int n = 0;  // running key-tile count
+        for (int si = s_begin; si < s_end; ++si) {
+            const Seg sg = load_seg(p.seg, si);
+            const int k = si - s_begin;
+            const int h = sg.head;
+            const int item = p.w_pair[2 * sg.pair + tile];
+            const int ntok = item >= 0 ? p.w_ntok[item] : 0;
+            const int tok0 = item >= 0 ? p.w_tok0[item] : 0;
+            const int kend_t = item >= 0 ? p.w_kend[item] : 0;
+            const int kv_end = p.pair_kend[sg.pair];
+            const int last_tile = (kv_end + kWKeys - 1) / kWKeys - 1;
+            const bool live = t_row < ntok;
+            // last visible key: the row's own position, and never past its item's key range
+            const int qlim = live ? min(p.tok_pos[tok0 + t_row], kend_t - 1) : -1;
+            const int orow = p.tok_row[tok0 + (live ? t_row : 0)];
+            const size_t oidx = static_cast<size_t>(orow) * p.H + h * g + jh;
+            // ---- Q_t -> shared memory: scaled into the exp2 domain, bf16, [chunk][row][64] SW128
+            // (the previous segment's S MMAs, the only readers, have completed: their
+            // sfull phases were consumed below)
+            {
+                // Warp-cooperative and coalesced: the warp's 32 rows, 16 at a time, one 512-byte
+                // row per load instruction (lane = 4 dims), all 16 loads in flight together.
+                uint8_t* qs = smem + kOffQ + tile * kQBytes;
+                const int c = lane >> 4, u = (lane & 15) >> 1, half = lane & 1;
+#pragma unroll 1
+                for (int i0 = 0; i0 < 32; i0 += 16) {
+                    float4 x[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int rowi = __shfl_sync(0xffffffffu, orow, i0 + i);
+                        const bool livei = __shfl_sync(0xffffffffu, live ? 1 : 0, i0 + i) != 0;
+                        const float* qp = p.q + (static_cast<size_t>(rowi) * p.H + h * g + (32 * q4 + i0 + i) % g) * kWD;
+                        x[i] = livei ? __ldg(reinterpret_cast<const float4*>(qp) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const uint2 v = make_uint2(pack_bf16(x[i].x * p.qscale, x[i].y * p.qscale),
+                                                   pack_bf16(x[i].z * p.qscale, x[i].w * p.qscale));
+                        *reinterpret_cast<uint2*>(qs + c * (kWRows * 128) + sw128(32 * q4 + i0 + i, u) + half * 8) = v;
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&qfull[tile]);
             }
-            tc_fence_after();
-            float sv[kWKeys];
-#pragma unroll
-            for (int c = 0; c < kWKeys / 32; ++c) tmem_ld32(tS + c * 32, sv + c * 32);
-            tmem_wait_ld();
-            // mask by absolute position, only on tiles that reach past this row's limit
-            // (earlier tiles are fully visible; dead rows mask everything)
-            if (kbase + kWKeys - 1 > qlim) {
-#pragma unroll
-                for (int i = 0; i < kWKeys; ++i)
-                    if (kbase + i > qlim) sv[i] = -INFINITY;
-            }
-            // row max as 8 independent chains
-            float mx8[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                mx8[k] = sv[k];
-#pragma unroll
-                for (int i = k + 8; i < kWKeys; i += 8) mx8[k] = fmaxf(mx8[k], sv[i]);
-            }
-            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-            // Lazy rescale: keep the exponent base of earlier tiles unless this tile's max
-            // exceeds it by more than 8 (P stays <= 2^8 in bf16, l and O in fp32), so O in
-            // TMEM is rescaled only when the base actually moves.
-            const float mnew = (m == -INFINITY || mx > m + 8.f) ? mx : m;
-            const float base = mnew == -INFINITY ? 0.f : mnew;
-            const float corr = m == -INFINITY ? 0.f : ex2_approx(m - base);
-            if (jt >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
-                // O must include P.V(jt-1) before it is rescaled
-                const bool done = mbar_wait_bounded(&pvdone[tile], static_cast<uint32_t>((jt - 1) & 1));
-                if (!__all_sync(0xffffffffu, done) || *abort_flag) {
+            float m = -INFINITY, l = 0.f;
+            for (int jt = sg.t0; jt < sg.t1 && ok; ++jt, ++n) {
+                const int kbase = jt * kWKeys;
+                const bool got = mbar_wait_bounded(&sfull[tile], static_cast<uint32_t>(n & 1));
+                if (!__all_sync(0xffffffffu, got) || *abort_flag) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                float sv[kWKeys];
+#pragma unroll
+                for (int c = 0; c < kWKeys / 32; ++c) tmem_ld32(tS + c * 32, sv + c * 32);
+                tmem_wait_ld();
+                // mask by absolute position, only on tiles that reach past this row's limit
+                // (earlier tiles are fully visible; dead rows mask everything)
+                if (kbase + kWKeys - 1 > qlim) {
+#pragma unroll
+                    for (int i = 0; i < kWKeys; ++i)
+                        if (kbase + i > qlim) sv[i] = -INFINITY;
+                }
+                // row max as 8 independent chains
+                float mx8[8];
+#pragma unroll
+                for (int kq = 0; kq < 8; ++kq) {
+                    mx8[kq] = sv[kq];
+#pragma unroll
+                    for (int i = kq + 8; i < kWKeys; i += 8) mx8[kq] = fmaxf(mx8[kq], sv[i]);
+                }
+                const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                // Lazy rescale: keep the exponent base of earlier tiles unless this tile's max
+                // exceeds it by more than 8 (P stays <= 2^8 in bf16, l and O in fp32), so O in
+                // TMEM is rescaled only when the base actually moves.
+                const float mnew = (m == -INFINITY || mx > m + 8.f) ? mx : m;
+                const float base = mnew == -INFINITY ? 0.f : mnew;
+                const float corr = m == -INFINITY ? 0.f : ex2_approx(m - base);
+                if (jt > sg.t0 && __any_sync(0xffffffffu, corr != 1.f)) {
+                    // O must include P.V of the previous tile before it is rescaled
+                    const bool done = mbar_wait_bounded(&pvdone[tile], static_cast<uint32_t>((n - 1) & 1));
+                    if (!__all_sync(0xffffffffu, done) || *abort_flag) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c = 0; c < kWD / 32; ++c) {
+                        float o[32];
+                        tmem_ld32(tO + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= corr;
+                        tmem_st32(tO + c * 32, o);
+                    }
+                    tmem_wait_st();
+                }
+                // P = 2^(S - base) as bf16 pairs over S's first 64 columns (all of S is in
+                // registers already), 64 keys at a time
+                float sum8[8];
+#pragma unroll
+                for (int kq = 0; kq < 8; ++kq) sum8[kq] = 0.f;
+#pragma unroll
+                for (int half = 0; half < kWKeys / 64; ++half) {
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float a = ex2_approx(sv[half * 64 + 2 * i] - base);
+                        const float b = ex2_approx(sv[half * 64 + 2 * i + 1] - base);
+                        sum8[i & 7] += a + b;
+                        pk[i] = pack_bf16(a, b);
+                    }
+                    tmem_st32u(tS + half * 32, pk);
+                }
+                tmem_wait_st();
+                l = l * corr + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
+                m = mnew;
+                if (tile == 0 && jt == last_tile && kv_end < kbase + kWKeys) {
+                    // keys past the context in the last tile: zero their V rows so P = 0 meets 0
+                    // (tile 0's P.V is issued first, so tile 1's sees the zeros too)
+                    const int s = n % kVStages;
+                    const bool landed = mbar_wait_bounded(&vfull[s], static_cast<uint32_t>(n / kVStages) & 1u);
+                    if (!__all_sync(0xffffffffu, landed)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* vd = smem + kOffV + s * kKVBytes;
+                    const int first = kv_end - kbase;
+                    const int units = (kWKeys - first) * 2 * 8;
+                    for (int x = threadIdx.x - 64; x < units; x += 128) {
+                        const int key = first + x / 16;
+                        const int c = (x / 8) & 1;
+                        *reinterpret_cast<uint4*>(vd + c * (kWKeys * 128) + sw128(key, x & 7)) = make_uint4(0, 0, 0, 0);
+                    }
+                    fence_proxy_async_smem();  // the zeroed V rows (generic writes) before the MMA reads them
+                }
+                tc_fence_before();
+                // one arrival per warp (count 4): the MMA starts once all rows of P_t are written
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pfull[tile]);
+            }
+            if (ok) {
+                const bool done = mbar_wait_bounded(&pvdone[tile], static_cast<uint32_t>((n - 1) & 1));
+                ok = __all_sync(0xffffffffu, done) && !*abort_flag;
+            }
+            // ---- epilogue
+            if (ok) tc_fence_after();
+            if (sg.slot < 0) {
+                // Final rows: o / l, or, in the shared-prefix pass, merged with the row the
+                // split-KV kernel wrote (normalised, log-sum-exp lse_s):
+                //   (o * 2^(m-M) + out * 2^(lse_s-M)) / (l * 2^(m-M) + 2^(lse_s-M)).
+                float wo = l > 0.f ? 1.f / l : 0.f, wr = 0.f;
+                if (ok && p.lse != nullptr && live) {
+                    const float ls = p.lse[oidx];
+                    const float mm = fmaxf(l > 0.f ? m : -INFINITY, ls);
+                    const float a = l > 0.f ? exp2f(m - mm) : 0.f;
+                    const float b = exp2f(ls - mm);
+                    const float inv = 1.f / (l * a + b);
+                    wo = a * inv;
+                    wr = b * inv;
+                }
+                float* op = p.out + oidx * kWD;
+#pragma unroll 1
+                for (int c = 0; c < kWD / 32 && ok; ++c) {
+                    float4 y[8];
+                    if (p.lse != nullptr && live) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) y[i] = *reinterpret_cast<const float4*>(op + c * 32 + 4 * i);
+                    }
+                    float o[32];
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_wait_ld();
+                    if (live) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            float4 x = make_float4(o[4 * i] * wo, o[4 * i + 1] * wo, o[4 * i + 2] * wo, o[4 * i + 3] * wo);
+                            if (p.lse != nullptr) {
+                                x.x += y[i].x * wr;
+                                x.y += y[i].y * wr;
+                                x.z += y[i].z * wr;
+                                x.w += y[i].w * wr;
+                            }
+                            *reinterpret_cast<float4*>(op + c * 32 + 4 * i) = x;
+                        }
+                    }
+                }
+            } else if (ok) {
+                // Partial: un-normalised O and (max, sum) of this row into the pair-head's
+                // slot; wide_merge_kernel combines the slots afterwards.
+                const size_t prow = (static_cast<size_t>(sg.slot) * 2 + tile) * kWRows + r;
+                float* po = p.part_o + prow * kWD;
 #pragma unroll 1
                 for (int c = 0; c < kWD / 32; ++c) {
                     float o[32];
                     tmem_ld32(tO + c * 32, o);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= corr;
-                    tmem_st32(tO + c * 32, o);
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(po + c * 32 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
                 }
-                tmem_wait_st();
-            }
-            // P = 2^(S - base) as bf16 pairs over S's first 64 columns (all of S is in
-            // registers already), 64 keys at a time
-            float sum8[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) sum8[k] = 0.f;
-#pragma unroll
-            for (int half = 0; half < kWKeys / 64; ++half) {
-                uint32_t pk[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float a = ex2_approx(sv[half * 64 + 2 * i] - base);
-                    const float b = ex2_approx(sv[half * 64 + 2 * i + 1] - base);
-                    sum8[i & 7] += a + b;
-                    pk[i] = pack_bf16(a, b);
-                }
-                tmem_st32u(tS + half * 32, pk);
-            }
-            tmem_wait_st();
-            l = l * corr + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
-            m = mnew;
-            if (tile == 0 && jt == ntiles - 1 && kv_end < kbase + kWKeys) {
-                // keys past the context in the last tile: zero their V rows so P = 0 meets 0
-                // (tile 0's P.V is issued first, so tile 1's sees the zeros too)
-                const int s = jt % kVStages;
-                const bool landed = mbar_wait_bounded(&vfull[s], static_cast<uint32_t>(jt / kVStages) & 1u);
-                if (!__all_sync(0xffffffffu, landed)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t* vd = smem + kOffV + s * kKVBytes;
-                const int first = kv_end - kbase;
-                const int units = (kWKeys - first) * 2 * 8;
-                for (int x = threadIdx.x - 64; x < units; x += 128) {
-                    const int key = first + x / 16;
-                    const int c = (x / 8) & 1;
-                    *reinterpret_cast<uint4*>(vd + c * (kWKeys * 128) + sw128(key, x & 7)) = make_uint4(0, 0, 0, 0);
-                }
-                fence_proxy_async_smem();  // the zeroed V rows (generic writes) before the MMA reads them
+                p.part_ml[prow * 2] = m;
+                p.part_ml[prow * 2 + 1] = l;
             }
             tc_fence_before();
-            // one arrival per warp (count 4): the MMA starts once all rows of P_t are written
             __syncwarp();
-            if (lane == 0) mbar_arrive(&pfull[tile]);
-        }
-        if (ok && ntiles > 0) {
-            const bool done = mbar_wait_bounded(&pvdone[tile], static_cast<uint32_t>((ntiles - 1) & 1));
-            ok = __all_sync(0xffffffffu, done) && !*abort_flag;
+            if (lane == 0) mbar_arrive(&ofree[tile]);
         }
         if (!ok) {
             *abort_flag = 1;
             if (lane == 0) atomicExch(p.err, kErrTimeout);
-        } else if (ntok > 0) {
-            tc_fence_after();
-            const int orow = p.tok_row[tok0 + (live ? t_row : 0)];
-            const size_t oidx = static_cast<size_t>(orow) * p.H + h * g + jh;
-            float* op = p.out + oidx * kWD;
-            // This partial is o / l with log-sum-exp m + log2(l). Shared-prefix pass: the row
-            // already holds the rest of the sequence's keys, normalised, with log-sum-exp
-            // lse_s; the merged row is (o * 2^(m-M) + out * 2^(lse_s-M)) / (l * 2^(m-M) + 2^(lse_s-M)).
-            float wo = l > 0.f ? 1.f / l : 0.f, wr = 0.f;
-            if (p.lse != nullptr && live) {
-                const float ls = p.lse[oidx];
-                const float mm = fmaxf(l > 0.f ? m : -INFINITY, ls);
-                const float a = l > 0.f ? exp2f(m - mm) : 0.f;
-                const float b = exp2f(ls - mm);
-                const float inv = 1.f / (l * a + b);
-                wo = a * inv;
-                wr = b * inv;
-            }
-#pragma unroll 1
-            for (int c = 0; c < kWD / 32; ++c) {
-                float o[32];
-                tmem_ld32(tO + c * 32, o);
-                tmem_wait_ld();
-                if (live) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        float4 x = make_float4(o[i] * wo, o[i + 1] * wo, o[i + 2] * wo, o[i + 3] * wo);
-                        if (p.lse != nullptr) {
-                            const float4 y = *reinterpret_cast<const float4*>(op + c * 32 + i);
-                            x.x += y.x * wr;
-                            x.y += y.y * wr;
-                            x.z += y.z * wr;
-                            x.w += y.w * wr;
-                        }
-                        *reinterpret_cast<float4*>(op + c * 32 + i) = x;
-                    }
-                }
-            }
         }
     }
     tc_fence_before();
@@ -548,16 +626,73 @@ __global__ void __launch_bounds__(kWThreads, 1)
     }
 }
 
+// One warp per row of a (pair, KV head) cut between CTAs: combines the row's partial slots
+// (slot order, so the result does not depend on which CTA finished first) and, in the
+// shared-prefix pass, the row the split-KV kernel wrote. Lane = 4 dims: coalesced.
+__global__ void __launch_bounds__(256) wide_merge_kernel(const WideParams p, const int32_t* split, int nsplit) {
+    const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int e = wid / (2 * kWRows);
+    if (e >= nsplit) return;
+    const int tile = (wid / kWRows) & 1, r = wid % kWRows;
+    const int pair = split[4 * e], h = split[4 * e + 1], s0 = split[4 * e + 2], ns = split[4 * e + 3];
+    const int item = p.w_pair[2 * pair + tile];
+    if (item < 0) return;
+    const int g = p.g;
+    const int t = r / g, j = r % g;
+    if (t >= p.w_ntok[item]) return;
+    const size_t oidx = static_cast<size_t>(p.tok_row[p.w_tok0[item] + t]) * p.H + h * g + j;
+    auto ml = [&](int s) { return p.part_ml + ((static_cast<size_t>(s) * 2 + tile) * kWRows + r) * 2; };
+    float mx = -INFINITY;
+    for (int s = s0 + lane; s < s0 + ns; s += 32) mx = fmaxf(mx, ml(s)[0]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = s0; s < s0 + ns; ++s) {
+        const float ms = ml(s)[0], ls = ml(s)[1];
+        const float w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
+        const float4 x = reinterpret_cast<const float4*>(p.part_o + ((static_cast<size_t>(s) * 2 + tile) * kWRows + r) * kWD)[lane];
+        L += w * ls;
+        acc.x += w * x.x;
+        acc.y += w * x.y;
+        acc.z += w * x.z;
+        acc.w += w * x.w;
+    }
+    float4* op = reinterpret_cast<float4*>(p.out + oidx * kWD) + lane;
+    float wo = L > 0.f ? 1.f / L : 0.f, wr = 0.f;
+    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p.lse != nullptr) {
+        // merge with the split-KV result: (acc * 2^(mx-M) + y * 2^(lse_s-M)) / (L * 2^(mx-M) + 2^(lse_s-M))
+        const float ls = p.lse[oidx];
+        const float mm = fmaxf(L > 0.f ? mx : -INFINITY, ls);
+        const float a = L > 0.f ? exp2f(mx - mm) : 0.f;
+        const float b = exp2f(ls - mm);
+        const float inv = 1.f / (L * a + b);
+        wo = a * inv;
+        wr = b * inv;
+        y = *op;
+    }
+    *op = make_float4(acc.x * wo + y.x * wr, acc.y * wo + y.y * wr, acc.z * wo + y.z * wr, acc.w * wo + y.w * wr);
+}
+
 }  // namespace
 
 size_t wide_smem_bytes() { return kSmemBytes; }
 
+cudaError_t launch_wide_merge(const WideParams& p, const int32_t* split, int nsplit, cudaStream_t st) {
+    if (nsplit <= 0) return cudaSuccess;
+    const int warps = nsplit * 2 * kWRows;
+    wide_merge_kernel<<<(warps + 7) / 8, 256, 0, st>>>(p, split, nsplit);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tmv1, const WideParams& p,
                                   cudaStream_t st) {
-    if (p.npairs <= 0) return cudaSuccess;
+    if (p.nctas <= 0) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(wide_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    wide_attn_kernel<<<dim3(p.npairs, p.kvh), kWThreads, kSmemBytes, st>>>(*tmk1, *tmv1, p);
+    wide_attn_kernel<<<p.nctas, kWThreads, kSmemBytes, st>>>(*tmk1, *tmv1, p);
     return cudaGetLastError();
 }
 

@@ -114,8 +114,13 @@ struct WideParams {
     // Shared-prefix pass: NULL = write the normalised output; else merge this partial with
     // the output row already written (and its log2-domain log-sum-exp [rows][H] here).
     const float* lse;
-    const int32_t* w_pair;  // [npairs][2] items of each CTA (second = -1: none), same table
-    int npairs;
+    const int32_t* w_pair;     // [pairs][2] items of a pair (second = -1: none), same table
+    const int32_t* pair_kend;  // [pairs] keys of the pair (the larger kend of its items)
+    const int32_t* cta_seg;    // [nctas+1] this launch's CTAs: segment ranges
+    const int32_t* seg;        // [segments][6] pair, head, first/end key tile, slot (-1 whole), pair-head
+    float* part_o;             // [slots][2][128][128] un-normalised partial O
+    float* part_ml;            // [slots][2][128][2] (max, sum), log2 domain
+    int nctas;
     int H;
     int kvh;
     int g;
@@ -149,6 +154,9 @@ cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st);
 size_t wide_smem_bytes();
 cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tmv1, const WideParams& p,
                                   cudaStream_t st);
+// Combines the partial slots of (pair, head)s cut between wide-kernel CTAs:
+// split = [nsplit][4] pair, head, first slot, slots.
+cudaError_t launch_wide_merge(const WideParams& p, const int32_t* split, int nsplit, cudaStream_t st);
 // Same merge as a programmatic dependent launch of the preceding attention kernel.
 cudaError_t launch_merge_dependent(const MergeParams& p, int nsplit, cudaStream_t st);
 cudaError_t launch_generic_attention(int dtype, const GenericParams& p, cudaStream_t st);
