@@ -136,9 +136,10 @@ PK_API int pk_batch_stats(const pk_batch* batch, int64_t* stats8);
  * for the rest of each sequence. `mode`: 0 off, 1 (default) where a cost estimate says it
  * is faster than reading the prefix once per sequence, 2 for every eligible group; it
  * applies from the next plan. pk_batch_prefix_stats: [0] prefix groups, [1] shared-prefix
- * work items, [2] shared keys summed over the groups. */
+ * work items, [2] shared keys summed over the groups, [3] sum over the groups of
+ * (query tokens x shared keys), the work the shared-prefix pass does per query head. */
 PK_API int pk_batch_set_prefix_sharing(pk_batch* batch, int mode);
-PK_API int pk_batch_prefix_stats(const pk_batch* batch, int64_t* stats3);
+PK_API int pk_batch_prefix_stats(const pk_batch* batch, int64_t* stats4);
 
 /* Per-kernel timing of this batch's own launches: with profiling on, CUDA events are
  * recorded on the launching stream around every kernel. pk_batch_profile_read synchronises

@@ -357,9 +357,9 @@ class PagedBatch:
         self._prefix_sharing = ("off", "auto", "always")[code]
 
     def prefix_stats(self) -> dict:
-        s = (C.c_int64 * 3)()
+        s = (C.c_int64 * 4)()
         _lib.check(self._lib.pk_batch_prefix_stats(self._b, s))
-        return dict(zip(("groups", "items", "shared_keys"), list(s)))
+        return dict(zip(("groups", "items", "shared_keys", "token_keys"), list(s)))
 
     # ------------------------------------------------------------------ per layer
     def write_and_attend(self, layer: int, q, k, v):

@@ -218,6 +218,7 @@ struct pk_batch {
     // nprefix) shared-prefix items (after the split-KV kernel, merged into its rows).
     int nwide = 0, nprefix = 0, nprefix_groups = 0;
     int64_t prefix_keys = 0;  // shared keys summed over the prefix groups
+    int64_t prefix_token_keys = 0;  // sum over the groups of query tokens x shared keys
     int prefix_sharing = 1;   // 0 off, 1 where the cost estimate favours it, 2 always
     std::vector<int32_t> w_seq, w_tok0, w_ntok, w_kend, tok_row, tok_pos;
     std::vector<int32_t> w_rows;   // rows of chunk items (appended separately)
@@ -462,6 +463,7 @@ void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>
                     if (fill > 0) close_item();
                     B->nprefix_groups++;
                     B->prefix_keys += keys;
+                    B->prefix_token_keys += toks * keys;
                 }
             }
         }
@@ -572,7 +574,7 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->w_seq.clear(); B->w_tok0.clear(); B->w_ntok.clear(); B->w_kend.clear();
     B->tok_row.clear(); B->tok_pos.clear(); B->w_rows.clear(); B->u_kb0.clear();
     B->nwide = B->nprefix = B->nprefix_groups = 0;
-    B->prefix_keys = 0;
+    B->prefix_keys = B->prefix_token_keys = 0;
     B->seq_kb0.assign(B->nseq, 0);
     const bool wide_ok = P->wide_ok && g <= 128 && 128 % g == 0;
     const int tpt = wide_ok ? 128 / g : 0;  // query tokens per wide item
@@ -1383,6 +1385,7 @@ int pk_batch_prefix_stats(const pk_batch* B, int64_t* s) {
     s[0] = B->nprefix_groups;
     s[1] = B->nprefix;
     s[2] = B->prefix_keys;
+    s[3] = B->prefix_token_keys;
     return PK_OK;
 }
 

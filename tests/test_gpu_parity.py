@@ -447,10 +447,10 @@ def test_shared_prefix_forks_match_oracle(mode):
     b.check()
     ps = b.prefix_stats()
     if mode == "off":
-        assert ps == {"groups": 0, "items": 0, "shared_keys": 0}
+        assert ps == {"groups": 0, "items": 0, "shared_keys": 0, "token_keys": 0}
     else:
         # 16 forks x 5 tokens x g=4 rows = 320 rows -> 3 items of 128 rows
-        assert ps == {"groups": 1, "items": 3, "shared_keys": 2048}, ps
+        assert ps == {"groups": 1, "items": 3, "shared_keys": 2048, "token_keys": 80 * 2048}, ps
     got, qh = out.cpu().numpy(), q.cpu().numpy()
     for i, (rows, ref) in oracle_rows(pool, w, range(w.nseq), qh).items():
         _close(got[rows], ref, True)
