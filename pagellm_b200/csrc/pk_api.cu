@@ -174,6 +174,8 @@ struct pk_pool {
     int tc_per_head = 0;
     int tc_stages = 0;
     size_t tc_smem = 0;
+    int tc_ctas_per_sm = 1;  // split-KV CTAs meant to share an SM (few KV heads per pool)
+    int tc_occ[3] = {0, 0, 0};  // cached CTAs per SM that fit, per NT (1, 2)
     std::string tc_why;
     CUtensorMap tmk{};
     CUtensorMap tmv{};
@@ -336,11 +338,21 @@ void setup_tc(pk_pool* P) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, P->device);
     const size_t stage = static_cast<size_t>(2) * P->block_size * P->kvh * P->d * 2;
-    // As many stages as fit in ~200 KB (at most 8): small tiles (few KV heads per GPU in the
-    // head-sharded layout) need more of them to keep enough bytes in flight per SM.
-    int stages = 8;
-    const size_t budget = std::min<size_t>(static_cast<size_t>(optin), size_t(200) << 10);
-    while (stages >= 2 && pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages) > budget) --stages;
+    // A CTA has one consumer warp per KV head. With few KV heads (the head-sharded layout
+    // gives 1-4 per GPU) one CTA per SM would leave most of the SM idle, so 8 / kvh CTAs share
+    // an SM, each with its share of shared memory; stages: as many as fit (at most 8).
+    int per_sm = 0;
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, P->device);
+    // Several CTAs per SM only while each still gets >= 3 stages (else fewer CTAs per SM).
+    int stages = 0;
+    for (int k = std::max(1, pk::kTcMaxKvHeads / P->kvh); k >= 1; --k) {
+        size_t budget = std::min<size_t>(static_cast<size_t>(optin), size_t(200) << 10);
+        if (k > 1 && per_sm > 0) budget = std::min<size_t>(budget, static_cast<size_t>(per_sm) / k - 1024);
+        stages = 8;
+        while (stages >= 2 && pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages) > budget) --stages;
+        P->tc_ctas_per_sm = k;
+        if (stages >= 3 || k == 1) break;
+    }
     (void)stage;
     if (stages < 2) return no("K/V block too large for two shared-memory stages");
     std::string why;
@@ -663,7 +675,10 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         B->total_blocks = static_cast<int>(T);
         // On small steps more CTAs would cut every unit into many partials whose merge
         // outweighs the bandwidth the extra SMs add.
-        B->ncta = static_cast<int>(split_kv_ctas(T, B->nu, P->num_sms));
+        int& occ = P->tc_occ[std::min(B->nt, 2)];
+        if (occ == 0) occ = pk::tc_max_active_ctas(P->d, B->nt, P->kvh, P->tc_smem);
+        const int per_sm = std::max(1, std::min(P->tc_ctas_per_sm, occ));
+        B->ncta = static_cast<int>(split_kv_ctas(T, B->nu, static_cast<int64_t>(P->num_sms) * per_sm));
         for (int u = 0; u < B->nu; ++u) {
             const int c0 = cta_of_block(B->u_blk[u], T, B->ncta);
             const int c1 = cta_of_block(B->u_blk[u + 1] - 1, T, B->ncta);

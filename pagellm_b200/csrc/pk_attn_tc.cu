@@ -616,6 +616,26 @@ cudaError_t launch_tc_t(const CUtensorMap* tmk, const CUtensorMap* tmv, const Tc
 
 }  // namespace
 
+template <int D, int NT>
+int max_active_t(int kvh, size_t smem) {
+    int n = 0;
+    if (cudaFuncSetAttribute(tc_attn_kernel<D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, tc_attn_kernel<D, NT>, (kvh + 1) * 32, smem) != cudaSuccess)
+        return 1;
+    return n;
+}
+
+int tc_max_active_ctas(int D, int NT, int kvh, size_t smem) {
+    if (D == 64 && NT == 1) return max_active_t<64, 1>(kvh, smem);
+    if (D == 64 && NT == 2) return max_active_t<64, 2>(kvh, smem);
+    if (D == 128 && NT == 1) return max_active_t<128, 1>(kvh, smem);
+    if (D == 128 && NT == 2) return max_active_t<128, 2>(kvh, smem);
+    if (D == 256 && NT == 1) return max_active_t<256, 1>(kvh, smem);
+    return 1;
+}
+
 size_t tc_smem_bytes(int D, int bs, int kvh, int stages) {
     return static_cast<size_t>(stages) * 2 * bs * kvh * D * 2 + 2 * stages * sizeof(uint64_t) + 1024;
 }

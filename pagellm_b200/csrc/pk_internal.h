@@ -150,6 +150,8 @@ struct PoolView {
 cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUtensorMap* tmv,
                                 const TcParams& p, size_t smem, cudaStream_t st);
 size_t tc_smem_bytes(int D, int bs, int kvh, int stages);
+// How many split-KV CTAs of this shape fit on one SM (registers, shared memory, threads).
+int tc_max_active_ctas(int D, int NT, int kvh, size_t smem);
 cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st);
 size_t wide_smem_bytes();
 cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tmv1, const WideParams& p,

@@ -187,8 +187,11 @@ def test_c5_long_context_shard():
 
 
 def test_c5_head_sharded_shard_matches_full():
-    """Head-sharded variant: a rank holding KV heads [h0, h0+kh) computes exactly the
-    full computation's output for query heads [h0*g, (h0+kh)*g)."""
+    """Head-sharded variant: a rank holding KV heads [h0, h0+kh) computes the full
+    computation's output for query heads [h0*g, (h0+kh)*g). Not bit for bit: a pool with
+    fewer KV heads runs several split-KV CTAs per SM, so the split points differ, and with
+    them the running max each partial rounds its bf16 P against; the difference stays an
+    order of magnitude inside the bf16 tolerance."""
     torch = torch_cuda()
     from pagellm_b200 import workloads
     from pagellm_b200.cache import PagedBatch
@@ -207,7 +210,8 @@ def test_c5_head_sharded_shard_matches_full():
         qs = q[:, h0 * g:(h0 + kh) * g].contiguous()
         ks, vs = k[:, h0:h0 + kh].contiguous(), v[:, h0:h0 + kh].contiguous()
         o = PagedBatch(sp, part.tables, part.starts, part.n_new).write_and_attend(0, qs, ks, vs)
-        assert torch.equal(o, out_full[:, h0 * g:(h0 + kh) * g])
+        ref = out_full[:, h0 * g:(h0 + kh) * g]
+        assert float((o - ref).abs().max()) <= BF16_ATOL / 10
 
 
 # ----------------------------------------------------------------------------- bit-exact ops
