@@ -234,6 +234,14 @@ PK_API int pk_bm_seq_push_hashes(pk_block_manager* m, int64_t seq, const uint8_t
                                  int64_t hash_len, int64_t count);
 /* BlockManager.fork (paged.py:257-263) and free (paged.py:265-271). */
 PK_API int pk_bm_fork(pk_block_manager* m, int64_t parent, int64_t child);
+/* Paged speculative rollback (no counterpart in pagellm's paged cache; pagellm rolls back
+ * contiguous caches only: cache/contiguous.py:33-38 truncate, engine/speculative.py:136-137;
+ * paged rollback is on its roadmap, README.md:370): keep the first n_tokens of a sequence.
+ * Blocks past them are released last block first (as free, cache/paged.py:265-271); the
+ * hash chain keeps the remaining full blocks; a kept partial last block published in the
+ * prefix cache and held by this sequence alone is unpublished (its next writes change it).
+ * n_tokens outside [0, blocks * block_size] -> PK_ERR_INVALID_ARG. */
+PK_API int pk_bm_truncate(pk_block_manager* m, int64_t seq, int64_t n_tokens);
 PK_API int pk_bm_free_seq(pk_block_manager* m, int64_t seq);
 /* BlockManager.block_table (paged.py:273-274); sequence ids with a table. */
 PK_API int pk_bm_table(const pk_block_manager* m, int64_t seq, int32_t* out, int64_t cap,

@@ -422,5 +422,25 @@ class OracleBlockManager:
         for b in reversed(t):
             self.alloc.decref(b)
 
+    def truncate(self, seq_id: int, num_tokens: int) -> None:
+        """Paged speculative rollback, the paged form of pagellm's contiguous
+        ``KVCache.truncate`` (``cache/contiguous.py:33-38``; paged rollback is a pagellm
+        roadmap item, ``README.md:370``): keep the first ``num_tokens`` tokens; release the
+        blocks past them last first (as ``free``, ``:265-271``); keep the hashes of the full
+        blocks that remain; unpublish a kept partial last block that only this sequence
+        holds, because its next writes change it in place."""
+        t = self.blocks[seq_id]
+        bs = self.block_size
+        if not 0 <= num_tokens <= len(t) * bs:
+            raise ValueError(f"cannot truncate a {len(t) * bs}-token table to {num_tokens}")
+        keep, full = self.blocks_needed(num_tokens), num_tokens // bs
+        while len(t) > keep:
+            self.alloc.decref(t.pop())
+        del self.hashes[seq_id][full:]
+        if keep > full:
+            b = t[full]
+            if self.alloc.ref[b] == 1 and b in self.alloc.hash_of:
+                del self.alloc.block_of[self.alloc.hash_of.pop(b)]
+
     def block_table(self, seq_id: int) -> list[int]:
         return self.blocks[seq_id]

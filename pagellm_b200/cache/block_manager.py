@@ -321,6 +321,15 @@ class BlockManager:
     def free(self, seq_id: int) -> None:
         _ck(_L().pk_bm_free_seq(self._n.ptr, int(seq_id)))
 
+    def truncate(self, seq_id: int, num_tokens: int) -> None:
+        """Roll the sequence back to its first ``num_tokens`` tokens (rejected speculative
+        tokens): the paged form of pagellm's contiguous ``KVCache.truncate``
+        (cache/contiguous.py:33-38). Blocks past them go back to the allocator, last first;
+        the K/V left in the kept last block is overwritten by the next writes, which
+        ``ensure_capacity(seq, n, write_from=num_tokens)`` makes private first as usual.
+        ``ValueError`` if ``num_tokens`` is outside ``[0, blocks * block_size]``."""
+        _ck(_L().pk_bm_truncate(self._n.ptr, int(seq_id), int(num_tokens)))
+
     def block_table(self, seq_id: int) -> list[int]:
         return _ids_list(_L().pk_bm_table, self._n.ptr, int(seq_id))
 

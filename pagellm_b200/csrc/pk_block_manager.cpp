@@ -450,6 +450,41 @@ PK_API int pk_bm_free_seq(pk_block_manager* m, int64_t seq) {
     return PK_OK;
 }
 
+// Paged speculative rollback: keep the first n_tokens of a sequence. pagellm rolls back only
+// contiguous caches (cache/contiguous.py:33-38, engine/speculative.py:136-137; paged rollback
+// is on its roadmap, README.md:370); this is its paged form. Blocks past the kept tokens are
+// released last block first, as free does (paged.py:265-271); the hash chain keeps only the
+// full blocks that remain; a kept partial last block that is published in the prefix cache
+// and held by this sequence alone is unpublished, since the next writes change it in place
+// (a shared one is copied on write by ensure_capacity instead, so its content stays).
+PK_API int pk_bm_truncate(pk_block_manager* m, int64_t seq, int64_t n_tokens) {
+    if (!m) return bm_fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    SeqTable* t;
+    int rc = get_table(m, seq, &t);
+    if (rc) return rc;
+    const int64_t cap = static_cast<int64_t>(t->blocks.size()) * m->block_size;
+    if (n_tokens < 0 || n_tokens > cap)
+        return bm_fail(PK_ERR_INVALID_ARG, "cannot truncate a %lld-token table to %lld tokens", (long long)cap,
+                       (long long)n_tokens);
+    const int64_t keep = m->blocks_needed(n_tokens), full = n_tokens / m->block_size;
+    while (static_cast<int64_t>(t->blocks.size()) > keep) {
+        const int32_t b = t->blocks.back();
+        t->blocks.pop_back();
+        rc = m->decref(b);
+        if (rc) return rc;
+    }
+    if (static_cast<int64_t>(t->hashes.size()) > full) t->hashes.resize(full);
+    if (keep > full) {
+        const int32_t b = t->blocks[full];
+        if (m->ref[b] == 1 && m->has_hash[b]) {
+            m->cached.erase(m->hash_of[b]);
+            m->hash_of[b].clear();
+            m->has_hash[b] = 0;
+        }
+    }
+    return PK_OK;
+}
+
 PK_API int pk_bm_table(const pk_block_manager* m, int64_t seq, int32_t* out, int64_t cap, int64_t* n) {
     if (!m) return bm_fail(PK_ERR_INVALID_ARG, "NULL pointer");
     auto it = m->tables.find(seq);

@@ -523,6 +523,40 @@ def test_shared_prefix_groups_mixed_step(H, KVH, bs):
     assert float(np.max(np.abs(outs["always"] - outs["off"]))) < 5e-3
 
 
+def test_speculative_rollback_on_the_paged_pool():
+    """Verify 5 draft tokens, keep 2 (BlockManager.truncate), decode the next token: it sees
+    exactly the 23 kept positions; the rejected drafts' K/V left in the kept block are
+    neither attended nor leaked, and the new token overwrites the first rejected slot."""
+    torch = torch_cuda()
+    from pagellm_b200.cache import BlockManager, PagedBatch, PagedKVPool
+
+    H, KVH, bs = 8, 2, 16
+    bm = BlockManager(32, bs)
+    pool = PagedKVPool(Shape(1, KVH, 128), 32, bs, "bfloat16")
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    prompt = list(range(20))
+    bm.allocate(0, prompt)
+
+    def step(start, n):
+        bm.ensure_capacity(0, start + n, write_from=start)
+        q = torch.randn((n, H, 128), generator=gen, device="cuda")
+        k = torch.randn((n, KVH, 128), generator=gen, device="cuda")
+        v = torch.randn((n, KVH, 128), generator=gen, device="cuda")
+        b = PagedBatch(pool, [bm.block_table(0)], [start], [n])
+        out = b.write_and_attend(0, q, k, v)
+        b.check()
+        return q, out
+
+    step(0, 20)                  # prefill
+    step(20, 5)                  # verify window: drafts at 20..24
+    bm.truncate(0, 22)           # 2 accepted
+    assert len(bm.block_table(0)) == 2
+    q, out = step(22, 1)         # next token lands at 22
+    slots = po.slot_mapping(bm.block_table(0), np.arange(23), bs)
+    kc, vc = gather_rows(pool, 0, slots)
+    _close(out.cpu().numpy(), po.attention_dense(q.cpu().numpy(), kc, vc, 22), True)
+
+
 def test_bounded_wait_gives_up_and_context_survives():
     """Failure detection without a GPU fault: a wait on a barrier phase that nothing
     completes returns after its limit with an error status the host reads; the context
