@@ -223,7 +223,8 @@ def run_ours(args):
     def step():
         if head_mode:
             attend_layer()
-            gather_heads(out)
+            if world > 1:  # one rank holds every head: nothing to gather
+                gather_heads(out)
             return
         if pairs_dev is not None:  # the step's copy-on-write copies (fork of the shared block)
             rc = lib.pk_pool_copy_blocks_dev(pool.handle, pairs_dev.data_ptr(), len(pairs_dev), st)
@@ -292,7 +293,7 @@ def run_ours(args):
         a0.record(stream)
         for _ in range(e_steps):
             res = PagedBatch(pool, (indptr, ids), w.starts, w.n_new).write_and_attend(0, qn, kn, vn)
-            if head_mode:  # slices back to the GPU, all-gather, full output to the host
+            if head_mode and world > 1:  # slices back to the GPU, all-gather, full output to the host
                 res = gather_heads(torch.from_numpy(res).to(dev)).cpu().numpy()
         a1.record(stream)
         barrier()
