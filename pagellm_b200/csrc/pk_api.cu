@@ -1139,6 +1139,8 @@ int pk_batch_destroy(pk_batch* B) {
     B->ws.release();
     B->counters.release();
     B->io.release();
+    B->lse.release();
+    B->wpart.release();
     for (cudaEvent_t e : B->ev_pool) cudaEventDestroy(e);
     if (B->ev_fork) cudaEventDestroy(B->ev_fork);
     if (B->ev_join) cudaEventDestroy(B->ev_join);
