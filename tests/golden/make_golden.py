@@ -151,6 +151,53 @@ def step_cases():
     return res
 
 
+def fork_case():
+    """Forks over a shared prefix, C4's shape in small: one request's 100-token prompt is
+    prefilled, forked 4 ways (BlockManager.fork), each fork's ensure_capacity copy-on-writes
+    the shared partial block (PagedKVPool.copy_block), then one gather step verifies 5
+    tokens per fork. bf16-rounded K/V/q-independent data, Llama-3-8B attention shape."""
+    rng = np.random.default_rng(21)
+    H, KVH, d, bs, nb, P, forks, nv = 32, 8, 128, 16, 48, 100, 4, 5
+    cfg = ModelConfig(vocab_size=8, dim=H * d, n_layers=1, n_heads=H, n_kv_heads=KVH)
+    pool = PagedKVPool(cfg, nb, bs, np.float32)
+    bm = BlockManager(nb, bs)
+    prompt = [int(t) for t in rng.integers(0, 8, P)]
+    bm.allocate(0, prompt)
+    ctx_slots = slot_mapping(bm.block_table(0), np.arange(P), bs).astype(np.int64)
+    kc = bf16_round(rng.standard_normal((P, KVH, d)).astype(np.float32))
+    vc = bf16_round(rng.standard_normal((P, KVH, d)).astype(np.float32))
+    pool.k_flat[0, ctx_slots] = kc
+    pool.v_flat[0, ctx_slots] = vc
+    for f in range(1, forks):
+        bm.fork(0, f)
+    pairs = []
+    for f in range(forks):
+        for src, dst in bm.ensure_capacity(f, P + nv, write_from=P):
+            pool.copy_block(src, dst)
+            pairs.append((src, dst))
+    tables = [bm.block_table(f) for f in range(forks)]
+    N = forks * nv
+    q = rng.standard_normal((N, H, d)).astype(np.float32)
+    k = bf16_round(rng.standard_normal((N, KVH, d)).astype(np.float32))
+    v = bf16_round(rng.standard_normal((N, KVH, d)).astype(np.float32))
+    kv = PagedBatch(pool, tables, [P] * forks, [nv] * forks, "gather", True)
+    out = kv.write_and_attend(0, q, k, v)
+    bits = lambda a: (a.view(np.uint32) >> np.uint32(16)).astype(np.uint16)  # noqa: E731
+    return dict(
+        dims=np.array([H, KVH, d, bs, nb], np.int64),
+        indptr=np.concatenate([[0], np.cumsum([len(t) for t in tables])]).astype(np.int64),
+        ids=np.concatenate([np.asarray(t, np.int64) for t in tables]),
+        starts=np.full(forks, P, np.int64),
+        n_new=np.full(forks, nv, np.int64),
+        ctx_slots=ctx_slots,
+        cow_pairs=np.asarray(pairs, np.int64).reshape(-1, 2),
+        kc=bits(kc), vc=bits(vc), q=q, k=bits(k), v=bits(v),
+        positions=kv.positions,
+        slots=kv.slots,
+        out=out,
+    )
+
+
 def slot_cases():
     rng = np.random.default_rng(3)
     out = {}
@@ -239,6 +286,7 @@ def main():
     np.savez_compressed(HERE / "batched_decode.npz", **batched_decode_case())
     for name, case in step_cases().items():
         np.savez_compressed(HERE / f"step_{name}.npz", **case)
+    np.savez_compressed(HERE / "step_bf16_forks.npz", **fork_case())
     np.savez_compressed(HERE / "slot_mapping.npz", **slot_cases())
     traces = [
         allocator_trace(11, 24, 4, True, 300),

@@ -66,6 +66,30 @@ def test_golden_step(name):
     np.testing.assert_array_equal(vr, c["v"])
 
 
+@pytest.mark.parametrize("mode", ["always", "off"])
+def test_golden_fork_cow_verify(mode):
+    """pagellm's own fork + copy-on-write + 5-token verify step (step_bf16_forks.npz) on the
+    CUDA path: CoW copies through copy_blocks, then the step with the shared-prefix
+    (cascade) pass forced on, and off."""
+    torch = torch_cuda()
+    from pagellm_b200.cache import PagedBatch, PagedKVPool
+
+    z = load_npz("step_bf16_forks.npz")
+    c = step_inputs(z)
+    pool = PagedKVPool(Shape(1, c["KVH"], c["d"]), c["num_blocks"], c["bs"], "bfloat16")
+    idx = torch.as_tensor(c["ctx_slots"], device="cuda")
+    pool.k_flat[0].index_copy_(0, idx, torch.as_tensor(c["kc"], device="cuda").to(pool.k.dtype))
+    pool.v_flat[0].index_copy_(0, idx, torch.as_tensor(c["vc"], device="cuda").to(pool.v.dtype))
+    pool.copy_blocks([tuple(map(int, p)) for p in z["cow_pairs"]])
+    batch = PagedBatch(pool, c["tables"], c["starts"], c["n_new"], "gather")
+    batch.prefix_sharing = mode
+    np.testing.assert_array_equal(batch.slots, c["slots"])
+    out = batch.write_and_attend(0, c["q"], c["k"], c["v"])
+    batch.check()
+    assert batch.prefix_stats()["groups"] == (1 if mode == "always" else 0)
+    _close(out, c["out"], True)
+
+
 def test_golden_paged_attention_cases():
     from pagellm_b200.cache import paged_attention
 

@@ -64,6 +64,27 @@ def test_write_and_attend_step(name):
     np.testing.assert_array_equal(vf[c["slots"]], c["v"])
 
 
+def test_fork_cow_verify_step():
+    """pagellm's fork + copy-on-write + verify step (step_bf16_forks.npz): the recorded CoW
+    pairs replayed with the oracle's copy_blocks, then the step."""
+    z = load_npz("step_bf16_forks.npz")
+    c = step_inputs(z)
+    meta = po.StepMeta(c["tables"], c["starts"], c["n_new"], c["bs"], attn="gather")
+    np.testing.assert_array_equal(meta.positions, c["positions"])
+    np.testing.assert_array_equal(meta.slots, c["slots"])
+    kpool = np.zeros((c["num_blocks"], c["bs"], c["KVH"], c["d"]), np.float32)
+    vpool = np.zeros_like(kpool)
+    kf = kpool.reshape(-1, c["KVH"], c["d"])
+    vf = vpool.reshape(-1, c["KVH"], c["d"])
+    kf[c["ctx_slots"]] = c["kc"]
+    vf[c["ctx_slots"]] = c["vc"]
+    pairs = [tuple(map(int, p)) for p in z["cow_pairs"]]
+    assert len(pairs) == 3  # 4 forks: the first 3 writers copy, the last keeps the block
+    po.copy_blocks(kpool[None], vpool[None], pairs)
+    out = po.write_and_attend(kf, vf, meta, c["q"], c["k"], c["v"], kpool, vpool)
+    np.testing.assert_allclose(out, c["out"], rtol=1e-5, atol=1e-6)
+
+
 def test_bf16_round_is_rne():
     x = np.array([1.0, 1.00390625, 1.01171875, -2.5, 3.0e-3, 65504.0, 1.0 + 2 ** -8], np.float32)
     bits = po.bf16_bits(x)
