@@ -25,7 +25,8 @@
 // multicast) signalling mbarriers; consumers wait, compute, and release the stage.
 //
 // Per consumer warp and 16-token tile, with the transposed formulation (tokens as MMA rows):
-//   S^T[16 x 8*NT] = K[16 x D] . Q^T[D x 8*NT]     (Q split as bf16 hi + lo for accuracy)
+//   S^T[16 x 8*NT] = K[16 x D] . Q^T[D x 8*NT]     (Q split as bf16 hi + lo for accuracy
+//                                                   where registers allow: NT=1, D<=128)
 //   online softmax down the columns (exp2 domain, scale folded into Q)
 //   P^T -> bf16, transposed in registers with movmatrix into the B operand
 //   O^T[D x 8*NT] += V^T[D x 16] . P^T[16 x 8*NT]  (V^T read with ldmatrix.trans)
@@ -194,7 +195,11 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
         const int row0 = p.offsets[seq] + t0;
 
         // Q^T as the B operand: column n = lane/4 of each n8 tile, dims 2*quad(+1), +8.
-        uint32_t qh[KS][NT][2], ql[KS][NT][2];
+        // Q's low half (q - bf16(q)) only where registers allow it: with two n8 tiles or
+        // head_dim 256 the 168-register cap of a 9-warp CTA would spill it, so there Q is
+        // used at bf16 (the precision the wide-tile kernel uses throughout).
+        constexpr bool kLo = NT == 1 && D <= 128;
+        uint32_t qh[KS][NT][2], ql[kLo ? KS : 1][NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int col = nt * 8 + grp;
@@ -212,7 +217,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                     x.y *= p.qscale;
                     const uint32_t hb = pack_bf16(x.x, x.y);
                     qh[ks][nt][half] = hb;
-                    ql[ks][nt][half] = pack_bf16(x.x - bf16_lo_f(hb), x.y - bf16_hi_f(hb));
+                    if constexpr (kLo) ql[ks][nt][half] = pack_bf16(x.x - bf16_lo_f(hb), x.y - bf16_hi_f(hb));
                 }
             }
         }
@@ -339,7 +344,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
 #pragma unroll
                         for (int nt = 0; nt < NT; ++nt) {
                             mma_bf16_16816(sacc[nt], a, qh[ks][nt][0], qh[ks][nt][1]);
-                            mma_bf16_16816(sacc[nt], a, ql[ks][nt][0], ql[ks][nt][1]);
+                            if constexpr (kLo) mma_bf16_16816(sacc[nt], a, ql[ks][nt][0], ql[ks][nt][1]);
                         }
                     }
                 }
