@@ -643,35 +643,54 @@ __global__ void __launch_bounds__(256) wide_merge_kernel(const WideParams p, con
     if (t >= p.w_ntok[item]) return;
     const size_t oidx = static_cast<size_t>(p.tok_row[p.w_tok0[item] + t]) * p.H + h * g + j;
     auto ml = [&](int s) { return p.part_ml + ((static_cast<size_t>(s) * 2 + tile) * kWRows + r) * 2; };
+    float4* op = reinterpret_cast<float4*>(p.out + oidx * kWD) + lane;
+    // the split-KV row and its log-sum-exp, loaded up front (independent of the slots)
+    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+    float ls = -INFINITY;
+    if (p.lse != nullptr) {
+        ls = p.lse[oidx];
+        y = *op;
+    }
+    // slots' (max, sum) spread over the lanes (slot s0 + 32i + lane), then the max
     float mx = -INFINITY;
     for (int s = s0 + lane; s < s0 + ns; s += 32) mx = fmaxf(mx, ml(s)[0]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float L = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = s0; s < s0 + ns; ++s) {
-        const float ms = ml(s)[0], ls = ml(s)[1];
-        const float w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
-        const float4 x = reinterpret_cast<const float4*>(p.part_o + ((static_cast<size_t>(s) * 2 + tile) * kWRows + r) * kWD)[lane];
-        L += w * ls;
-        acc.x += w * x.x;
-        acc.y += w * x.y;
-        acc.z += w * x.z;
-        acc.w += w * x.w;
+    for (int b0 = s0; b0 < s0 + ns; b0 += 32) {
+        // this lane's slot weight, then every slot of the batch broadcast by shuffles; the
+        // row loads of a batch are independent of each other
+        const int sl = b0 + lane;
+        float w = 0.f, lw = 0.f;
+        if (sl < s0 + ns) {
+            const float ms = ml(sl)[0];
+            w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
+            lw = w * ml(sl)[1];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+        L += lw;
+        const int nb = min(32, s0 + ns - b0);
+#pragma unroll 4
+        for (int i = 0; i < nb; ++i) {
+            const float wi = __shfl_sync(0xffffffffu, w, i);
+            const float4 x = reinterpret_cast<const float4*>(p.part_o + ((static_cast<size_t>(b0 + i) * 2 + tile) * kWRows + r) * kWD)[lane];
+            acc.x += wi * x.x;
+            acc.y += wi * x.y;
+            acc.z += wi * x.z;
+            acc.w += wi * x.w;
+        }
     }
-    float4* op = reinterpret_cast<float4*>(p.out + oidx * kWD) + lane;
     float wo = L > 0.f ? 1.f / L : 0.f, wr = 0.f;
-    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
     if (p.lse != nullptr) {
         // merge with the split-KV result: (acc * 2^(mx-M) + y * 2^(lse_s-M)) / (L * 2^(mx-M) + 2^(lse_s-M))
-        const float ls = p.lse[oidx];
         const float mm = fmaxf(L > 0.f ? mx : -INFINITY, ls);
         const float a = L > 0.f ? exp2f(mx - mm) : 0.f;
         const float b = exp2f(ls - mm);
         const float inv = 1.f / (L * a + b);
         wo = a * inv;
         wr = b * inv;
-        y = *op;
     }
     *op = make_float4(acc.x * wo + y.x * wr, acc.y * wo + y.y * wr, acc.z * wo + y.z * wr, acc.w * wo + y.w * wr);
 }
