@@ -11,8 +11,9 @@ contexts U{512..4096}). Under torchrun every rank runs its own batch on its own 
 * ``value``: tokens/s over all ranks, K steps timed with CUDA events (inputs resident).
 * ``e2e``: the same through the public Python API from pinned HOST buffers, every step
   re-planning the batch (block tables up), q/k/v up and the output down.
-* ``roofline``: the tensor-core attention kernel's algorithmic bytes / its event-timed
-  duration against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+* ``roofline``: the dominant kernel's algorithmic bytes (split-KV decode) or FLOPs (the
+  tcgen05 wide-tile pass, C3/C4) per event-timed launch against the measured HBM copy
+  bandwidth or sustained bf16 throughput (MEASURED_PEAKS.json).
 * ``cpu_baseline``: the CPU oracle (numpy restatement of pagellm's gather path) on a
   bounded sample of the same workload on this host.
 ``--impl reference`` times that CPU path alone (rank 0; other ranks exit).
@@ -39,6 +40,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode-attn tokens/s & achieved HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1400.0  # sustained under the power cap
+TC_C2_NCU_TRAFFIC = 626_081_000  # dram__bytes_read.sum + dram__bytes_write.sum, one C2 launch
 RESULT_OUT = sys.stdout
 
 
@@ -73,10 +75,15 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100",
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi's first query initialises NVML, which can stall the GPU for a while
+            # on a fresh box: let that happen before any timed work
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 10.0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except OSError:
             self.proc = None
         return self
@@ -373,7 +380,9 @@ def run_ours(args):
             "unit": "GB/s",
             "frac": round(achieved / hbm, 4),
             "peak_source": hbm_src,
-            "traffic": None,
+            # DRAM read + write bytes of one launch from ncu (profiles/tc_attn_kernel_c2.md);
+            # recorded for the default workload only
+            "traffic": TC_C2_NCU_TRAFFIC if (args.config == "c2" and world == 1 and kind == 1) else None,
             "algorithmic_bytes_per_launch": alg_attn,
             "avg_launch_us": round(avg_ms * 1e3, 2),
             "kernel_us": {n: round(prof_ms[i] / max(1, prof_n[i]) * 1e3, 2)
@@ -465,7 +474,7 @@ def main():
     RESULT_OUT = _claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
