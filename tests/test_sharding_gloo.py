@@ -115,3 +115,40 @@ def test_head_slice_partition():
     assert [(s.q0, s.q1) for s in sl] == [(0, 16), (16, 32), (32, 48), (48, 64)]
     with pytest.raises(ValueError):
         head_slice(0, 3, 8, 64)
+
+
+def _dying_worker(rank, world, port, path):
+    """Rank 1 leaves after joining the group (between steps, nothing in flight); rank 0
+    must learn of it from its next collective, through the process group's short timeout,
+    as an exception on the host - no device is involved."""
+    import time
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from pagellm_b200.sharding import gather_heads
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    dist.barrier()  # both ranks reached the step boundary
+    if rank == 1:
+        return  # the rank dies here: its process exits without the next collective
+    t0 = time.time()
+    try:
+        gather_heads(torch.zeros((4, 2, 8)))
+        outcome = "no error"
+    except Exception as e:  # noqa: BLE001 - gloo raises RuntimeError subclasses
+        outcome = f"detected after {time.time() - t0:.1f} s: {type(e).__name__}"
+    with open(path, "w") as f:
+        f.write(outcome)
+
+
+def test_dead_rank_is_detected_on_the_host():
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "outcome.txt")
+        mp.start_processes(_dying_worker, args=(2, _port(), path), nprocs=2, join=True,
+                           start_method="spawn")
+        outcome = open(path).read()
+    assert outcome.startswith("detected"), outcome
+    assert float(outcome.split()[2]) < 30.0, outcome
