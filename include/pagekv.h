@@ -153,6 +153,10 @@ PK_API int pk_batch_profile_read(pk_batch* batch, double* ms5, int64_t* count5);
  * (<= 2 s) and the kernel reports it. *timed_out = 1 when that happened as designed.
  * Synchronises the device. */
 PK_API int pk_selftest_bounded_wait(int device, int64_t limit_ns, int* timed_out);
+/* Host-side fault injection for tests (no counterpart in pagellm): the next attention call
+ * (write_and_attend / attend, any batch) returns PK_ERR_CUDA before launching anything, as
+ * a failed launch would; later calls run normally. No GPU fault is involved. */
+PK_API int pk_test_inject_launch_failure(void);
 /* Host-only dry run of the split-KV planner (no device needed): given per-unit block
  * counts, returns for each CTA its first block [ncta+1], with
  * ncta = max(1, min(max_ctas, total, max(total / 16, ceil(n_units / 3)))): at least 16

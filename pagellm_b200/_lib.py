@@ -53,6 +53,7 @@ SIGNATURES: dict[str, tuple] = {
     "pk_batch_write_and_attend_host": (_i32, [_p, _i32, _i32, _p, _p, _p, _p, _p]),
     "pk_batch_check": (_i32, [_p, _p]),
     "pk_batch_stats": (_i32, [_p, _pi64]),
+    "pk_test_inject_launch_failure": (_i32, []),
     "pk_bm_truncate": (_i32, [_p, _i64, _i64]),
     "pk_batch_set_prefix_sharing": (_i32, [_p, _i32]),
     "pk_batch_prefix_stats": (_i32, [_p, _pi64]),

@@ -5,6 +5,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -797,11 +798,17 @@ pk::WideParams wide_params(pk_batch* B, int layer, int H, const float* q, float*
     return w;
 }
 
+// Host-side fault injection for tests: the next attention call of any batch fails as a
+// launch error would, before it launches anything.
+std::atomic<int> g_inject_launch_failure{0};
+
 int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaStream_t st,
                 const float* k_new = nullptr, const float* v_new = nullptr) {
     // k_new set: fused append - the split-KV kernel appends its units' rows, and the rows
     // of wide-tile sequences are appended just before the wide kernel, on its stream.
     pk_pool* P = B->pool;
+    if (g_inject_launch_failure.exchange(0) != 0)
+        return fail(PK_ERR_CUDA, "injected launch failure (pk_test_inject_launch_failure)");
     if (B->plan_H != H) {
         int rc = build_attention_plan(B, H, st);
         if (rc != PK_OK) return rc;
@@ -1384,6 +1391,11 @@ int pk_batch_stats(const pk_batch* B, int64_t* s) {
     s[4] = B->nsplit;
     s[5] = B->ngeneric;
     s[6] = B->launches;
+    return PK_OK;
+}
+
+int pk_test_inject_launch_failure(void) {
+    g_inject_launch_failure.store(1);
     return PK_OK;
 }
 

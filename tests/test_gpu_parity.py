@@ -581,6 +581,26 @@ def test_speculative_rollback_on_the_paged_pool():
     _close(out.cpu().numpy(), po.attention_dense(q.cpu().numpy(), kc, vc, 22), True)
 
 
+def test_injected_launch_failure_raises_and_batch_recovers():
+    """Fault injection on the host (SURVEY-style test hook, no GPU fault): the next
+    attention call fails as a launch error would, raises, and leaves the batch usable."""
+    from pagellm_b200 import _lib, workloads
+    from pagellm_b200.cache import PagedBatch
+
+    w = workloads.c2(1, batch=4)
+    pool = make_pool(w, 0)
+    b = PagedBatch(pool, w.tables, w.starts, w.n_new)
+    q, k, v = dev_inputs(w, 1)
+    assert _lib.load().pk_test_inject_launch_failure() == 0
+    with pytest.raises(RuntimeError, match="injected"):
+        b.write_and_attend(0, q, k, v)
+    out = b.write_and_attend(0, q, k, v)  # nothing was appended by the failed call
+    b.check()
+    got, qh = out.cpu().numpy(), q.cpu().numpy()
+    for i, (rows, ref) in oracle_rows(pool, w, range(w.nseq), qh).items():
+        _close(got[rows], ref, True)
+
+
 def test_bounded_wait_gives_up_and_context_survives():
     """Failure detection without a GPU fault: a wait on a barrier phase that nothing
     completes returns after its limit with an error status the host reads; the context
