@@ -409,7 +409,7 @@ def test_fused_append_single_launch_c2():
     assert st["launches"] == 1 and st["split_units"] > 0
 
 
-@pytest.mark.parametrize("H,KVH,bs", [(32, 8, 16), (64, 8, 16), (16, 4, 32)])
+@pytest.mark.parametrize("H,KVH,bs", [(32, 8, 16), (64, 8, 16), (16, 4, 32), (8, 8, 16), (16, 1, 64)])
 def test_wide_tile_chunks_match_oracle(H, KVH, bs):
     """Chunked prefill / long verify windows on the tcgen05 wide-tile kernel: prefill from
     position 0, chunks over a cached prefix with lengths off the 128-row tile, next to
@@ -485,7 +485,7 @@ def test_shared_prefix_forks_match_oracle(mode):
     torch.cuda.synchronize()
 
 
-@pytest.mark.parametrize("H,KVH,bs", [(32, 8, 16), (64, 8, 16), (16, 4, 32)])
+@pytest.mark.parametrize("H,KVH,bs", [(32, 8, 16), (64, 8, 16), (16, 4, 32), (8, 8, 16), (16, 1, 64)])
 def test_shared_prefix_groups_mixed_step(H, KVH, bs):
     """Several prefix groups in one step beside unshared decode rows and a prefill chunk:
     prefixes off block boundaries, one member whose first new token lies inside the shared
@@ -531,9 +531,18 @@ def test_shared_prefix_groups_mixed_step(H, KVH, bs):
         b.check()
         ps = b.prefix_stats()
         if mode == "always":
-            # group 3 is cut to the blocks before its member starting at 100
-            keys = 700 // bs * bs + 4 * bs + 100 // bs * bs
-            assert ps["groups"] == 3 and ps["shared_keys"] == keys, ps
+            # a member with n_new * g >= 64 query rows takes the wide chunk path and leaves
+            # its group; a group needs two members left; its prefix is cut at the first
+            # block holding any remaining member's first new token (group 3: the member at 100)
+            g = H // KVH
+            groups = keys = 0
+            for pre, mem in spec:
+                left = [st for st, n in mem if n * g < 64]
+                if pre and len(left) >= 2:
+                    groups += 1
+                    keys += min([pre // bs] + [st // bs for st in left]) * bs
+            assert ps["groups"] == groups and ps["shared_keys"] == keys, ps
+            assert groups >= 2
             assert b.stats()["wide_items"] > 0
     qh = q.cpu().numpy()
     meta = po.StepMeta(tables, starts, n_new, bs)
