@@ -397,7 +397,8 @@ def run_ours(args):
                                       + 16 * w.nseq),
             "d2h_bytes_per_step": int(out.numel() * 4),
             "steps": e_steps,
-            "path": "PagedBatch(pool, tables, starts, n_new).write_and_attend(0, q, k, v) on pinned numpy",
+            "path": "PagedBatch(pool, tables, starts, n_new).write_and_attend(0, q, k, v) on pinned numpy; "
+                    "the result crosses PCIe as the kernels' stores into the page-locked output",
         },
         "gpu_launches": int(launches_per_step * args.steps),
         "clocks": clk,

@@ -117,7 +117,11 @@ PK_API int pk_batch_write_and_attend(pk_batch* batch, int layer, int n_heads, co
 PK_API int pk_batch_attend(pk_batch* batch, int layer, int n_heads, const float* q_dev, float* out_dev,
                     void* stream);
 /* write_and_attend from HOST buffers: uploads q/k/v, runs the layer and downloads out,
- * all on `stream`; returns after `out_host` is filled (synchronous). */
+ * all on `stream`; returns after `out_host` is filled (synchronous). When `out_host` lies
+ * wholly inside one page-locked allocation the device can address (cudaMallocHost,
+ * cudaHostAlloc, cudaHostRegister), the kernels store the result into it directly, so the
+ * transfer overlaps the attention; steps with a shared-prefix pass, and pageable buffers,
+ * get a device-to-host copy after the kernels. */
 PK_API int pk_batch_write_and_attend_host(pk_batch* batch, int layer, int n_heads, const float* q_host,
                                    const float* k_host, const float* v_host, float* out_host,
                                    void* stream);
@@ -129,6 +133,10 @@ PK_API int pk_batch_check(pk_batch* batch, void* stream);
  * [5] rows on the CUDA-core kernel, [6] kernels launched by the last call, [7] wide-tile
  * work items (128 query rows each) on the tcgen05 kernel. */
 PK_API int pk_batch_stats(const pk_batch* batch, int64_t* stats8);
+/* Bytes moved by the last pk_batch_write_and_attend_host: [0] host to device, [1] device to
+ * host by a copy after the kernels, [2] stored by the kernels straight into the caller's
+ * page-locked result buffer. */
+PK_API int pk_batch_io_stats(const pk_batch* batch, int64_t* stats3);
 /* Shared-prefix (cascade) attention - no counterpart in pagellm, whose attention reads every
  * sequence's keys separately (cache/paged.py:454-463): sequences of a step whose block
  * tables begin with the same block ids (forks, prefix-cache hits) have the shared keys

@@ -46,13 +46,14 @@ SIGNATURES: dict[str, tuple] = {
     "pk_slot_mapping": (_i32, [_p, _i64, _p, _i64, _i32, _p, _p, _p]),
     "pk_batch_create": (_i32, [_p, C.POINTER(_p)]),
     "pk_batch_destroy": (_i32, [_p]),
-    "pk_batch_plan": (_i32, [_p, _i32, _pi64, _pi32, _pi64, _pi64, _pi64, _p]),
+    "pk_batch_plan": (_i32, [_p, _i32, _p, _p, _p, _p, _p, _p]),
     "pk_batch_rows": (_i32, [_p, C.POINTER(_p), C.POINTER(_p)]),
     "pk_batch_write_and_attend": (_i32, [_p, _i32, _i32, _p, _p, _p, _p, _p]),
     "pk_batch_attend": (_i32, [_p, _i32, _i32, _p, _p, _p]),
     "pk_batch_write_and_attend_host": (_i32, [_p, _i32, _i32, _p, _p, _p, _p, _p]),
     "pk_batch_check": (_i32, [_p, _p]),
     "pk_batch_stats": (_i32, [_p, _pi64]),
+    "pk_batch_io_stats": (_i32, [_p, _pi64]),
     "pk_test_inject_launch_failure": (_i32, []),
     "pk_bm_truncate": (_i32, [_p, _i64, _i64]),
     "pk_batch_set_prefix_sharing": (_i32, [_p, _i32]),

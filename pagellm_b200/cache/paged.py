@@ -50,8 +50,21 @@ def _torch():
 
 
 def _stream(device) -> int:
+    """Raw handle of the caller's current torch stream on ``device``."""
     torch = _torch()
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None and device.index is not None and torch.cuda.is_initialized():
+        return raw(device.index)  # no Stream object: this runs on every step
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def _addr(a: np.ndarray) -> int:
+    """Address of a C-contiguous array's data; the buffer-protocol route is several times
+    cheaper than ``ndarray.ctypes`` and is taken for every writable, non-empty array."""
+    try:
+        return C.addressof(C.c_char.from_buffer(a))
+    except (TypeError, ValueError):  # read-only or empty
+        return a.ctypes.data
 
 
 def _dtype_code(dtype):
@@ -299,10 +312,8 @@ class PagedBatch:
         _lib.check(lib.pk_batch_set_prefix_sharing(self._b, 1))  # recycled handles: default
         self._prefix_sharing = "auto"
         rows = C.c_int64()
-        _lib.check(lib.pk_batch_plan(
-            self._b, len(n_new_a), indptr.ctypes.data_as(C.POINTER(C.c_int64)),
-            ids.ctypes.data_as(C.POINTER(C.c_int32)), starts_a.ctypes.data_as(C.POINTER(C.c_int64)),
-            n_new_a.ctypes.data_as(C.POINTER(C.c_int64)), C.byref(rows), _stream(pool.device)))
+        _lib.check(lib.pk_batch_plan(self._b, len(n_new_a), _addr(indptr), _addr(ids), _addr(starts_a),
+                                     _addr(n_new_a), C.byref(rows), _stream(pool.device)))
         self.num_rows = rows.value
         self._slots = None
 
@@ -338,6 +349,13 @@ class PagedBatch:
         keys = ("rows", "tc_units", "tc_ctas", "tc_blocks", "split_units", "generic_rows", "launches",
                 "wide_items")
         return dict(zip(keys, list(s)))
+
+    def io_stats(self) -> dict:
+        """Bytes the last host-buffer ``write_and_attend`` moved: ``h2d``, ``d2h`` (a copy
+        after the kernels) and ``direct`` (stored by the kernels into the page-locked result)."""
+        s = (C.c_int64 * 3)()
+        _lib.check(self._lib.pk_batch_io_stats(self._b, s))
+        return dict(zip(("h2d", "d2h", "direct"), list(s)))
 
     _PREFIX_MODES = {False: 0, "off": 0, True: 1, "auto": 1, "always": 2}
 
@@ -399,7 +417,7 @@ class PagedBatch:
             kh = np.ascontiguousarray(k, dtype=np.float32)
             vh = np.ascontiguousarray(v, dtype=np.float32)
             _lib.check(self._lib.pk_batch_write_and_attend_host(
-                self._b, layer, H, qh.ctypes.data, kh.ctypes.data, vh.ctypes.data, out.ctypes.data, st))
+                self._b, layer, H, _addr(qh), _addr(kh), _addr(vh), _addr(out), st))
         else:
             torch = _torch()
             qd = torch.from_numpy(qh).to(P.device)

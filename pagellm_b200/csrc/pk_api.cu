@@ -155,6 +155,42 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+PFN_cuPointerGetAttribute_v4000 pointer_attribute_fn() {
+    static PFN_cuPointerGetAttribute_v4000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuPointerGetAttribute", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuPointerGetAttribute_v4000>(p);
+    });
+    return fn;
+}
+
+// Device address of the host range [p, p + bytes) when all of it lies inside one
+// page-locked allocation that the current device can address (cudaMallocHost, cudaHostAlloc
+// and cudaHostRegister ranges are mapped under unified addressing), else nullptr. The
+// allocation's extent comes from the driver, so a kernel never stores past the end of a
+// buffer shorter than `bytes`: such a buffer, and pageable memory, get nullptr.
+void* mapped_host_range(void* p, size_t bytes) {
+    PFN_cuPointerGetAttribute_v4000 fn = pointer_attribute_fn();
+    if (!fn || !p || bytes == 0) return nullptr;
+    const CUdeviceptr a = reinterpret_cast<CUdeviceptr>(p);
+    unsigned int mtype = 0;
+    CUdeviceptr start = 0, dptr = 0;
+    size_t size = 0;
+    if (fn(&mtype, CU_POINTER_ATTRIBUTE_MEMORY_TYPE, a) != CUDA_SUCCESS || mtype != CU_MEMORYTYPE_HOST)
+        return nullptr;
+    if (fn(&start, CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, a) != CUDA_SUCCESS ||
+        fn(&size, CU_POINTER_ATTRIBUTE_RANGE_SIZE, a) != CUDA_SUCCESS ||
+        fn(&dptr, CU_POINTER_ATTRIBUTE_DEVICE_POINTER, a) != CUDA_SUCCESS)
+        return nullptr;
+    if (a < start || a - start > size || bytes > size - (a - start)) return nullptr;
+    if (dptr == 0 || dptr % 16 != 0) return nullptr;
+    return reinterpret_cast<void*>(dptr);
+}
+
 }  // namespace
 
 struct pk_pool {
@@ -204,6 +240,10 @@ struct pk_batch {
     bool fuse_append_ok = true;
     std::vector<int32_t> app_rows;  // winner rows when slots repeat (else empty = all rows)
     std::vector<int32_t> writer_seq, writer_idx;  // per block id, scratch of the check
+    std::vector<uint64_t> written;                // bit per block id: written this step
+    // positions / slots of the step's rows (rows buffer) not built yet; the plan's stream
+    mutable bool rows_pending = false;
+    cudaStream_t rows_stream = nullptr;
     DevBuf counters;  // per (unit, KV head) merge counters, zero between launches
     // Wide-tile work runs on a side stream, forked from and joined back into the caller's
     // stream with events, so it overlaps the split-KV kernel.
@@ -242,6 +282,10 @@ struct pk_batch {
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
     int launches = 0;
+    // bytes the last pk_batch_write_and_attend_host moved: host to device, device to host
+    // by a copy after the kernels, stored by the kernels straight into the caller's
+    // page-locked result buffer
+    int64_t io_h2d = 0, io_d2h = 0, io_direct = 0;
     // Optional per-kernel timing: events recorded on the launching stream around each
     // launch, resolved by pk_batch_profile_read.
     bool profiling = false;
@@ -252,6 +296,17 @@ struct pk_batch {
     const int64_t* positions() const { return static_cast<const int64_t*>(rows.ptr); }
     const int64_t* slots() const { return static_cast<const int64_t*>(rows.ptr) + nrows; }
 };
+
+// Positions and slots of the step's rows (paged.py:412-424) on the device, built on first
+// use: a decode step with the fused append never reads them.
+static cudaError_t ensure_rows(const pk_batch* B, cudaStream_t st) {
+    if (!B->rows_pending) return cudaSuccess;
+    B->rows_pending = false;
+    return pk::launch_plan_rows(B->meta.at<int32_t>(4), B->meta.at<int32_t>(3), B->meta.at<int32_t>(2),
+                                B->meta.at<int32_t>(0), B->meta.at<int32_t>(1), B->pool->block_size,
+                                B->nrows, static_cast<int64_t*>(B->rows.ptr),
+                                static_cast<int64_t*>(B->rows.ptr) + B->nrows, st);
+}
 
 namespace {
 
@@ -827,6 +882,10 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
     }
     if (B->nwide > 0) {
         if (k_new != nullptr) {
+            if (B->rows_pending) {
+                PK_CUDA(ensure_rows(B, ws));
+                B->launches++;
+            }
             PK_CUDA(prof_begin(B, ws));
             PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_new, v_new,
                                       B->slots(), B->plan.at<int32_t>(10),
@@ -1187,11 +1246,22 @@ int pk_batch_plan(pk_batch* B, int nseq, const int64_t* table_indptr, const int3
             return fail(PK_ERR_OUT_OF_RANGE, "seq %d: positions up to %lld need %lld blocks, table has %lld",
                         i, (long long)(ctx - 1), (long long)need, (long long)(te - tb));
         if (need > 0 && !table_ids) return fail(PK_ERR_INVALID_ARG, "table_ids is NULL");
-        for (int64_t j = tb; j < tb + need; ++j) {
-            const int32_t b = table_ids[j];
-            if (b < 0 || b >= P->num_blocks)
-                return fail(PK_ERR_OUT_OF_RANGE, "seq %d: block id %d outside [0, %lld)", i, b,
-                            (long long)P->num_blocks);
+        // range check as a min / max reduction (vectorised); the offender only on failure
+        int32_t lo = 0, hi = 0;
+        if (need > 0) {
+            lo = hi = table_ids[tb];
+            for (int64_t j = tb + 1; j < tb + need; ++j) {
+                lo = std::min(lo, table_ids[j]);
+                hi = std::max(hi, table_ids[j]);
+            }
+        }
+        if (lo < 0 || hi >= P->num_blocks) {
+            for (int64_t j = tb; j < tb + need; ++j) {
+                const int32_t b = table_ids[j];
+                if (b < 0 || b >= P->num_blocks)
+                    return fail(PK_ERR_OUT_OF_RANGE, "seq %d: block id %d outside [0, %lld)", i, b,
+                                (long long)P->num_blocks);
+            }
         }
         // Only the referenced prefix of each table is uploaded.
         B->ids.insert(B->ids.end(), table_ids + tb, table_ids + tb + need);
@@ -1211,6 +1281,7 @@ int pk_batch_plan(pk_batch* B, int nseq, const int64_t* table_indptr, const int3
     if (B->writer_seq.size() != static_cast<size_t>(P->num_blocks)) {
         B->writer_seq.assign(P->num_blocks, -1);
         B->writer_idx.assign(P->num_blocks, -1);
+        B->written.assign((P->num_blocks + 63) / 64, 0);
     }
     std::vector<int32_t> touched;
     bool dup_slot = false;
@@ -1221,6 +1292,7 @@ int pk_batch_plan(pk_batch* B, int nseq, const int64_t* table_indptr, const int3
             if (B->writer_seq[b] < 0) {
                 B->writer_seq[b] = i;
                 B->writer_idx[b] = j;
+                B->written[b >> 6] |= uint64_t(1) << (b & 63);
                 touched.push_back(b);
             } else if (B->writer_seq[b] != i || B->writer_idx[b] != j) {
                 B->fuse_append_ok = false;
@@ -1229,15 +1301,24 @@ int pk_batch_plan(pk_batch* B, int nseq, const int64_t* table_indptr, const int3
             }
         }
     }
-    for (int i = 0; i < nseq && B->fuse_append_ok; ++i)
-        for (int32_t j = 0; j < B->indptr[i + 1] - B->indptr[i]; ++j) {
-            const int32_t b = B->ids[B->indptr[i] + j];
-            if (B->writer_seq[b] >= 0 && (B->writer_seq[b] != i || B->writer_idx[b] != j)) {
+    // every table entry against the written set: a bitmap (one bit per block, L1-resident)
+    // first, the writer's (sequence, index) only for written blocks
+    const uint64_t* wbits = B->written.data();
+    for (int i = 0; i < nseq && B->fuse_append_ok; ++i) {
+        const int32_t* t = B->ids.data() + B->indptr[i];
+        const int32_t n = B->indptr[i + 1] - B->indptr[i];
+        for (int32_t j = 0; j < n; ++j) {
+            const int32_t b = t[j];
+            if (((wbits[b >> 6] >> (b & 63)) & 1) && (B->writer_seq[b] != i || B->writer_idx[b] != j)) {
                 B->fuse_append_ok = false;
                 break;
             }
         }
-    for (int32_t b : touched) B->writer_seq[b] = B->writer_idx[b] = -1;
+    }
+    for (int32_t b : touched) {
+        B->writer_seq[b] = B->writer_idx[b] = -1;
+        B->written[b >> 6] = 0;
+    }
     if (dup_slot) {
         // last row wins per slot (numpy fancy assignment order)
         std::unordered_map<int64_t, int32_t> last;
@@ -1270,15 +1351,15 @@ int pk_batch_plan(pk_batch* B, int nseq, const int64_t* table_indptr, const int3
     int rc = B->meta.commit(st);
     if (rc != PK_OK) return rc;
     PK_CUDA(B->rows.reserve(static_cast<size_t>(std::max<int64_t>(rows, 1)) * 16));
-    PK_CUDA(pk::launch_plan_rows(B->meta.at<int32_t>(4), B->meta.at<int32_t>(3), B->meta.at<int32_t>(2),
-                                 B->meta.at<int32_t>(0), B->meta.at<int32_t>(1), bs, rows,
-                                 static_cast<int64_t*>(B->rows.ptr),
-                                 static_cast<int64_t*>(B->rows.ptr) + rows, st));
+    B->rows_pending = rows > 0;  // built by the first reader (ensure_rows)
+    B->rows_stream = st;
     return PK_OK;
 }
 
 int pk_batch_rows(const pk_batch* B, const int64_t** positions_dev, const int64_t** slots_dev) {
     if (!B) return fail(PK_ERR_INVALID_ARG, "batch is NULL");
+    DeviceScope ds(B->pool->device);
+    PK_CUDA(ensure_rows(B, B->rows_stream));
     if (positions_dev) *positions_dev = B->positions();
     if (slots_dev) *slots_dev = B->slots();
     return PK_OK;
@@ -1323,6 +1404,10 @@ int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* 
         return attend_impl(B, layer, n_heads, q_dev, out_dev, st, k_dev, v_dev);
     if (B->nrows > 0) {
         const bool listed = !B->app_rows.empty();
+        if (B->rows_pending) {
+            PK_CUDA(ensure_rows(B, st));
+            B->launches++;
+        }
         PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_dev, v_dev,
                                   B->slots(), listed ? B->meta.at<int32_t>(5) : nullptr,
@@ -1353,16 +1438,42 @@ int pk_batch_write_and_attend_host(pk_batch* B, int layer, int n_heads, const fl
     float* kd = qd + up(qn);
     float* vd = kd + up(kn);
     float* od = vd + up(kn);
+    B->io_h2d = B->io_d2h = B->io_direct = 0;
     if (B->nrows > 0) {
         PK_CUDA(cudaMemcpyAsync(qd, q_host, qn * sizeof(float), cudaMemcpyHostToDevice, st));
         PK_CUDA(cudaMemcpyAsync(kd, k_host, kn * sizeof(float), cudaMemcpyHostToDevice, st));
         PK_CUDA(cudaMemcpyAsync(vd, v_host, kn * sizeof(float), cudaMemcpyHostToDevice, st));
+        B->io_h2d = static_cast<int64_t>(qn + 2 * kn) * sizeof(float);
+        // the attention plan now, while the copies run (pk_batch_write_and_attend reuses it)
+        if (layer >= 0 && layer < P->n_layers && B->plan_H != n_heads) {
+            rc = build_attention_plan(B, n_heads, st);
+            if (rc != PK_OK) return rc;
+        }
+        // A page-locked result buffer is stored into by the kernels themselves: the result
+        // crosses PCIe while the attention runs instead of in a copy after it. Not with a
+        // shared-prefix pass, which reads the split-KV rows back from the output.
+        if (B->plan_H == n_heads && B->nprefix == 0) {
+            if (float* direct = static_cast<float*>(mapped_host_range(out_host, qn * sizeof(float)))) {
+                od = direct;
+                B->io_direct = static_cast<int64_t>(qn) * sizeof(float);
+            }
+        }
     }
     rc = pk_batch_write_and_attend(B, layer, n_heads, qd, kd, vd, od, stream);
     if (rc != PK_OK) return rc;
-    if (B->nrows > 0)
+    if (B->nrows > 0 && B->io_direct == 0) {
         PK_CUDA(cudaMemcpyAsync(out_host, od, qn * sizeof(float), cudaMemcpyDeviceToHost, st));
+        B->io_d2h = static_cast<int64_t>(qn) * sizeof(float);
+    }
     PK_CUDA(cudaStreamSynchronize(st));
+    return PK_OK;
+}
+
+int pk_batch_io_stats(const pk_batch* B, int64_t* s) {
+    if (!B || !s) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    s[0] = B->io_h2d;
+    s[1] = B->io_d2h;
+    s[2] = B->io_direct;
     return PK_OK;
 }
 

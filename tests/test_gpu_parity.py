@@ -87,7 +87,36 @@ def test_golden_fork_cow_verify(mode):
     out = batch.write_and_attend(0, c["q"], c["k"], c["v"])
     batch.check()
     assert batch.prefix_stats()["groups"] == (1 if mode == "always" else 0)
+    # the shared-prefix pass reads the split-KV rows back from the output, so its result
+    # comes back by a copy after the kernels; without it the kernels store it directly
+    io = batch.io_stats()
+    assert (io["d2h"], io["direct"]) == ((out.nbytes, 0) if mode == "always" else (0, out.nbytes)), io
     _close(out, c["out"], True)
+
+
+def test_host_buffer_result_paths():
+    """write_and_attend from host arrays: a page-locked result buffer (what the Python
+    surface hands out) is stored into by the kernels, with no device-to-host copy; a pageable
+    buffer through the C entry gets the copy; both equal the device-buffer result bit for bit."""
+    torch = torch_cuda()
+    from pagellm_b200 import _lib, workloads
+    from pagellm_b200.cache import PagedBatch
+
+    w = workloads.c2(3)
+    pool = make_pool(w)
+    q, k, v = dev_inputs(w)
+    b = PagedBatch(pool, w.csr(), w.starts, w.n_new)
+    ref = b.write_and_attend(0, q, k, v).cpu().numpy()  # re-appending equal rows is a no-op
+    qh, kh, vh = q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy()
+    got = b.write_and_attend(0, qh, kh, vh)
+    assert b.io_stats() == {"h2d": qh.nbytes + kh.nbytes + vh.nbytes, "d2h": 0, "direct": qh.nbytes}
+    np.testing.assert_array_equal(got, ref)
+    out = np.full_like(qh, np.nan)  # pageable
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(_lib.load().pk_batch_write_and_attend_host(b._b, 0, w.H, qh.ctypes.data, kh.ctypes.data,
+                                                          vh.ctypes.data, out.ctypes.data, st))
+    assert b.io_stats() == {"h2d": qh.nbytes + kh.nbytes + vh.nbytes, "d2h": qh.nbytes, "direct": 0}
+    np.testing.assert_array_equal(out, ref)
 
 
 def test_golden_paged_attention_cases():
