@@ -165,12 +165,15 @@ PK_API int pk_selftest_bounded_wait(int device, int64_t limit_ns, int* timed_out
  * (write_and_attend / attend, any batch) returns PK_ERR_CUDA before launching anything, as
  * a failed launch would; later calls run normally. No GPU fault is involved. */
 PK_API int pk_test_inject_launch_failure(void);
-/* Host-only dry run of the split-KV planner (no device needed): given per-unit block
- * counts, returns for each CTA its first block [ncta+1], with
- * ncta = max(1, min(max_ctas, total, max(total / 16, ceil(n_units / 3)))): at least 16
- * blocks per CTA, unless many short units are better spread 3 per CTA. */
-PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,
-                      int64_t* cta_first_block, int* ncta);
+/* Host-only dry run of the split-KV planner (no device needed). The units' blocks, end to
+ * end, are cut into contiguous CTA ranges; a range costs its blocks plus
+ * `unit_switch_blocks` per unit boundary inside it (a CTA that crosses into another unit
+ * reloads queries, publishes a partial and usually merges the unit it ends in); the cut
+ * minimises the largest cost over at most n = max(1, min(max_ctas, total, max(total / 16,
+ * ceil(n_units / 3)))) CTAs. Writes *ncta (<= n) and, if cta_first_block is not NULL, the
+ * first block of each CTA [*ncta + 1] (the caller provides n + 1 entries). */
+PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas, int unit_switch_blocks,
+                             int64_t* cta_first_block, int* ncta);
 
 
 /* Decode attention that allocates nothing. No counterpart in the reference: pagellm has no

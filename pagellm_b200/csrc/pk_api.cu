@@ -257,6 +257,7 @@ struct pk_batch {
     int nu = 0, total_blocks = 0, ncta = 0, nt = 1, nsplit = 0;
     int ngeneric = 0;
     std::vector<int32_t> u_seq, u_t0, u_n, u_blk, sp_u, sp_c0, sp_c1, gen_rows;
+    std::vector<int32_t> cta_blk;  // [ncta + 1] first block of each split-KV CTA
     // Wide-tile work items: [0, nwide) chunk items (side stream), then [nwide, nwide +
     // nprefix) shared-prefix items (after the split-KV kernel, merged into its rows).
     int nwide = 0, nprefix = 0, nprefix_groups = 0;
@@ -450,15 +451,56 @@ int64_t split_kv_ctas(int64_t T, int64_t nu, int64_t max_ctas) {
 // wide-tile tensor-core kernel; fewer rows stay on the split-KV kernel's units.
 constexpr int64_t kWideMinRows = 64;
 
-// CTA c of n owns blocks [c*T/n, (c+1)*T/n).
-inline int64_t cta_lo(int64_t c, int64_t T, int64_t n) { return c * T / n; }
+// Time a split-KV CTA loses per unit boundary inside its block range (B200, C2 decode
+// shape, per-CTA globaltimer trace): it reloads queries, publishes a partial for the unit
+// it leaves, and the unit it ends in it usually finishes last of that unit's CTAs, so it
+// merges the unit's partials at the end of its run. CTAs crossing one boundary ran 112 us
+// against 102.6 us for those inside one unit, with equal block counts.
+constexpr double kUnitSwitchUs = 9.0;
 
-int cta_of_block(int64_t j, int64_t T, int64_t n) {
-    int64_t c = j * n / T;
-    while (c + 1 < n && cta_lo(c + 1, T, n) <= j) ++c;
-    while (c > 0 && cta_lo(c, T, n) > j) --c;
-    return static_cast<int>(c);
+// The units' blocks (in unit order, prefix sums ub[0..nu]) cut into contiguous CTA ranges,
+// at most n of them. A range costs its blocks plus `switch_cost` blocks per unit boundary
+// inside it; the cut minimises the largest cost: bisection on the bound, each CTA filled
+// greedily up to it. Returns the CTAs used; first[0..count] are their first blocks.
+template <typename I>
+int partition_blocks(const I* ub, int64_t nu, int64_t n, int64_t switch_cost, std::vector<int32_t>& first) {
+    const int64_t T = nu > 0 ? static_cast<int64_t>(ub[nu]) : 0;
+    first.assign(1, 0);
+    if (T <= 0 || n <= 0) return 0;
+    auto fill = [&](int64_t X, bool keep) -> int64_t {
+        int64_t b = 0, count = 0, u = 0;
+        while (b < T) {
+            while (static_cast<int64_t>(ub[u + 1]) <= b) ++u;
+            int64_t R = X, e = b, uu = u;
+            for (;;) {
+                const int64_t take = std::min<int64_t>(static_cast<int64_t>(ub[uu + 1]) - e, R);
+                e += take;
+                R -= take;
+                if (e < static_cast<int64_t>(ub[uu + 1]) || uu + 1 >= nu || R < switch_cost + 1) break;
+                R -= switch_cost;
+                ++uu;
+            }
+            if (e == b) e = b + 1;
+            b = e;
+            ++count;
+            if (keep) first.push_back(static_cast<int32_t>(b));
+        }
+        return count;
+    };
+    int64_t lo = (T + n - 1) / n, hi = T + switch_cost * nu;  // hi: one CTA always fits
+    while (lo < hi) {
+        const int64_t mid = lo + (hi - lo) / 2;
+        if (fill(mid, false) <= n) hi = mid;
+        else lo = mid + 1;
+    }
+    return static_cast<int>(fill(lo, true));
 }
+
+// CTA of block j under the partition `first` (count + 1 entries).
+int cta_of_block(const std::vector<int32_t>& first, int64_t j) {
+    return static_cast<int>(std::upper_bound(first.begin(), first.end(), static_cast<int32_t>(j)) - first.begin()) - 1;
+}
+
 
 // Shared prefixes (cascade attention). Sequences whose block tables begin with the same
 // block ids - forks and prefix-cache hits in pagellm (cache/paged.py:187-203, :257-263) -
@@ -474,6 +516,14 @@ constexpr double kWideUsPerKeyTile = 2.5;     // one CTA (256 rows) over one 128
 constexpr double kWideFixedUs = 5.0;          // launch, Q load, epilogue
 constexpr int64_t kWideMinTilesPerCta = 4;    // stream-K shares smaller than this cost more than they save
 constexpr double kSplitKvBytesPerUs = 6.0e6;  // split-KV streaming rate (HBM / L2)
+
+// Unit-boundary cost in blocks for a pool: kUnitSwitchUs of one CTA's share of the
+// split-KV streaming rate (`ctas` CTAs sharing it), over the K+V bytes of one block.
+int64_t unit_switch_blocks(const pk_pool* P, int64_t ctas) {
+    const double cta_rate = kSplitKvBytesPerUs / static_cast<double>(std::max<int64_t>(1, ctas));
+    const double blk = static_cast<double>(P->block_bytes()) * 2.0;
+    return std::max<int64_t>(0, std::llround(kUnitSwitchUs * cta_rate / blk));
+}
 
 void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>& tc_seqs) {
     pk_pool* P = B->pool;
@@ -631,6 +681,7 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan_H = -1;
     B->u_seq.clear(); B->u_t0.clear(); B->u_n.clear(); B->u_blk.assign(1, 0);
     B->sp_u.clear(); B->sp_c0.clear(); B->sp_c1.clear(); B->gen_rows.clear();
+    B->cta_blk.assign(1, 0);
     B->use_tc = false;
     B->nu = B->total_blocks = B->ncta = B->nsplit = B->ngeneric = 0;
     B->nt = 1;
@@ -734,10 +785,12 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         int& occ = P->tc_occ[std::min(B->nt, 2)];
         if (occ == 0) occ = pk::tc_max_active_ctas(P->d, B->nt, P->kvh, P->tc_smem);
         const int per_sm = std::max(1, std::min(P->tc_ctas_per_sm, occ));
-        B->ncta = static_cast<int>(split_kv_ctas(T, B->nu, static_cast<int64_t>(P->num_sms) * per_sm));
+        const int64_t nmax = split_kv_ctas(T, B->nu, static_cast<int64_t>(P->num_sms) * per_sm);
+        B->ncta = partition_blocks(B->u_blk.data(), B->nu, nmax,
+                                   unit_switch_blocks(P, static_cast<int64_t>(P->num_sms) * per_sm), B->cta_blk);
         for (int u = 0; u < B->nu; ++u) {
-            const int c0 = cta_of_block(B->u_blk[u], T, B->ncta);
-            const int c1 = cta_of_block(B->u_blk[u + 1] - 1, T, B->ncta);
+            const int c0 = cta_of_block(B->cta_blk, B->u_blk[u]);
+            const int c1 = cta_of_block(B->cta_blk, B->u_blk[u + 1] - 1);
             if (c0 != c1) {
                 B->sp_u.push_back(u);
                 B->sp_c0.push_back(c0);
@@ -775,6 +828,7 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan.add(B->cta_seg.data(), B->cta_seg.size() * 4);
     B->plan.add(B->seg.data(), B->seg.size() * 4);
     B->plan.add(B->split.data(), B->split.size() * 4);
+    B->plan.add(B->cta_blk.data(), B->cta_blk.size() * 4);
     if (B->nslots > 0)
         PK_CUDA(B->wpart.reserve(static_cast<size_t>(B->nslots) * 2 * 128 * (128 + 2) * sizeof(float)));
     if (B->nprefix > 0) PK_CUDA(B->lse.reserve(static_cast<size_t>(B->nrows) * H * sizeof(float)));
@@ -919,6 +973,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.nu = B->nu;
         p.total_blocks = B->total_blocks;
         p.ncta = B->ncta;
+        p.cta_blk = B->plan.at<int32_t>(21);
         p.kvh = P->kvh;
         p.g = g;
         p.H = H;
@@ -1576,18 +1631,21 @@ int pk_selftest_bounded_wait(int device, int64_t limit_ns, int* timed_out) {
     return PK_OK;
 }
 
-int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas,
+int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int max_ctas, int unit_switch_blocks,
                       int64_t* cta_first_block, int* ncta) {
-    if (n_units < 0 || max_ctas <= 0 || !ncta) return fail(PK_ERR_INVALID_ARG, "bad arguments");
-    int64_t T = 0;
+    if (n_units < 0 || max_ctas <= 0 || unit_switch_blocks < 0 || !ncta || (n_units > 0 && !unit_blocks))
+        return fail(PK_ERR_INVALID_ARG, "bad arguments");
+    std::vector<int64_t> ub(static_cast<size_t>(n_units) + 1, 0);
     for (int64_t i = 0; i < n_units; ++i) {
         if (unit_blocks[i] <= 0) return fail(PK_ERR_INVALID_ARG, "unit %lld has no blocks", (long long)i);
-        T += unit_blocks[i];
+        ub[i + 1] = ub[i] + unit_blocks[i];
+        if (ub[i + 1] >= (int64_t(1) << 31)) return fail(PK_ERR_UNSUPPORTED, "too many blocks");
     }
-    const int64_t n = split_kv_ctas(T, n_units, max_ctas);
-    *ncta = static_cast<int>(n);
+    const int64_t n = split_kv_ctas(ub[n_units], n_units, max_ctas);
+    std::vector<int32_t> first;
+    *ncta = partition_blocks(ub.data(), n_units, n, unit_switch_blocks, first);
     if (cta_first_block)
-        for (int64_t c = 0; c <= n; ++c) cta_first_block[c] = n ? cta_lo(c, T, n) : 0;
+        for (int c = 0; c <= *ncta; ++c) cta_first_block[c] = first[c];
     return PK_OK;
 }
 

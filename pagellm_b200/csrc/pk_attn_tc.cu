@@ -10,8 +10,9 @@
 // tokens (g = query heads per KV head), so one unit's (token, head) columns fit one or two
 // n8 MMA tiles. A unit reads the blocks that hold positions 0..unit_ctx-1 (from block
 // u_kb0 on when a shared prefix is attended by the wide-tile kernel instead). All units'
-// blocks are laid end to end and the total is cut into `ncta` equal ranges: CTA c owns
-// blocks [c*T/ncta, (c+1)*T/ncta). A unit that falls inside one CTA is finished there;
+// blocks are laid end to end and the total is cut into `ncta` contiguous ranges: CTA c owns
+// blocks [cta_blk[c], cta_blk[c+1]) (the planner's cut, which charges every unit boundary
+// inside a range), or [c*T/ncta, (c+1)*T/ncta) without cta_blk. A unit inside one CTA is finished there;
 // a unit cut by CTA boundaries leaves one partial (max, sum, un-normalised output) per
 // CTA; the last CTA to finish a (unit, KV head) merges them in place (per-unit counters),
 // or, without counters, merge_kernel does it in a second launch.
@@ -49,8 +50,10 @@ __device__ __forceinline__ int upper_bound_i32(const int32_t* a, int n, int x) {
     return lo;
 }
 
-// CTA whose block range [c*T/n, (c+1)*T/n) holds block j.
-__device__ __forceinline__ int cta_of_block(int j, int T, int n) {
+// CTA whose block range holds block j: the planner's ranges (first blocks cta_blk[0..n]),
+// else the equal ranges [c*T/n, (c+1)*T/n).
+__device__ __forceinline__ int cta_of_block(int j, int T, int n, const int32_t* cta_blk) {
+    if (cta_blk != nullptr) return upper_bound_i32(cta_blk, n + 1, j) - 1;
     int c = static_cast<int>(static_cast<int64_t>(j) * n / T);
     while (c + 1 < n && static_cast<int64_t>(c + 1) * T / n <= j) ++c;
     while (c > 0 && static_cast<int64_t>(c) * T / n > j) --c;
@@ -127,8 +130,8 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     const int c = blockIdx.x;
-    const int lo = static_cast<int>(static_cast<int64_t>(c) * p.total_blocks / p.ncta);
-    const int hi = static_cast<int>(static_cast<int64_t>(c + 1) * p.total_blocks / p.ncta);
+    const int lo = p.cta_blk ? p.cta_blk[c] : static_cast<int>(static_cast<int64_t>(c) * p.total_blocks / p.ncta);
+    const int hi = p.cta_blk ? p.cta_blk[c + 1] : static_cast<int>(static_cast<int64_t>(c + 1) * p.total_blocks / p.ncta);
     const int u_first = upper_bound_i32(p.u_blk, p.nu + 1, lo) - 1;
 
     if (warp == nwc) {
@@ -441,8 +444,8 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 // The last of the unit's CTAs to finish head h merges: its own partial is
                 // still in registers, every other CTA's partial is fetched with one batch of
                 // independent loads per CTA. The counter is left at zero for the next launch.
-                const int cf = cta_of_block(ublk0, p.total_blocks, p.ncta);
-                const int cl = cta_of_block(p.u_blk[u + 1] - 1, p.total_blocks, p.ncta);
+                const int cf = cta_of_block(ublk0, p.total_blocks, p.ncta, p.cta_blk);
+                const int cl = cta_of_block(p.u_blk[u + 1] - 1, p.total_blocks, p.ncta, p.cta_blk);
                 __syncwarp();
                 int last = 0;
                 if (lane == 0) {
@@ -453,11 +456,13 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 }
                 if (__shfl_sync(0xffffffffu, last, 0)) {
                     __threadfence();
-                    // Two passes in CTA order cf..cl, so the result does not depend on which
-                    // CTA merges: the global max, then the weighted sums in that order, with
-                    // this CTA's own partial (bit-identical to what it stored) taken from
-                    // registers at its place in the order.
+                    // One pass in CTA order cf..cl with a running max (online softmax merge),
+                    // so the result does not depend on which CTA merges: this CTA's own
+                    // partial (bit-identical to what it stored) is taken from registers at
+                    // its place in the order. Each step's loads are independent of the
+                    // running values, so two CTAs' partials are in flight together.
                     float mx[NT][2], den[NT][2];
+                    float num[KS][NT][4];
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -465,27 +470,17 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                             mx[nt][e] = -INFINITY;
                             den[nt][e] = 0.f;
                         }
-#pragma unroll 4
-                    for (int cc = cf; cc <= cl; ++cc) {
-                        const size_t ob = ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols;
-#pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                            for (int e = 0; e < 2; ++e) {
-                                const int col = nt * 8 + 2 * quad + e;
-                                const float mc = cc == c ? m[nt][e] : __ldcg(p.part_ml + (ob + col) * 2);
-                                mx[nt][e] = fmaxf(mx[nt][e], mc);
-                            }
-                    }
-                    float num[KS][NT][4];
 #pragma unroll
                     for (int mt = 0; mt < KS; ++mt)
 #pragma unroll
                         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                             for (int i = 0; i < 4; ++i) num[mt][nt][i] = 0.f;
-#pragma unroll 2
-                    for (int cc = cf; cc <= cl; ++cc) {
+                    // Where registers allow (one n8 tile, D <= 128), a step's loads go into
+                    // arrays and two steps are unrolled; elsewhere that spills, so the loads
+                    // are folded into the accumulation one step at a time.
+                    constexpr bool kArr = NT == 1 && D <= 128;
+                    auto merge_step = [&](int cc) {
                         const size_t ob = ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols;
                         const bool own = cc == c;
 #pragma unroll
@@ -495,17 +490,41 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                                 const int col = nt * 8 + 2 * quad + e;
                                 const float mc = own ? m[nt][e] : __ldcg(p.part_ml + (ob + col) * 2);
                                 const float lc = own ? l[nt][e] : __ldcg(p.part_ml + (ob + col) * 2 + 1);
-                                const float w = mc == -INFINITY ? 0.f : exp2f(mc - mx[nt][e]);
-                                den[nt][e] += lc * w;
                                 const float* po = p.part_o + (ob + col) * D;
+                                float o0[kArr ? KS : 1], o1[kArr ? KS : 1];
+                                if constexpr (kArr) {
+#pragma unroll
+                                    for (int mt = 0; mt < KS; ++mt) {
+                                        o0[mt] = own ? acc[mt][nt][e] : __ldcg(po + mt * 16 + grp);
+                                        o1[mt] = own ? acc[mt][nt][2 + e] : __ldcg(po + mt * 16 + grp + 8);
+                                    }
+                                }
+                                const float mn = fmaxf(mx[nt][e], mc);
+                                const float a = mx[nt][e] == -INFINITY ? 0.f : exp2f(mx[nt][e] - mn);
+                                const float b = mc == -INFINITY ? 0.f : exp2f(mc - mn);
+                                mx[nt][e] = mn;
+                                den[nt][e] = den[nt][e] * a + lc * b;
 #pragma unroll
                                 for (int mt = 0; mt < KS; ++mt) {
-                                    const float o0 = own ? acc[mt][nt][e] : __ldcg(po + mt * 16 + grp);
-                                    const float o1 = own ? acc[mt][nt][2 + e] : __ldcg(po + mt * 16 + grp + 8);
-                                    num[mt][nt][e] += o0 * w;
-                                    num[mt][nt][2 + e] += o1 * w;
+                                    float x0, x1;
+                                    if constexpr (kArr) {
+                                        x0 = o0[mt];
+                                        x1 = o1[mt];
+                                    } else {
+                                        x0 = own ? acc[mt][nt][e] : __ldcg(po + mt * 16 + grp);
+                                        x1 = own ? acc[mt][nt][2 + e] : __ldcg(po + mt * 16 + grp + 8);
+                                    }
+                                    num[mt][nt][e] = num[mt][nt][e] * a + x0 * b;
+                                    num[mt][nt][2 + e] = num[mt][nt][2 + e] * a + x1 * b;
                                 }
                             }
+                    };
+                    if constexpr (kArr) {
+#pragma unroll 2
+                        for (int cc = cf; cc <= cl; ++cc) merge_step(cc);
+                    } else {
+#pragma unroll 1
+                        for (int cc = cf; cc <= cl; ++cc) merge_step(cc);
                     }
                     store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp);
                 }

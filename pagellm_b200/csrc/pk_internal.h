@@ -38,6 +38,8 @@ struct TcParams {
     // [rows][H] log2-domain log-sum-exp of each output row (max + log2(sum)); NULL = not
     // written. The shared-prefix pass merges its partial with the row through it.
     float* lse;
+    // [ncta + 1] first block of each CTA's range; NULL = equal ranges [c*T/ncta, (c+1)*T/ncta)
+    const int32_t* cta_blk;
     int nu;
     int total_blocks;
     int ncta;

@@ -43,30 +43,74 @@ def test_pool_create_rejects_bad_arguments_before_touching_cuda():
     assert lib.pk_batch_plan(None, 0, None, None, None, None, None, None) == _lib.PK_ERR_INVALID_ARG
 
 
-@pytest.mark.parametrize("blocks,ctas", [([3, 1, 7, 2], 148), ([100] * 64, 148), ([144, 230, 31], 5),
-                                         ([1], 148), (list(range(1, 300)), 148), ([2, 1] * 256, 148)])
-def test_split_kv_partition_is_balanced_and_complete(blocks, ctas):
-    """CTA c owns blocks [c*T/n, (c+1)*T/n): every block once, sizes differ by at most 1,
-    n = max(1, min(max_ctas, T, max(T // 16, ceil(units / 3)))) so no CTA is empty, and a
-    CTA gets 16 blocks or more unless the units are many and short."""
+def _partition(blocks, ctas, switch):
     lib = _lib.load()
     b = np.asarray(blocks, dtype=np.int64)
     T = int(b.sum())
     n = max(1, min(ctas, T, max(T // 16, -(-len(b) // 3))))
-    first = np.zeros(n + 1, dtype=np.int64)
+    first = np.full(n + 1, -1, dtype=np.int64)
     got = C.c_int()
-    assert lib.pk_plan_partition(b.ctypes.data_as(C.POINTER(C.c_int64)), len(b), ctas,
+    assert lib.pk_plan_partition(b.ctypes.data_as(C.POINTER(C.c_int64)), len(b), ctas, switch,
                                  first.ctypes.data_as(C.POINTER(C.c_int64)), C.byref(got)) == 0
-    assert got.value == n and first[0] == 0 and first[-1] == T
-    sizes = np.diff(first)
-    assert sizes.min() == T // n and sizes.max() - sizes.min() <= 1
-    if T // 16 >= -(-len(b) // 3):  # block-driven count
-        assert sizes.min() >= min(T, 16)
+    return T, n, first[:got.value + 1], got.value
+
+
+def _range_cost(bounds, b, e, switch):
+    """Blocks of [b, e) plus `switch` per unit boundary strictly inside it."""
+    return (e - b) + switch * int(np.count_nonzero((bounds > b) & (bounds < e)))
+
+
+def _optimum(blocks, n, switch):
+    """Smallest achievable largest range cost with at most n non-empty ranges (exact DP)."""
+    ub = np.concatenate([[0], np.cumsum(blocks)])
+    T, inner = int(ub[-1]), ub[1:-1]
+    inf = float("inf")
+    best = [0.0] + [inf] * T  # best[e]: min max cost covering [0, e) with k ranges
+    out = inf
+    for _ in range(n):
+        nxt = [inf] * (T + 1)
+        for e in range(1, T + 1):
+            nxt[e] = min((max(best[b], _range_cost(inner, b, e, switch)) for b in range(e) if best[b] < inf),
+                         default=inf)
+        best = nxt
+        out = min(out, best[T])
+    return out
+
+
+@pytest.mark.parametrize("blocks,ctas", [([3, 1, 7, 2], 148), ([100] * 64, 148), ([144, 230, 31], 5),
+                                         ([1], 148), (list(range(1, 300)), 148), ([2, 1] * 256, 148)])
+@pytest.mark.parametrize("switch", [0, 6])
+def test_split_kv_partition_is_complete(blocks, ctas, switch):
+    """Every block once in contiguous, non-empty CTA ranges, at most
+    n = max(1, min(max_ctas, T, max(T // 16, ceil(units / 3)))) of them; with no unit cost
+    the largest range is ceil(T / n) blocks, the least possible."""
+    T, n, first, used = _partition(blocks, ctas, switch)
+    assert 1 <= used <= n and first[0] == 0 and first[-1] == T
+    assert np.all(np.diff(first) > 0)
+    if switch == 0:
+        assert np.diff(first).max() == -(-T // n)
+
+
+@pytest.mark.parametrize("seed", range(6))
+@pytest.mark.parametrize("switch", [0, 2, 6])
+def test_split_kv_partition_minimises_the_largest_cost(seed, switch):
+    """The cut's largest cost (blocks + switch per unit boundary inside a range) equals the
+    optimum over all cuts into at most n ranges, found by exhaustive dynamic programming."""
+    rng = np.random.default_rng(seed)
+    blocks = rng.integers(1, 25, rng.integers(2, 9)).tolist()
+    ctas = int(rng.integers(2, 7))
+    T, n, first, used = _partition(blocks, ctas, switch)
+    inner = np.cumsum(blocks)[:-1]
+    worst = max(_range_cost(inner, int(first[c]), int(first[c + 1]), switch) for c in range(used))
+    assert worst == _optimum(blocks, n, switch), (blocks, n, switch, first)
 
 
 def test_partition_rejects_empty_units():
     lib = _lib.load()
     b = np.array([2, 0, 3], dtype=np.int64)
     n = C.c_int()
-    assert lib.pk_plan_partition(b.ctypes.data_as(C.POINTER(C.c_int64)), 3, 8, None, C.byref(n)) \
+    assert lib.pk_plan_partition(b.ctypes.data_as(C.POINTER(C.c_int64)), 3, 8, 0, None, C.byref(n)) \
+        == _lib.PK_ERR_INVALID_ARG
+    ok = np.array([2, 1, 3], dtype=np.int64)
+    assert lib.pk_plan_partition(ok.ctypes.data_as(C.POINTER(C.c_int64)), 3, 8, -1, None, C.byref(n)) \
         == _lib.PK_ERR_INVALID_ARG
