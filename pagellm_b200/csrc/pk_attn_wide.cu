@@ -406,7 +406,6 @@ __global__ void __launch_bounds__(kWThreads, 1)
         int n = 0;  // running key-tile count
         for (int si = s_begin; si < s_end; ++si) {
             const Seg sg = load_seg(p.seg, si);
-            const int k = si - s_begin;
             const int h = sg.head;
             const int item = p.w_pair[2 * sg.pair + tile];
             const int ntok = item >= 0 ? p.w_ntok[item] : 0;
@@ -552,7 +551,17 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 ok = __all_sync(0xffffffffu, done) && !*abort_flag;
             }
             // ---- epilogue
+            // O leaves TMEM one row per thread; the rows go to global memory through the 4 KB
+            // of the tile's Q buffer that hold this warp's own 32 Q rows (dimensions 0-63):
+            // every S MMA that read Q_t has completed, and this warp writes its next Q rows
+            // only after this. 32 columns at a time, so that each store (and, in the
+            // shared-prefix pass, each load of the split-KV row) covers 128 contiguous bytes
+            // of 4 rows instead of 16 bytes of 32 rows. float4 slot i of staging row r sits at
+            // slot i ^ (r & 7): conflict-free both ways.
             if (ok) tc_fence_after();
+            float* stg = reinterpret_cast<float*>(smem + kOffQ + tile * kQBytes + q4 * 4096);
+            auto stg4 = [&](int row, int i) { return reinterpret_cast<float4*>(stg + row * 32 + 4 * (i ^ (row & 7))); };
+            const int sub = lane >> 3, cq = lane & 7;  // transposed: row 4*kk + sub, 4 columns at 4*cq
             if (sg.slot < 0) {
                 // Final rows: o / l, or, in the shared-prefix pass, merged with the row the
                 // split-KV kernel wrote (normalised, log-sum-exp lse_s):
@@ -567,47 +576,71 @@ __global__ void __launch_bounds__(kWThreads, 1)
                     wo = a * inv;
                     wr = b * inv;
                 }
-                float* op = p.out + oidx * kWD;
+                // the rows this lane stores in the transposed pass: their output offsets,
+                // liveness and split-KV weights, from the lanes that own them
+                const unsigned long long oidx64 = oidx;
+                float* orow[8];
+                float wrr[8];
+                bool liv[8];
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const int src = 4 * kk + sub;
+                    const unsigned long long oi = __shfl_sync(0xffffffffu, oidx64, src);
+                    orow[kk] = p.out + static_cast<size_t>(oi) * kWD + 4 * cq;
+                    wrr[kk] = __shfl_sync(0xffffffffu, wr, src);
+                    liv[kk] = __shfl_sync(0xffffffffu, live ? 1 : 0, src) != 0;
+                }
 #pragma unroll 1
                 for (int c = 0; c < kWD / 32 && ok; ++c) {
-                    float4 y[8];
-                    if (p.lse != nullptr && live) {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) y[i] = *reinterpret_cast<const float4*>(op + c * 32 + 4 * i);
-                    }
                     float o[32];
                     tmem_ld32(tO + c * 32, o);
                     tmem_wait_ld();
-                    if (live) {
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            float4 x = make_float4(o[4 * i] * wo, o[4 * i + 1] * wo, o[4 * i + 2] * wo, o[4 * i + 3] * wo);
-                            if (p.lse != nullptr) {
-                                x.x += y[i].x * wr;
-                                x.y += y[i].y * wr;
-                                x.z += y[i].z * wr;
-                                x.w += y[i].w * wr;
-                            }
-                            *reinterpret_cast<float4*>(op + c * 32 + 4 * i) = x;
-                        }
+                    for (int i = 0; i < 8; ++i)
+                        *stg4(lane, i) = make_float4(o[4 * i] * wo, o[4 * i + 1] * wo, o[4 * i + 2] * wo, o[4 * i + 3] * wo);
+                    __syncwarp();
+                    float4 y[8];
+                    if (p.lse != nullptr) {
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk)
+                            y[kk] = liv[kk] ? *reinterpret_cast<const float4*>(orow[kk] + c * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        float4 x = *stg4(4 * kk + sub, cq);
+                        if (p.lse != nullptr) {
+                            x.x += y[kk].x * wrr[kk];
+                            x.y += y[kk].y * wrr[kk];
+                            x.z += y[kk].z * wrr[kk];
+                            x.w += y[kk].w * wrr[kk];
+                        }
+                        if (liv[kk]) *reinterpret_cast<float4*>(orow[kk] + c * 32) = x;
+                    }
+                    __syncwarp();
                 }
             } else if (ok) {
                 // Partial: un-normalised O and (max, sum) of this row into the pair-head's
-                // slot; wide_merge_kernel combines the slots afterwards.
-                const size_t prow = (static_cast<size_t>(sg.slot) * 2 + tile) * kWRows + r;
-                float* po = p.part_o + prow * kWD;
+                // slot; wide_merge_kernel combines the slots afterwards. The warp's 32 slot
+                // rows are consecutive.
+                const size_t prow0 = (static_cast<size_t>(sg.slot) * 2 + tile) * kWRows + 32 * q4;
+                float* po = p.part_o + prow0 * kWD + 4 * cq;
 #pragma unroll 1
                 for (int c = 0; c < kWD / 32; ++c) {
                     float o[32];
                     tmem_ld32(tO + c * 32, o);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4*>(po + c * 32 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+                    for (int i = 0; i < 8; ++i)
+                        *stg4(lane, i) = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                    __syncwarp();
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        *reinterpret_cast<float4*>(po + static_cast<size_t>(4 * kk + sub) * kWD + c * 32) =
+                            *stg4(4 * kk + sub, cq);
+                    __syncwarp();
                 }
-                p.part_ml[prow * 2] = m;
-                p.part_ml[prow * 2 + 1] = l;
+                p.part_ml[(prow0 + lane) * 2] = m;
+                p.part_ml[(prow0 + lane) * 2 + 1] = l;
             }
             tc_fence_before();
             __syncwarp();
