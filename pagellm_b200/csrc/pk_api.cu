@@ -11,6 +11,8 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <queue>
+#include <array>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -625,26 +627,52 @@ void build_wide_schedule(pk_batch* B) {
     if (W > 0) {
         const int64_t G = std::max<int64_t>(1, std::min<int64_t>(P->num_sms, W / kWideMinTilesPerCta));
         const size_t seg0 = B->seg.size() / 6;
-        // pair-heads in order: [base, base + T) of the work axis
-        int x = B->npair_chunk, h = 0;
-        int64_t base = 0;
-        for (int64_t c = 0; c < G; ++c) {
-            const int64_t lo = c * W / G, hi = (c + 1) * W / G;
-            int64_t pos = lo;
-            while (pos < hi) {
-                const int64_t T = tiles(x);
-                const int64_t a = pos - base, b = std::min<int64_t>(hi - base, T);
-                // pair-head index: the chunk pair-heads come first
-                const int ph = B->ncta_chunk + (x - B->npair_chunk) * kvh + h;
-                add_seg(x, h, static_cast<int>(a), static_cast<int>(b), 0, ph);
-                pos = base + b;
-                if (b == T) {
-                    base += T;
-                    if (++h == kvh) {
-                        h = 0;
-                        ++x;
-                    }
-                }
+        // Whole pair-heads first: longest first, each to the least-loaded CTA that stays
+        // within ceil(W / G) tiles (a whole pair-head needs no partial and no merge). The
+        // pair-heads that fit nowhere are cut into pieces that fill the CTAs' spare
+        // capacity in CTA order, so the makespan is the same ceil(W / G) as an even cut,
+        // while only those few pair-heads leave partials for the merge.
+        const int nphp = B->npair_prefix * kvh;
+        auto ph_tiles = [&](int q) { return static_cast<int64_t>(tiles(B->npair_chunk + q / kvh)); };
+        const int64_t target = (W + G - 1) / G;
+        std::vector<int> order(nphp);
+        for (int q = 0; q < nphp; ++q) order[q] = q;
+        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return ph_tiles(a) > ph_tiles(b); });
+        std::vector<int64_t> load(G, 0);
+        std::vector<std::vector<std::array<int64_t, 3>>> segs_of(G);  // {q, t0, t1}
+        using LoadCta = std::pair<int64_t, int64_t>;                   // (load, cta), min-heap
+        std::priority_queue<LoadCta, std::vector<LoadCta>, std::greater<LoadCta>> heap;
+        for (int64_t c = 0; c < G; ++c) heap.push({0, c});
+        std::vector<int> rest;
+        for (int q : order) {
+            const LoadCta top = heap.top();
+            if (top.first + ph_tiles(q) <= target) {
+                heap.pop();
+                segs_of[top.second].push_back({q, 0, ph_tiles(q)});
+                load[top.second] = top.first + ph_tiles(q);
+                heap.push({load[top.second], top.second});
+            } else {
+                rest.push_back(q);
+            }
+        }
+        std::sort(rest.begin(), rest.end());
+        int64_t c = 0;
+        for (int q : rest) {
+            int64_t t = 0;
+            const int64_t T = ph_tiles(q);
+            while (t < T) {
+                while (c + 1 < G && load[c] >= target) ++c;  // the last CTA takes any rounding rest
+                const int64_t take = std::max<int64_t>(1, std::min<int64_t>(T - t, target - load[c]));
+                segs_of[c].push_back({q, t, t + take});
+                load[c] += take;
+                t += take;
+            }
+        }
+        for (int64_t cc = 0; cc < G; ++cc) {
+            for (const auto& sg : segs_of[cc]) {
+                const int q = static_cast<int>(sg[0]);
+                add_seg(B->npair_chunk + q / kvh, q % kvh, static_cast<int>(sg[1]), static_cast<int>(sg[2]), 0,
+                        B->ncta_chunk + q);
             }
             B->cta_seg.push_back(static_cast<int32_t>(B->seg.size() / 6));
         }
