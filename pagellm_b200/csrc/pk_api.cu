@@ -964,14 +964,12 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
     }
     if (B->nwide > 0) {
         if (k_new != nullptr) {
-            if (B->rows_pending) {
-                PK_CUDA(ensure_rows(B, ws));
-                B->launches++;
-            }
             PK_CUDA(prof_begin(B, ws));
-            PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_new, v_new,
-                                      B->slots(), B->plan.at<int32_t>(10),
-                                      static_cast<int64_t>(B->w_rows.size()), P->kvh * P->d, ws));
+            PK_CUDA(pk::launch_append_table(P->dtype, P->k_layer(layer), P->v_layer(layer), k_new, v_new,
+                                            B->meta.at<int32_t>(4), B->meta.at<int32_t>(3), B->meta.at<int32_t>(2),
+                                            B->meta.at<int32_t>(0), B->meta.at<int32_t>(1), P->block_size,
+                                            B->plan.at<int32_t>(10), static_cast<int64_t>(B->w_rows.size()),
+                                            P->kvh * P->d, ws));
             PK_CUDA(prof_end(B, kProfAppend, ws));
             B->launches++;
         }
@@ -1487,15 +1485,13 @@ int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* 
         return attend_impl(B, layer, n_heads, q_dev, out_dev, st, k_dev, v_dev);
     if (B->nrows > 0) {
         const bool listed = !B->app_rows.empty();
-        if (B->rows_pending) {
-            PK_CUDA(ensure_rows(B, st));
-            B->launches++;
-        }
         PK_CUDA(prof_begin(B, st));
-        PK_CUDA(pk::launch_append(P->dtype, P->k_layer(layer), P->v_layer(layer), k_dev, v_dev,
-                                  B->slots(), listed ? B->meta.at<int32_t>(5) : nullptr,
-                                  listed ? static_cast<int64_t>(B->app_rows.size()) : B->nrows,
-                                  P->kvh * P->d, st));
+        PK_CUDA(pk::launch_append_table(P->dtype, P->k_layer(layer), P->v_layer(layer), k_dev, v_dev,
+                                        B->meta.at<int32_t>(4), B->meta.at<int32_t>(3), B->meta.at<int32_t>(2),
+                                        B->meta.at<int32_t>(0), B->meta.at<int32_t>(1), P->block_size,
+                                        listed ? B->meta.at<int32_t>(5) : nullptr,
+                                        listed ? static_cast<int64_t>(B->app_rows.size()) : B->nrows,
+                                        P->kvh * P->d, st));
         PK_CUDA(prof_end(B, kProfAppend, st));
         B->launches++;
     }

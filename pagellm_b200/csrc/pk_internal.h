@@ -170,6 +170,12 @@ cudaError_t launch_plan_rows(const int32_t* row_seq, const int32_t* offsets, con
 cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k,
                           const float* v, const int64_t* slots, const int32_t* rows, int64_t n,
                           int rowlen, cudaStream_t st);
+// The same with each row's slot resolved from the block table (row -> sequence -> position
+// -> block id), with no per-row slots array.
+cudaError_t launch_append_table(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k,
+                                const float* v, const int32_t* row_seq, const int32_t* offsets,
+                                const int32_t* starts, const int32_t* indptr, const int32_t* ids, int bs,
+                                const int32_t* rows, int64_t n, int rowlen, cudaStream_t st);
 cudaError_t launch_copy_blocks(void* k, void* v, const int64_t* pairs, int64_t npairs, int layers,
                                int64_t layer_bytes, int64_t block_bytes, cudaStream_t st);
 cudaError_t launch_bounded_wait_selftest(int* err, unsigned long long limit_ns, cudaStream_t st);

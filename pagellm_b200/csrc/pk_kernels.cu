@@ -59,12 +59,30 @@ __device__ __forceinline__ void store4(__nv_bfloat16* dst, float4 x) {
 __device__ __forceinline__ void store1(float* dst, float x) { *dst = x; }
 __device__ __forceinline__ void store1(__nv_bfloat16* dst, float x) { *dst = __float2bfloat16_rn(x); }
 
+// Where row r of the step goes: its slot from the per-row slots array, or resolved from the
+// block table (position starts[s] + r - offsets[s] of its sequence s, paged.py:412-424), so
+// that the append needs no separate per-row planning launch.
+struct SlotsArray {
+    const int64_t* slots;
+    __device__ __forceinline__ int64_t operator()(int64_t r) const { return slots[r]; }
+};
+struct SlotsTable {
+    const int32_t *row_seq, *offsets, *starts, *indptr, *ids;
+    int bs;
+    __device__ __forceinline__ int64_t operator()(int64_t r) const {
+        const int s = row_seq[r];
+        const int64_t pos = static_cast<int64_t>(starts[s]) + (r - offsets[s]);
+        const int64_t blk = pos / bs;
+        return static_cast<int64_t>(ids[indptr[s] + blk]) * bs + (pos - blk * bs);
+    }
+};
+
 // rows == NULL: rows 0..n-1; otherwise only the listed rows (used when several rows of a
 // step share a slot: the list then holds the last writer of each slot).
-template <typename T>
+template <typename T, typename Slot>
 __global__ void append_vec4_kernel(T* __restrict__ pk_, T* __restrict__ pv_,
                                    const float* __restrict__ k, const float* __restrict__ v,
-                                   const int64_t* __restrict__ slots, const int32_t* __restrict__ rows,
+                                   const Slot slot, const int32_t* __restrict__ rows,
                                    int64_t n, int rowlen) {
     const int per_row = rowlen / 4;
     const int64_t total = n * per_row;
@@ -73,16 +91,18 @@ __global__ void append_vec4_kernel(T* __restrict__ pk_, T* __restrict__ pv_,
         const int64_t ri = i / per_row;
         const int c = static_cast<int>(i - ri * per_row) * 4;
         const int64_t r = rows ? rows[ri] : ri;
-        const int64_t dst = slots[r] * rowlen + c;
-        store4(pk_ + dst, *reinterpret_cast<const float4*>(k + r * rowlen + c));
-        store4(pv_ + dst, *reinterpret_cast<const float4*>(v + r * rowlen + c));
+        const float4 kx = *reinterpret_cast<const float4*>(k + r * rowlen + c);
+        const float4 vx = *reinterpret_cast<const float4*>(v + r * rowlen + c);
+        const int64_t dst = slot(r) * rowlen + c;
+        store4(pk_ + dst, kx);
+        store4(pv_ + dst, vx);
     }
 }
 
-template <typename T>
+template <typename T, typename Slot>
 __global__ void append_scalar_kernel(T* __restrict__ pk_, T* __restrict__ pv_,
                                      const float* __restrict__ k, const float* __restrict__ v,
-                                     const int64_t* __restrict__ slots, const int32_t* __restrict__ rows,
+                                     const Slot slot, const int32_t* __restrict__ rows,
                                      int64_t n, int rowlen) {
     const int64_t total = n * rowlen;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -90,8 +110,9 @@ __global__ void append_scalar_kernel(T* __restrict__ pk_, T* __restrict__ pv_,
         const int64_t ri = i / rowlen;
         const int c = static_cast<int>(i - ri * rowlen);
         const int64_t r = rows ? rows[ri] : ri;
-        store1(pk_ + slots[r] * rowlen + c, k[r * rowlen + c]);
-        store1(pv_ + slots[r] * rowlen + c, v[r * rowlen + c]);
+        const int64_t dst = slot(r) * rowlen + c;
+        store1(pk_ + dst, k[r * rowlen + c]);
+        store1(pv_ + dst, v[r * rowlen + c]);
     }
 }
 
@@ -246,9 +267,9 @@ cudaError_t launch_slot_mapping(const int32_t* table, int64_t table_len, const i
     return cudaGetLastError();
 }
 
-cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k,
-                          const float* v, const int64_t* slots, const int32_t* rows, int64_t n,
-                          int rowlen, cudaStream_t st) {
+template <typename Slot>
+cudaError_t launch_append_t(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k, const float* v,
+                            const Slot& slot, const int32_t* rows, int64_t n, int rowlen, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
     // 4-wide path only when every row start is 16-byte aligned on both sides.
     const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
@@ -258,15 +279,29 @@ cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, con
     if (dtype == 0) {
         float* pk_ = static_cast<float*>(pool_k_layer);
         float* pv_ = static_cast<float*>(pool_v_layer);
-        if (vec) append_vec4_kernel<float><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, rows, n, rowlen);
-        else append_scalar_kernel<float><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, rows, n, rowlen);
+        if (vec) append_vec4_kernel<float, Slot><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slot, rows, n, rowlen);
+        else append_scalar_kernel<float, Slot><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slot, rows, n, rowlen);
     } else {
         auto* pk_ = static_cast<__nv_bfloat16*>(pool_k_layer);
         auto* pv_ = static_cast<__nv_bfloat16*>(pool_v_layer);
-        if (vec) append_vec4_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, rows, n, rowlen);
-        else append_scalar_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slots, rows, n, rowlen);
+        if (vec) append_vec4_kernel<__nv_bfloat16, Slot><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slot, rows, n, rowlen);
+        else append_scalar_kernel<__nv_bfloat16, Slot><<<grid, 256, 0, st>>>(pk_, pv_, k, v, slot, rows, n, rowlen);
     }
     return cudaGetLastError();
+}
+
+cudaError_t launch_append(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k,
+                          const float* v, const int64_t* slots, const int32_t* rows, int64_t n,
+                          int rowlen, cudaStream_t st) {
+    return launch_append_t(dtype, pool_k_layer, pool_v_layer, k, v, SlotsArray{slots}, rows, n, rowlen, st);
+}
+
+cudaError_t launch_append_table(int dtype, void* pool_k_layer, void* pool_v_layer, const float* k,
+                                const float* v, const int32_t* row_seq, const int32_t* offsets,
+                                const int32_t* starts, const int32_t* indptr, const int32_t* ids, int bs,
+                                const int32_t* rows, int64_t n, int rowlen, cudaStream_t st) {
+    return launch_append_t(dtype, pool_k_layer, pool_v_layer, k, v,
+                           SlotsTable{row_seq, offsets, starts, indptr, ids, bs}, rows, n, rowlen, st);
 }
 
 cudaError_t launch_copy_blocks(void* k, void* v, const int64_t* pairs, int64_t npairs, int layers,
