@@ -125,9 +125,6 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
         fence_mbar_init();
     }
     __syncthreads();
-    // Let a programmatically dependent launch (the partial merge) be scheduled now: its CTAs
-    // fit beside this one on each SM and can load their metadata while this grid runs.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     const int c = blockIdx.x;
     const int lo = p.cta_blk ? p.cta_blk[c] : static_cast<int>(static_cast<int64_t>(c) * p.total_blocks / p.ncta);
@@ -567,66 +564,6 @@ __global__ void merge_kernel(const MergeParams p) {
     }
 }
 
-// Merge of split units launched as a programmatic dependent of the attention kernel: one
-// CTA per split unit, one warp per KV head. Metadata is read before griddepcontrol.wait
-// (it does not come from the attention kernel); the partials after it, when the attention
-// grid has completed and its writes are visible. Each lane owns up to four
-// (column, 4-dim chunk) items so one segment's loads are in flight together.
-__global__ void __launch_bounds__(kTcMaxKvHeads * 32) merge_pdl_kernel(const MergeParams p) {
-    const int e = blockIdx.x;
-    const int h = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int u = p.split_u[e];
-    const int c0 = p.split_c0[e];
-    const int c1 = p.split_c1[e];
-    const int row0 = p.offsets[p.u_seq[u]] + p.u_t0[u];
-    const int ncols = p.u_n[u] * p.g;
-    const int chunks = p.D / 4;
-    const int items = ncols * chunks;
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int base = 0; base < items; base += 128) {
-        float M[4], L[4];
-        float4 O[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            M[k] = -INFINITY;
-            L[k] = 0.f;
-            O[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        for (int c = c0; c <= c1; ++c) {
-            const size_t seg = (static_cast<size_t>(u) + c) * p.kvh + h;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int it = base + lane + 32 * k;
-                if (it >= items) continue;
-                const size_t idx = seg * kMaxCols + it / chunks;
-                const float ms = p.part_ml[idx * 2];
-                const float ls = p.part_ml[idx * 2 + 1];
-                const float4 os = reinterpret_cast<const float4*>(p.part_o + idx * p.D)[it % chunks];
-                const float mn = fmaxf(M[k], ms);
-                const float a = M[k] == -INFINITY ? 0.f : exp2f(M[k] - mn);
-                const float b = ms == -INFINITY ? 0.f : exp2f(ms - mn);
-                L[k] = L[k] * a + ls * b;
-                O[k].x = O[k].x * a + os.x * b;
-                O[k].y = O[k].y * a + os.y * b;
-                O[k].z = O[k].z * a + os.z * b;
-                O[k].w = O[k].w * a + os.w * b;
-                M[k] = mn;
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int it = base + lane + 32 * k;
-            if (it >= items) continue;
-            const int col = it / chunks;
-            const float inv = 1.f / L[k];
-            float* op = p.out + (static_cast<size_t>(row0 + col / p.g) * p.H + h * p.g + col % p.g) * p.D;
-            reinterpret_cast<float4*>(op)[it % chunks] =
-                make_float4(O[k].x * inv, O[k].y * inv, O[k].z * inv, O[k].w * inv);
-        }
-    }
-}
-
 template <int D, int NT>
 cudaError_t launch_tc_t(const CUtensorMap* tmk, const CUtensorMap* tmv, const TcParams& p,
                         size_t smem, cudaStream_t st) {
@@ -672,21 +609,6 @@ cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUt
     if (D == 128 && NT == 2) return launch_tc_t<128, 2>(tmk, tmv, p, smem, st);
     if (D == 256 && NT == 1) return launch_tc_t<256, 1>(tmk, tmv, p, smem, st);
     return cudaErrorInvalidValue;
-}
-
-cudaError_t launch_merge_dependent(const MergeParams& p, int nsplit, cudaStream_t st) {
-    if (nsplit <= 0) return cudaSuccess;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nsplit);
-    cfg.blockDim = dim3(p.kvh * 32);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, merge_pdl_kernel, p);
 }
 
 cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st) {

@@ -161,8 +161,6 @@ cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tm
 // Combines the partial slots of (pair, head)s cut between wide-kernel CTAs:
 // split = [nsplit][4] pair, head, first slot, slots.
 cudaError_t launch_wide_merge(const WideParams& p, const int32_t* split, int nsplit, cudaStream_t st);
-// Same merge as a programmatic dependent launch of the preceding attention kernel.
-cudaError_t launch_merge_dependent(const MergeParams& p, int nsplit, cudaStream_t st);
 cudaError_t launch_generic_attention(int dtype, const GenericParams& p, cudaStream_t st);
 cudaError_t launch_plan_rows(const int32_t* row_seq, const int32_t* offsets, const int32_t* starts,
                              const int32_t* indptr, const int32_t* ids, int bs, int64_t nrows,
