@@ -250,7 +250,7 @@ struct pk_batch {
     // Wide-tile work runs on a side stream, forked from and joined back into the caller's
     // stream with events, so it overlaps the split-KV kernel.
     cudaStream_t side = nullptr;
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_pack = nullptr;
     DevBuf rows;    // positions [nrows] then slots [nrows]
     DevBuf err;     // one int
     // attention plan for plan_H query heads
@@ -274,6 +274,7 @@ struct pk_batch {
     std::vector<int32_t> pair_kend, cta_seg, seg, ph_info, split;
     int ncta_chunk = 0, ncta_prefix = 0, nslots = 0, nph = 0, nwsplit = 0;
     DevBuf wpart;  // partial O and (max, sum) of pair-heads cut between CTAs
+    DevBuf qpk;    // packed bf16 query tiles of the wide-tile items (+1 zero tile)
     std::vector<int32_t> u_kb0;    // per unit: first block read (after a shared prefix)
     std::vector<int32_t> seq_kb0;  // scratch: per sequence
     int tc_max_new = 0;            // most new tokens of a sequence on the split-KV kernel
@@ -859,6 +860,8 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan.add(B->cta_blk.data(), B->cta_blk.size() * 4);
     if (B->nslots > 0)
         PK_CUDA(B->wpart.reserve(static_cast<size_t>(B->nslots) * 2 * 128 * (128 + 2) * sizeof(float)));
+    if (!B->w_seq.empty())
+        PK_CUDA(B->qpk.reserve((B->w_seq.size() * P->kvh + 1) * static_cast<size_t>(pk::kWideQTileBytes)));
     if (B->nprefix > 0) PK_CUDA(B->lse.reserve(static_cast<size_t>(B->nrows) * H * sizeof(float)));
     int rc = B->plan.commit(st);
     if (rc != PK_OK) return rc;
@@ -920,6 +923,8 @@ pk::WideParams wide_params(pk_batch* B, int layer, int H, const float* q, float*
     w.pair_kend = B->plan.at<int32_t>(17);
     w.cta_seg = B->plan.at<int32_t>(18) + first;
     w.seg = B->plan.at<int32_t>(19);
+    w.qpk = static_cast<const uint8_t*>(B->qpk.ptr);
+    w.q_zero_tile = static_cast<int>(B->w_seq.size()) * P->kvh;
     w.part_o = static_cast<float*>(B->wpart.ptr);
     w.part_ml = static_cast<float*>(B->wpart.ptr) + static_cast<size_t>(B->nslots) * 2 * 128 * 128;
     w.tok_row = B->plan.at<int32_t>(13);
@@ -954,24 +959,57 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
     const int g = H / P->kvh;
     // ---- wide-tile part (side stream when split-KV work runs beside it)
     cudaStream_t ws = st;
-    if (B->nwide > 0 && B->use_tc) {
+    const int nitems = B->nwide + B->nprefix;
+    const bool fork = (B->nwide > 0 || B->nprefix > 0) && B->use_tc;
+    if (fork) {
         if (!B->side) PK_CUDA(cudaStreamCreateWithFlags(&B->side, cudaStreamNonBlocking));
         if (!B->ev_fork) PK_CUDA(cudaEventCreateWithFlags(&B->ev_fork, cudaEventDisableTiming));
         if (!B->ev_join) PK_CUDA(cudaEventCreateWithFlags(&B->ev_join, cudaEventDisableTiming));
+        if (!B->ev_pack) PK_CUDA(cudaEventCreateWithFlags(&B->ev_pack, cudaEventDisableTiming));
         PK_CUDA(cudaEventRecord(B->ev_fork, st));
         PK_CUDA(cudaStreamWaitEvent(B->side, B->ev_fork, 0));
-        ws = B->side;
+        if (B->nwide > 0) ws = B->side;
+    }
+    // Query tiles of every wide item are packed once (bf16 shared-memory images the wide
+    // kernel fetches with one bulk copy). With chunk items that happens in the same launch
+    // as the chunk rows' append, on the wide stream; with only a shared-prefix pass the pack
+    // runs on the side stream beside the split-KV kernel (or first, without one).
+    bool pack_on_side = false;
+    if (B->nwide == 0 && B->nprefix > 0) {
+        const pk::WideParams wp = wide_params(B, layer, H, q, out, 0, 0, nullptr);
+        cudaStream_t ps = fork ? B->side : st;
+        PK_CUDA(pk::launch_wide_q_pack(wp, nitems, static_cast<uint8_t*>(B->qpk.ptr), ps));
+        B->launches++;
+        if (ps != st) {
+            PK_CUDA(cudaEventRecord(B->ev_pack, ps));
+            pack_on_side = true;
+        }
     }
     if (B->nwide > 0) {
+        const pk::WideParams wp = wide_params(B, layer, H, q, out, 0, 0, nullptr);
+        pk::WideAppend a{};
         if (k_new != nullptr) {
-            PK_CUDA(prof_begin(B, ws));
-            PK_CUDA(pk::launch_append_table(P->dtype, P->k_layer(layer), P->v_layer(layer), k_new, v_new,
-                                            B->meta.at<int32_t>(4), B->meta.at<int32_t>(3), B->meta.at<int32_t>(2),
-                                            B->meta.at<int32_t>(0), B->meta.at<int32_t>(1), P->block_size,
-                                            B->plan.at<int32_t>(10), static_cast<int64_t>(B->w_rows.size()),
-                                            P->kvh * P->d, ws));
-            PK_CUDA(prof_end(B, kProfAppend, ws));
-            B->launches++;
+            a.pool_k = reinterpret_cast<__nv_bfloat16*>(P->k_layer(layer));
+            a.pool_v = reinterpret_cast<__nv_bfloat16*>(P->v_layer(layer));
+            a.k = k_new;
+            a.v = v_new;
+            a.row_seq = B->meta.at<int32_t>(4);
+            a.offsets = B->meta.at<int32_t>(3);
+            a.starts = B->meta.at<int32_t>(2);
+            a.indptr = B->meta.at<int32_t>(0);
+            a.ids = B->meta.at<int32_t>(1);
+            a.rows = B->plan.at<int32_t>(10);
+            a.n = static_cast<int64_t>(B->w_rows.size());
+            a.rowlen = P->kvh * P->d;
+            a.bs = P->block_size;
+        }
+        PK_CUDA(prof_begin(B, ws));
+        PK_CUDA(pk::launch_wide_prep(wp, nitems, static_cast<uint8_t*>(B->qpk.ptr), a, ws));
+        PK_CUDA(prof_end(B, kProfAppend, ws));
+        B->launches++;
+        if (B->nprefix > 0 && ws != st) {
+            PK_CUDA(cudaEventRecord(B->ev_pack, ws));
+            pack_on_side = true;
         }
         const pk::WideParams w = wide_params(B, layer, H, q, out, 0, B->ncta_chunk, nullptr);
         PK_CUDA(prof_begin(B, ws));
@@ -1043,6 +1081,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         // shared-prefix items: after the split-KV kernel has written the rows they merge into
         const pk::WideParams w = wide_params(B, layer, H, q, out, B->ncta_chunk, B->ncta_prefix,
                                              static_cast<const float*>(B->lse.ptr));
+        if (pack_on_side) PK_CUDA(cudaStreamWaitEvent(st, B->ev_pack, 0));
         PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, st));
         if (B->nwsplit > 0) {
@@ -1052,8 +1091,10 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         PK_CUDA(prof_end(B, kProfWide, st));
         B->launches++;
     }
-    if (ws != st) {
-        PK_CUDA(cudaEventRecord(B->ev_join, ws));
+    if (fork) {
+        // everything issued on the side stream (append, chunk tiles, or the pack) before the
+        // caller's stream moves on
+        PK_CUDA(cudaEventRecord(B->ev_join, B->side));
         PK_CUDA(cudaStreamWaitEvent(st, B->ev_join, 0));
     }
     if (B->ngeneric > 0) {
@@ -1288,9 +1329,11 @@ int pk_batch_destroy(pk_batch* B) {
     B->io.release();
     B->lse.release();
     B->wpart.release();
+    B->qpk.release();
     for (cudaEvent_t e : B->ev_pool) cudaEventDestroy(e);
     if (B->ev_fork) cudaEventDestroy(B->ev_fork);
     if (B->ev_join) cudaEventDestroy(B->ev_join);
+    if (B->ev_pack) cudaEventDestroy(B->ev_pack);
     if (B->side) cudaStreamDestroy(B->side);
     delete B;
     return PK_OK;

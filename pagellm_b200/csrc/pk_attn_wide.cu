@@ -55,6 +55,7 @@ constexpr uint32_t kTmemCols = 512;
 // O_0 [256,384), O_1 [384,512).
 constexpr uint32_t kColO = 2 * kWKeys;
 static_assert(kColO + 2 * kWD <= kTmemCols, "TMEM budget");
+static_assert(kWideQTileBytes == kWRows * kWD * 2, "packed query tile size");
 
 // shared memory carve-up (bytes from a 1024-aligned base)
 constexpr int kQBytes = kWRows * kWD * 2;   // 32 KB per query tile (bf16): [chunk][row][64]
@@ -201,7 +202,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
     uint64_t* sfull = vempty + kVStages;  // [tile]
     uint64_t* pfull = sfull + 2;          // [tile], one arrival per softmax warp
     uint64_t* pvdone = pfull + 2;         // [tile]
-    uint64_t* qfull = pvdone + 2;         // [tile], Q of the next segment in shared memory
+    uint64_t* qfull = pvdone + 2;         // [tile], Q of the next segment in shared memory (bulk copy)
     uint64_t* ofree = qfull + 2;          // [tile], O of the last segment read out of TMEM
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ofree + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
             mbar_init(&sfull[t], 1);
             mbar_init(&pfull[t], 4);
             mbar_init(&pvdone[t], 1);
-            mbar_init(&qfull[t], 4);
+            mbar_init(&qfull[t], 1);
             mbar_init(&ofree[t], 4);
         }
         *abort_flag = 0;
@@ -272,9 +273,32 @@ __global__ void __launch_bounds__(kWThreads, 1)
                         tma_load_4d(dst + c * (kWKeys * 128) + b * p.bs * 128, map, 0, slot0, sg.head, c, bar);
                 }
             };
+            // Q tiles of segment k: one bulk copy per query tile from the packed tiles, issued
+            // once the epilogue of segment k-1 has left that buffer (ofree of both tiles)
+            auto issue_q = [&](int k) {
+                const Seg sg = load_seg(p.seg, s_begin + k);
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    const int item = p.w_pair[2 * sg.pair + t];
+                    const int qt = item >= 0 ? item * p.kvh + sg.head : p.q_zero_tile;
+                    mbar_arrive_expect_tx(&qfull[t], kQBytes);
+                    bulk_load(smem + kOffQ + t * kQBytes, p.qpk + static_cast<size_t>(qt) * kQBytes, kQBytes, &qfull[t]);
+                }
+            };
+            int nq = 0;  // segments whose Q has been issued
+            if (s_begin < s_end) {
+                issue_q(0);
+                nq = 1;
+            }
             unsigned long long idle_since = global_ns();
-            while (vs < s_end) {
+            while (vs < s_end || s_begin + nq < s_end) {
                 bool progressed = false;
+                if (s_begin + nq < s_end && mbar_test_wait(&ofree[0], static_cast<uint32_t>((nq - 1) & 1)) &&
+                    mbar_test_wait(&ofree[1], static_cast<uint32_t>((nq - 1) & 1))) {
+                    issue_q(nq);
+                    ++nq;
+                    progressed = true;
+                }
                 if (ks < s_end && mbar_test_wait(&kempty[nk % kKStages], ((nk / kKStages) & 1u) ^ 1u)) {
                     issue(&tmk, smem + kOffK + (nk % kKStages) * kKVBytes, &kfull[nk % kKStages], sk, kt);
                     ++nk;
@@ -302,6 +326,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 }
             }
             // never leave the CTA with copies still landing in its shared memory
+            if (nq > 0)
+                for (int t = 0; t < 2; ++t) mbar_wait_bounded(&qfull[t], static_cast<uint32_t>((nq - 1) & 1));
             for (int t = max(0, nk - kKStages); t < nk; ++t)
                 mbar_wait_bounded(&kfull[t % kKStages], static_cast<uint32_t>(t / kKStages) & 1u);
             for (int t = max(0, nv - kVStages); t < nv; ++t)
@@ -418,35 +444,6 @@ __global__ void __launch_bounds__(kWThreads, 1)
             const int qlim = live ? min(p.tok_pos[tok0 + t_row], kend_t - 1) : -1;
             const int orow = p.tok_row[tok0 + (live ? t_row : 0)];
             const size_t oidx = static_cast<size_t>(orow) * p.H + h * g + jh;
-            // ---- Q_t -> shared memory: scaled into the exp2 domain, bf16, [chunk][row][64] SW128
-            // (the previous segment's S MMAs, the only readers, have completed: their
-            // sfull phases were consumed below)
-            {
-                // Warp-cooperative and coalesced: the warp's 32 rows, 16 at a time, one 512-byte
-                // row per load instruction (lane = 4 dims), all 16 loads in flight together.
-                uint8_t* qs = smem + kOffQ + tile * kQBytes;
-                const int c = lane >> 4, u = (lane & 15) >> 1, half = lane & 1;
-#pragma unroll 1
-                for (int i0 = 0; i0 < 32; i0 += 16) {
-                    float4 x[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int rowi = __shfl_sync(0xffffffffu, orow, i0 + i);
-                        const bool livei = __shfl_sync(0xffffffffu, live ? 1 : 0, i0 + i) != 0;
-                        const float* qp = p.q + (static_cast<size_t>(rowi) * p.H + h * g + (32 * q4 + i0 + i) % g) * kWD;
-                        x[i] = livei ? __ldg(reinterpret_cast<const float4*>(qp) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const uint2 v = make_uint2(pack_bf16(x[i].x * p.qscale, x[i].y * p.qscale),
-                                                   pack_bf16(x[i].z * p.qscale, x[i].w * p.qscale));
-                        *reinterpret_cast<uint2*>(qs + c * (kWRows * 128) + sw128(32 * q4 + i0 + i, u) + half * 8) = v;
-                    }
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&qfull[tile]);
-            }
             float m = -INFINITY, l = 0.f;
             for (int jt = sg.t0; jt < sg.t1 && ok; ++jt, ++n) {
                 const int kbase = jt * kWKeys;
@@ -642,6 +639,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
                 p.part_ml[(prow0 + lane) * 2] = m;
                 p.part_ml[(prow0 + lane) * 2 + 1] = l;
             }
+            // the staging writes (generic proxy) before the next Q bulk copy into this buffer
+            fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&ofree[tile]);
@@ -736,6 +735,91 @@ cudaError_t launch_wide_merge(const WideParams& p, const int32_t* split, int nsp
     if (nsplit <= 0) return cudaSuccess;
     const int warps = nsplit * 2 * kWRows;
     wide_merge_kernel<<<(warps + 7) / 8, 256, 0, st>>>(p, split, nsplit);
+    return cudaGetLastError();
+}
+
+// Query tiles for the wide-tile kernel, packed once per call: tile item * kvh + h holds the
+// item's 128 rows (token r / g, query head h * g + r % g), scaled into the exp2 domain and
+// rounded to bf16, in the exact shared-memory image the S MMA reads ([64-dim chunk][row]
+// [64], 128-byte swizzle), so that a CTA fetches it with one 32 KB bulk copy. Rows past the
+// item's tokens are zero, and so is the extra last tile (the empty half of a pair).
+__device__ __forceinline__ void pack_q_tile(const WideParams& p, int ntiles, uint8_t* __restrict__ qpk, int b) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* dst = qpk + static_cast<size_t>(b) * kQBytes;
+    const bool real = b < ntiles;
+    const int item = real ? b / p.kvh : 0, h = real ? b % p.kvh : 0;
+    const int ntok = real ? p.w_ntok[item] : 0;
+    const int tok0 = real ? p.w_tok0[item] : 0;
+    const int g = p.g;
+    const int c = lane >> 4, u = (lane & 15) >> 1, half = lane & 1;
+#pragma unroll 1
+    for (int i0 = 0; i0 < 32; i0 += 16) {
+        float4 x[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int r = 32 * warp + i0 + i;
+            x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r / g < ntok) {
+                const int row = p.tok_row[tok0 + r / g];
+                const float* qp = p.q + (static_cast<size_t>(row) * p.H + h * g + r % g) * kWD;
+                x[i] = __ldg(reinterpret_cast<const float4*>(qp) + lane);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int r = 32 * warp + i0 + i;
+            const uint2 v = make_uint2(pack_bf16(x[i].x * p.qscale, x[i].y * p.qscale),
+                                       pack_bf16(x[i].z * p.qscale, x[i].w * p.qscale));
+            *reinterpret_cast<uint2*>(dst + c * (kWRows * 128) + sw128(r, u) + half * 8) = v;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(128) wide_q_pack_kernel(const WideParams p, int ntiles, uint8_t* __restrict__ qpk) {
+    pack_q_tile(p, ntiles, qpk, blockIdx.x);
+}
+
+// The pack and the append of the chunk rows (rows[0..n) of the step, fp32 -> the bf16
+// pool, slot from the block table: sequence row_seq[r], position starts[s] + r - offsets[s])
+// in one launch: CTAs 0..ntiles pack, the rest append 4 dims per thread.
+__global__ void __launch_bounds__(128) wide_prep_kernel(const WideParams p, int ntiles, uint8_t* __restrict__ qpk,
+                                                        const WideAppend a) {
+    if (static_cast<int>(blockIdx.x) <= ntiles) {
+        pack_q_tile(p, ntiles, qpk, blockIdx.x);
+        return;
+    }
+    const int per_row = a.rowlen / 4;
+    const int64_t total = a.n * per_row;
+    for (int64_t i = (blockIdx.x - ntiles - 1) * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x - ntiles - 1) * blockDim.x) {
+        const int64_t ri = i / per_row;
+        const int c = static_cast<int>(i - ri * per_row) * 4;
+        const int64_t r = a.rows[ri];
+        const float4 kx = *reinterpret_cast<const float4*>(a.k + r * a.rowlen + c);
+        const float4 vx = *reinterpret_cast<const float4*>(a.v + r * a.rowlen + c);
+        const int sq = a.row_seq[r];
+        const int64_t pos = static_cast<int64_t>(a.starts[sq]) + (r - a.offsets[sq]);
+        const int64_t blk = pos / a.bs;
+        const int64_t slot = static_cast<int64_t>(a.ids[a.indptr[sq] + blk]) * a.bs + (pos - blk * a.bs);
+        const int64_t dst = slot * a.rowlen + c;
+        *reinterpret_cast<uint2*>(a.pool_k + dst) = make_uint2(pack_bf16(kx.x, kx.y), pack_bf16(kx.z, kx.w));
+        *reinterpret_cast<uint2*>(a.pool_v + dst) = make_uint2(pack_bf16(vx.x, vx.y), pack_bf16(vx.z, vx.w));
+    }
+}
+
+cudaError_t launch_wide_q_pack(const WideParams& p, int nitems, uint8_t* qpk, cudaStream_t st) {
+    if (nitems <= 0) return cudaSuccess;
+    const int ntiles = nitems * p.kvh;
+    wide_q_pack_kernel<<<ntiles + 1, 128, 0, st>>>(p, ntiles, qpk);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_wide_prep(const WideParams& p, int nitems, uint8_t* qpk, const WideAppend& a, cudaStream_t st) {
+    if (nitems <= 0) return cudaSuccess;
+    const int ntiles = nitems * p.kvh;
+    const int64_t items = a.n * (a.rowlen / 4);
+    const int64_t ablocks = std::min<int64_t>((items + 127) / 128, 148 * 16);
+    wide_prep_kernel<<<static_cast<unsigned>(ntiles + 1 + std::max<int64_t>(ablocks, 1)), 128, 0, st>>>(p, ntiles, qpk, a);
     return cudaGetLastError();
 }
 

@@ -122,6 +122,10 @@ struct WideParams {
     const int32_t* seg;        // [segments][6] pair, head, first/end key tile, slot (-1 whole), pair-head
     float* part_o;             // [slots][2][128][128] un-normalised partial O
     float* part_ml;            // [slots][2][128][2] (max, sum), log2 domain
+    // [items * kvh + 1][32 KB] query tiles packed by launch_wide_q_pack (bf16, scaled,
+    // in the shared-memory image the MMA reads); tile item * kvh + head, the last all zero
+    const uint8_t* qpk;
+    int q_zero_tile;
     int nctas;
     int H;
     int kvh;
@@ -158,6 +162,25 @@ cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st);
 size_t wide_smem_bytes();
 cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tmv1, const WideParams& p,
                                   cudaStream_t st);
+// Bytes of one packed query tile of the wide-tile kernel (128 rows x 128 dims, bf16).
+constexpr int kWideQTileBytes = 128 * 128 * 2;
+// Packs the query tiles of `nitems` wide-tile items (all KV heads) plus the zero tile into
+// p.qpk-sized memory at `qpk`.
+cudaError_t launch_wide_q_pack(const WideParams& p, int nitems, uint8_t* qpk, cudaStream_t st);
+// Append of chunk rows into a bf16 pool, slots resolved from the block table.
+struct WideAppend {
+    __nv_bfloat16* pool_k;
+    __nv_bfloat16* pool_v;
+    const float* k;
+    const float* v;
+    const int32_t *row_seq, *offsets, *starts, *indptr, *ids;
+    const int32_t* rows;  // [n] the step rows to append
+    int64_t n;
+    int rowlen;           // kvh * head_dim
+    int bs;
+};
+// launch_wide_q_pack and the append of `a` in one launch (a.n == 0: pack only).
+cudaError_t launch_wide_prep(const WideParams& p, int nitems, uint8_t* qpk, const WideAppend& a, cudaStream_t st);
 // Combines the partial slots of (pair, head)s cut between wide-kernel CTAs:
 // split = [nsplit][4] pair, head, first slot, slots.
 cudaError_t launch_wide_merge(const WideParams& p, const int32_t* split, int nsplit, cudaStream_t st);
