@@ -1116,6 +1116,8 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.D = P->d;
         p.bs = P->block_size;
         p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(P->d)));
+        p.k_new = k_new;  // fused calls only (then every row of the step is on this kernel)
+        p.v_new = v_new;
         PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_generic_attention(P->dtype, p, st));
         PK_CUDA(prof_end(B, kProfGeneric, st));
@@ -1525,6 +1527,10 @@ int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* 
     // decode steps; with several new tokens per sequence one scatter kernel first is faster
     // than each unit fetching its rows on its critical path.
     if (B->ngeneric == 0 && B->fuse_append_ok && (B->use_tc || B->nwide > 0) && B->tc_max_new <= kFuseMaxNew)
+        return attend_impl(B, layer, n_heads, q_dev, out_dev, st, k_dev, v_dev);
+    // A step wholly on the CUDA-core kernel appends inside it as well: its CTAs read the
+    // step's rows from the inputs and one CTA per (row, KV head) stores each to the pool.
+    if (B->ngeneric > 0 && !B->use_tc && B->nwide == 0 && B->fuse_append_ok)
         return attend_impl(B, layer, n_heads, q_dev, out_dev, st, k_dev, v_dev);
     if (B->nrows > 0) {
         const bool listed = !B->app_rows.empty();

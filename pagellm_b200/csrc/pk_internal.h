@@ -91,6 +91,11 @@ struct GenericParams {
     const int32_t* starts;
     const int32_t* offsets;
     const int32_t* rows;  // rows to process (indices into q/out)
+    // Fused append (NULL: off): keys at positions >= the sequence's start are read from these
+    // fp32 rows [step rows][kvh][D] (rounded to the pool type), and the CTA of (row, first
+    // query head of a KV head) stores its row to the pool (pool_k / pool_v layer bases).
+    const float* k_new;
+    const float* v_new;
     int nrows;
     int H;
     int kvh;

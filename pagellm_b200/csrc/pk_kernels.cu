@@ -139,6 +139,28 @@ __global__ void copy_blocks_kernel(uint8_t* __restrict__ k, uint8_t* __restrict_
 __device__ __forceinline__ float load_f(const float* p) { return *p; }
 __device__ __forceinline__ float load_f(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
+// x as the pool would hold it (bf16 pools round to nearest even).
+__device__ __forceinline__ float as_pool(float x, const float*) { return x; }
+__device__ __forceinline__ float as_pool(float x, const __nv_bfloat16*) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Fused append for the CUDA-core kernels: the CTA of (row r, first query head of KV head kh)
+// stores the step's row r (fp32 inputs) to its pool slot; other CTAs read new keys from the
+// inputs, so nothing in the launch reads those slots.
+template <typename T>
+__device__ __forceinline__ void generic_store_new_row(const GenericParams& p, int r, int seq, int kh) {
+    const int64_t pos = static_cast<int64_t>(p.starts[seq]) + (r - p.offsets[seq]);
+    const int64_t blk = pos / p.bs;
+    const int64_t slot = static_cast<int64_t>(p.ids[p.indptr[seq] + blk]) * p.bs + (pos - blk * p.bs);
+    T* pk_ = const_cast<T*>(static_cast<const T*>(p.pool_k)) + (slot * p.kvh + kh) * p.D;
+    T* pv_ = const_cast<T*>(static_cast<const T*>(p.pool_v)) + (slot * p.kvh + kh) * p.D;
+    const float* kr = p.k_new + (static_cast<size_t>(r) * p.kvh + kh) * p.D;
+    const float* vr = p.v_new + (static_cast<size_t>(r) * p.kvh + kh) * p.D;
+    for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+        store1(pk_ + d, kr[d]);
+        store1(pv_ + d, vr[d]);
+    }
+}
+
 template <typename T, int DPL>
 __global__ void __launch_bounds__(128) generic_attn_kernel(const GenericParams p) {
     constexpr int NW = 4;
@@ -165,13 +187,16 @@ __global__ void __launch_bounds__(128) generic_attn_kernel(const GenericParams p
     }
     float m = -INFINITY, l = 0.f;
     for (int j = warp; j <= pos; j += NW) {
+        // a row of this step (fused append): from the inputs, as the pool will hold it
+        const bool fresh = p.k_new != nullptr && j >= p.starts[seq];
+        const size_t src = fresh ? (static_cast<size_t>(p.offsets[seq] + j - p.starts[seq]) * p.kvh + kh) * p.D : 0;
         const int64_t slot = static_cast<int64_t>(tbl[j / p.bs]) * p.bs + (j % p.bs);
         const size_t off = (static_cast<size_t>(slot) * p.kvh + kh) * p.D;
         float dot = 0.f;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
             const int d = lane + 32 * i;
-            if (d < p.D) dot = fmaf(qv[i], load_f(kpool + off + d), dot);
+            if (d < p.D) dot = fmaf(qv[i], fresh ? as_pool(p.k_new[src + d], kpool) : load_f(kpool + off + d), dot);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
@@ -183,7 +208,7 @@ __global__ void __launch_bounds__(128) generic_attn_kernel(const GenericParams p
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
             const int d = lane + 32 * i;
-            const float vv = d < p.D ? load_f(vpool + off + d) : 0.f;
+            const float vv = d < p.D ? (fresh ? as_pool(p.v_new[src + d], vpool) : load_f(vpool + off + d)) : 0.f;
             acc[i] = fmaf(w, vv, acc[i] * corr);
         }
         m = mnew;
@@ -197,6 +222,7 @@ __global__ void __launch_bounds__(128) generic_attn_kernel(const GenericParams p
         const int d = lane + 32 * i;
         if (d < p.D) sm_acc[warp * p.D + d] = acc[i];
     }
+    if (p.k_new != nullptr && head % g == 0) generic_store_new_row<T>(p, r, seq, kh);
     __syncthreads();
     float mx = -INFINITY;
     for (int w = 0; w < NW; ++w) mx = fmaxf(mx, sm_m[w]);
@@ -214,12 +240,147 @@ __global__ void __launch_bounds__(128) generic_attn_kernel(const GenericParams p
     }
 }
 
+// Key-parallel variant for head_dim <= 32: lane = key. Each lane scores one key of a
+// round of 32 per warp against the whole q row held in registers, the warp makes one
+// online-softmax update per round, and the lanes' partial outputs are summed once at the
+// end. At these head sizes generic_attn_kernel's one-key-per-warp loop is a chain of
+// dependent loads per key; here a chain serves 32 keys.
+// One key's row (head_dim <= 32) into registers; head_dim 32 rows (16-byte aligned: the row
+// starts at a multiple of 32 elements) as vector loads, others element by element.
+__device__ __forceinline__ void load_row32(const float* src, int D, float (&x)[32]) {
+    if (D == 32) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 v = reinterpret_cast<const float4*>(src)[i];
+            x[4 * i] = v.x;
+            x[4 * i + 1] = v.y;
+            x[4 * i + 2] = v.z;
+            x[4 * i + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int d = 0; d < 32; ++d) x[d] = d < D ? src[d] : 0.f;
+    }
+}
+__device__ __forceinline__ void load_row32(const __nv_bfloat16* src, int D, float (&x)[32]) {
+    if (D == 32) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 v = reinterpret_cast<const uint4*>(src)[i];
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                x[8 * i + 2 * k] = __uint_as_float(w[k] << 16);
+                x[8 * i + 2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int d = 0; d < 32; ++d) x[d] = d < D ? __bfloat162float(src[d]) : 0.f;
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) generic_attn_small_kernel(const GenericParams p) {
+    constexpr int NW = 4, DM = 32;
+    __shared__ float sm_m[NW], sm_l[NW];
+    __shared__ float sm_acc[NW][DM];
+    const int r = p.rows[blockIdx.x];
+    const int head = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int seq = p.row_seq[r];
+    const int pos = p.starts[seq] + (r - p.offsets[seq]);  // sees keys 0..pos
+    const int g = p.H / p.kvh;
+    const int kh = head / g;
+    const T* kpool = static_cast<const T*>(p.pool_k);
+    const T* vpool = static_cast<const T*>(p.pool_v);
+    const int32_t* tbl = p.ids + p.indptr[seq];
+    const float* qp = p.q + (static_cast<size_t>(r) * p.H + head) * p.D;
+    float qv[DM], acc[DM];
+#pragma unroll
+    for (int d = 0; d < DM; ++d) {
+        qv[d] = d < p.D ? qp[d] : 0.f;
+        acc[d] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int j0 = warp * 32; j0 <= pos; j0 += NW * 32) {
+        const int j = j0 + lane;
+        const bool live = j <= pos;  // lane 0 always is: every round has a finite max
+        size_t off = 0;
+        if (live) {
+            const int64_t slot = static_cast<int64_t>(tbl[j / p.bs]) * p.bs + (j % p.bs);
+            off = (static_cast<size_t>(slot) * p.kvh + kh) * p.D;
+        }
+        float s = -INFINITY;
+        float kv[DM], vv[DM];
+        if (live && p.k_new != nullptr && j >= p.starts[seq]) {
+            // a row of this step: from the inputs, as the pool will hold it
+            const size_t src = (static_cast<size_t>(p.offsets[seq] + j - p.starts[seq]) * p.kvh + kh) * p.D;
+            float dot = 0.f;
+#pragma unroll
+            for (int d = 0; d < DM; ++d) {
+                kv[d] = d < p.D ? as_pool(p.k_new[src + d], kpool) : 0.f;
+                vv[d] = d < p.D ? as_pool(p.v_new[src + d], vpool) : 0.f;
+                dot = fmaf(qv[d], kv[d], dot);
+            }
+            s = dot * p.scale;
+        } else if (live) {
+            load_row32(kpool + off, p.D, kv);
+            load_row32(vpool + off, p.D, vv);
+            float dot = 0.f;
+#pragma unroll
+            for (int d = 0; d < DM; ++d) dot = fmaf(qv[d], kv[d], dot);
+            s = dot * p.scale;
+        } else {
+#pragma unroll
+            for (int d = 0; d < DM; ++d) vv[d] = 0.f;
+        }
+        float rmax = s;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+        const float mnew = fmaxf(m, rmax);
+        const float corr = expf(m - mnew);
+        const float w = live ? expf(s - mnew) : 0.f;
+        float wsum = w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+        l = l * corr + wsum;
+#pragma unroll
+        for (int d = 0; d < DM; ++d) acc[d] = fmaf(w, vv[d], acc[d] * corr);
+        m = mnew;
+    }
+#pragma unroll
+    for (int d = 0; d < DM; ++d) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[d] += __shfl_xor_sync(0xffffffffu, acc[d], o);
+        if (lane == d) sm_acc[warp][d] = acc[d];
+    }
+    if (lane == 0) {
+        sm_m[warp] = m;
+        sm_l[warp] = l;
+    }
+    if (p.k_new != nullptr && head % g == 0) generic_store_new_row<T>(p, r, seq, kh);
+    __syncthreads();
+    if (threadIdx.x < p.D) {
+        float mx = -INFINITY;
+        for (int w = 0; w < NW; ++w) mx = fmaxf(mx, sm_m[w]);
+        float den = 0.f, num = 0.f;
+        for (int w = 0; w < NW; ++w) {
+            const float wt = sm_m[w] == -INFINITY ? 0.f : expf(sm_m[w] - mx);
+            den += wt * sm_l[w];
+            num += wt * sm_acc[w][threadIdx.x];
+        }
+        p.out[(static_cast<size_t>(r) * p.H + head) * p.D + threadIdx.x] = num / den;
+    }
+}
+
 template <typename T>
 cudaError_t launch_generic_t(const GenericParams& p, cudaStream_t st) {
     const int dpl = (p.D + 31) / 32;
     const dim3 grid(p.nrows, p.H);
     const size_t smem = 4 * p.D * sizeof(float);
-    if (dpl <= 1) generic_attn_kernel<T, 1><<<grid, 128, smem, st>>>(p);
+    if (p.D <= 32) generic_attn_small_kernel<T><<<grid, 128, 0, st>>>(p);
+    else if (dpl <= 1) generic_attn_kernel<T, 1><<<grid, 128, smem, st>>>(p);
     else if (dpl <= 2) generic_attn_kernel<T, 2><<<grid, 128, smem, st>>>(p);
     else if (dpl <= 4) generic_attn_kernel<T, 4><<<grid, 128, smem, st>>>(p);
     else if (dpl <= 8) generic_attn_kernel<T, 8><<<grid, 128, smem, st>>>(p);
