@@ -40,7 +40,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode-attn tokens/s & achieved HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1400.0  # sustained under the power cap
-TC_C2_NCU_TRAFFIC = 626_773_248  # dram__bytes_read.sum + dram__bytes_write.sum, one C2 launch
+TC_C2_NCU_TRAFFIC = 625_797_376  # dram__bytes_read.sum + dram__bytes_write.sum, one C2 launch
 RESULT_OUT = sys.stdout
 
 
