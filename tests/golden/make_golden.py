@@ -1,9 +1,8 @@
 """Generate the golden fixtures in this folder by running pagellm itself.
 
-Run in a checkout that has the pagellm sources (default ``/root/reference/src``, or set
-``PAGELLM_SRC``):
+Run with ``PAGELLM_SRC`` naming the ``src`` directory of a pagellm checkout:
 
-    python tests/golden/make_golden.py
+    PAGELLM_SRC=<pagellm checkout>/src python tests/golden/make_golden.py
 
 Every fixture records seeded inputs together with the outputs of pagellm's own
 functions on them (``pagellm.cache.paged``, ``pagellm.model.transformer``). The tests
@@ -22,7 +21,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-sys.path.insert(0, os.environ.get("PAGELLM_SRC", "/root/reference/src"))
+if not os.environ.get("PAGELLM_SRC"):
+    sys.exit("set PAGELLM_SRC to the src directory of a pagellm checkout")
+sys.path.insert(0, os.environ["PAGELLM_SRC"])
 
 from pagellm.cache.paged import (  # noqa: E402
     BlockManager,

@@ -620,7 +620,7 @@ def test_speculative_rollback_on_the_paged_pool():
 
 
 def test_injected_launch_failure_raises_and_batch_recovers():
-    """Fault injection on the host (SURVEY-style test hook, no GPU fault): the next
+    """Fault injection on the host (a test hook in the library, no GPU fault): the next
     attention call fails as a launch error would, raises, and leaves the batch usable."""
     from pagellm_b200 import _lib, workloads
     from pagellm_b200.cache import PagedBatch
