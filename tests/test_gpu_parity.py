@@ -302,6 +302,57 @@ def test_fp32_pool_append_exact():
     assert torch.equal(pool.v_flat[2].index_select(0, sl), v)
 
 
+@pytest.mark.parametrize("D,dt", [(32, "bfloat16"), (96, "bfloat16"), (16, np.float32), (48, np.float32)])
+def test_cuda_core_path_appends_in_kernel(D, dt):
+    """Head sizes the tensor-core kernel does not take run on the CUDA-core kernels, which
+    append the step's rows inside the attention launch (lanes over keys at head_dim <= 32,
+    over dimensions above). The pool holds the rows exactly as the append kernel would
+    write them (bf16: round to nearest even), the output matches the oracle on the pool's
+    contents, and the step is one launch; decode rows and multi-token rows are mixed."""
+    torch = torch_cuda()
+    from pagellm_b200.cache import PagedBatch, PagedKVPool
+
+    bf = dt == "bfloat16"
+    H, KVH, bs, nb = 8, 2, 16, 64
+    pool = PagedKVPool(Shape(1, KVH, D), nb, bs, dt)
+    g = torch.Generator(device="cuda").manual_seed(D)
+    pool.k.copy_(torch.randn(pool.k.shape, generator=g, device="cuda").to(pool.k.dtype))
+    pool.v.copy_(torch.randn(pool.v.shape, generator=g, device="cuda").to(pool.v.dtype))
+    ctx = [1, 16, 33, 70, 5, 129]
+    n_new = [1, 1, 4, 2, 5, 1]
+    perm = np.random.default_rng(D).permutation(nb)
+    tables, used = [], 0
+    for c_ in ctx:
+        n = -(-c_ // bs)
+        tables.append(perm[used:used + n].tolist())
+        used += n
+    starts = [c_ - n for c_, n in zip(ctx, n_new)]
+    b = PagedBatch(pool, tables, starts, n_new)
+    rows = sum(n_new)
+    q = torch.randn((rows, H, D), generator=g, device="cuda")
+    k = torch.randn((rows, KVH, D), generator=g, device="cuda")
+    v = torch.randn((rows, KVH, D), generator=g, device="cuda")
+    out = b.write_and_attend(0, q, k, v).cpu().numpy()
+    b.check()
+    st = b.stats()
+    assert st["generic_rows"] == rows and st["tc_units"] == 0 and st["launches"] == 1, st
+    sl = torch.as_tensor(b.slots, device="cuda")
+    if bf:
+        assert np.array_equal(bf16_bits_of_tensor(pool.k_flat[0].index_select(0, sl)),
+                              bf16_bits_of_tensor(k.to(torch.bfloat16)))
+        assert np.array_equal(bf16_bits_of_tensor(pool.v_flat[0].index_select(0, sl)),
+                              bf16_bits_of_tensor(v.to(torch.bfloat16)))
+    else:
+        assert torch.equal(pool.k_flat[0].index_select(0, sl), k)
+        assert torch.equal(pool.v_flat[0].index_select(0, sl), v)
+    meta = po.StepMeta(tables, starts, n_new, bs)
+    qh = q.cpu().numpy()
+    for i in range(len(ctx)):
+        kc, vc = gather_rows(pool, 0, meta.ctx_slots[i])
+        a, z = meta.offsets[i], meta.offsets[i + 1]
+        _close(out[a:z], po.attention_dense(qh[a:z], kc, vc, starts[i]), bf)
+
+
 # ----------------------------------------------------------------------------- edges
 def test_edge_cases_context_lengths():
     """ctx 1, block-aligned contexts, a zero-row sequence and mixed window sizes."""
