@@ -114,3 +114,19 @@ def test_partition_rejects_empty_units():
     ok = np.array([2, 1, 3], dtype=np.int64)
     assert lib.pk_plan_partition(ok.ctypes.data_as(C.POINTER(C.c_int64)), 3, 8, -1, None, C.byref(n)) \
         == _lib.PK_ERR_INVALID_ARG
+
+
+def test_host_array_addresses():
+    """The Python surface passes numpy buffers to the C ABI by address: the buffer-protocol
+    route for writable arrays, ndarray.ctypes for read-only and empty ones; all agree."""
+    import pagellm_b200.cache.paged as paged
+
+    a = np.arange(10, dtype=np.int64)
+    assert paged._addr(a) == a.ctypes.data
+    ro = np.arange(6, dtype=np.int32)
+    ro.setflags(write=False)
+    assert paged._addr(ro) == ro.ctypes.data
+    empty = np.zeros(0, dtype=np.int32)
+    assert paged._addr(empty) == empty.ctypes.data
+    sub = np.arange(16, dtype=np.float32)[4:]
+    assert paged._addr(sub) == sub.ctypes.data
