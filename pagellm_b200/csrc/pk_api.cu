@@ -455,11 +455,12 @@ int64_t split_kv_ctas(int64_t T, int64_t nu, int64_t max_ctas) {
 constexpr int64_t kWideMinRows = 64;
 
 // Time a split-KV CTA loses per unit boundary inside its block range (B200, C2 decode
-// shape, per-CTA globaltimer trace): it reloads queries, publishes a partial for the unit
-// it leaves, and the unit it ends in it usually finishes last of that unit's CTAs, so it
-// merges the unit's partials at the end of its run. CTAs crossing one boundary ran 112 us
-// against 102.6 us for those inside one unit, with equal block counts.
-constexpr double kUnitSwitchUs = 9.0;
+// shape): it reloads queries, publishes a partial for the unit it leaves, and the unit it
+// ends in it usually finishes last of that unit's CTAs, so it merges the unit's partials at
+// the end of its run. Per-CTA globaltimer traces showed ~9.5 us (112 us against 102.6 us at
+// equal block counts); a sweep of the cost (5 / 9 / 14 / 20 / 28 us) put the fastest C2 step
+// at 14 us (602k against 596k tok/s at 9), the long-sequence C5 step being indifferent.
+constexpr double kUnitSwitchUs = 14.0;
 
 // The units' blocks (in unit order, prefix sums ub[0..nu]) cut into contiguous CTA ranges,
 // at most n of them. A range costs its blocks plus `switch_cost` blocks per unit boundary
