@@ -13,8 +13,11 @@
  *       q, out: [rows][n_heads][head_dim]     k, v: [rows][n_kv_heads][head_dim]
  *   - The pool stores K and V as [layers][num_blocks][block_size][n_kv_heads][head_dim]
  *     in float32 or bfloat16; a token's slot is block * block_size + offset.
- *   - The library keeps no global state besides the thread-local error message and
- *     needs no locking for the single-engine-thread use pagellm makes of its cache.
+ *   - Global state: the thread-local error message, the one-shot test hook
+ *     pk_test_inject_launch_failure, and the device array (and its per-device address
+ *     cache) of pk_decode_attend_static. Pools, batches and block managers are independent
+ *     objects; none needs locking for the single-engine-thread use pagellm makes of its
+ *     cache.
  */
 #ifndef PAGEKV_H
 #define PAGEKV_H
@@ -176,6 +179,15 @@ PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int ma
                              int64_t* cta_first_block, int* ncta);
 
 
+/* Head-sharded output gather (no counterpart in pagellm, which runs in one process): every
+ * rank of `world` computed the query heads [r*H/world, (r+1)*H/world) of all `rows` rows;
+ * after an all-gather of those [rows][H/world][head_dim] slices into src_dev
+ * [world][rows][row_floats] (row_floats = H/world * head_dim), dst_dev receives the
+ * [rows][H][head_dim] output PagedBatch.write_and_attend (cache/paged.py:441-464) returns.
+ * float32 device buffers, 16-byte aligned, row_floats a multiple of 4. */
+PK_API int pk_gather_interleave(const float* src_dev, float* dst_dev, int world, int64_t rows,
+                                int64_t row_floats, void* stream);
+
 /* Decode attention that allocates nothing. No counterpart in the reference: pagellm has no
  * device memory at all. For callers that cannot call cudaMalloc - a serving framework that
  * hands out all of HBM through its own caching allocator, or a plugin host that forbids
@@ -189,7 +201,8 @@ PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int ma
  * sequences, fails with PK_ERR_INVALID_ARG before launching anything. Every call on a device
  * shares that array and leaves it dirty (the error word is cleared per call): calls that
  * overlap on the GPU race. The first call on a device looks the array's address up - make it
- * before any stream capture. err_dev (optional) receives 1 if a bounded device wait gave up.
+ * before any stream capture. err_dev (required, a device int the caller owns and clears):
+ * set to 1 if a bounded device wait gave up, so a timeout is never lost.
  * Pageable table_ids / ctx arrays are copied before return; pinned ones must stay valid until
  * the stream has run the call. */
 PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, int n_heads, int nseq,

@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "pk_batch_set_prefix_sharing": (_i32, [_p, _i32]),
     "pk_batch_prefix_stats": (_i32, [_p, _pi64]),
     "pk_plan_partition": (_i32, [_pi64, _i64, _i32, _i32, _pi64, C.POINTER(_i32)]),
+    "pk_gather_interleave": (_i32, [_p, _p, _i32, _i64, _i64, _p]),
     "pk_decode_attend_static": (_i32, [_p, _i32, _i32, _i32, _pi64, _pi32, _pi64, _p, _p, _p, _p]),
     "pk_selftest_bounded_wait": (_i32, [_i32, _i64, C.POINTER(_i32)]),
     "pk_batch_profile": (_i32, [_p, _i32]),

@@ -390,7 +390,8 @@ void setup_tc(pk_pool* P) {
     P->tc_ok = false;
     auto no = [&](const char* w) { P->tc_why = w; };
     if (P->dtype != PK_BF16) return no("pool is not bf16");
-    if (P->d % 64 != 0 || P->d > 256) return no("head_dim not in {64,128,256}");
+    // only these head sizes have a compiled instance (launch_tc_attention, tc_max_active_ctas)
+    if (P->d != 64 && P->d != 128 && P->d != 256) return no("head_dim not in {64,128,256}");
     if (P->block_size % 16 != 0 || P->block_size > 256) return no("block_size not a multiple of 16 (<=256)");
     if (P->kvh > pk::kTcMaxKvHeads) return no("more than 8 KV heads");
     const int64_t slots = static_cast<int64_t>(P->n_layers) * P->num_blocks * P->block_size;
@@ -1702,6 +1703,18 @@ int pk_selftest_bounded_wait(int device, int64_t limit_ns, int* timed_out) {
     cudaFree(word);
     if (e != cudaSuccess) return fail(PK_ERR_CUDA, "bounded-wait self-test: %s", cudaGetErrorString(e));
     *timed_out = v == pk::kErrTimeout ? 1 : 0;
+    return PK_OK;
+}
+
+int pk_gather_interleave(const float* src_dev, float* dst_dev, int world, int64_t rows, int64_t row_floats,
+                         void* stream) {
+    if (world <= 0 || rows < 0 || row_floats < 0) return fail(PK_ERR_INVALID_ARG, "bad sizes");
+    if (rows == 0 || row_floats == 0) return PK_OK;
+    if (!src_dev || !dst_dev) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    if (row_floats % 4 != 0) return fail(PK_ERR_INVALID_ARG, "row_floats %lld is not a multiple of 4", (long long)row_floats);
+    int rc;
+    if ((rc = check_aligned(src_dev, "src")) || (rc = check_aligned(dst_dev, "dst"))) return rc;
+    PK_CUDA(pk::launch_interleave_heads(src_dev, dst_dev, world, rows, row_floats, static_cast<cudaStream_t>(stream)));
     return PK_OK;
 }
 

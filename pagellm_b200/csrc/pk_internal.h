@@ -205,6 +205,10 @@ cudaError_t launch_append_table(int dtype, void* pool_k_layer, void* pool_v_laye
 cudaError_t launch_copy_blocks(void* k, void* v, const int64_t* pairs, int64_t npairs, int layers,
                                int64_t layer_bytes, int64_t block_bytes, cudaStream_t st);
 cudaError_t launch_bounded_wait_selftest(int* err, unsigned long long limit_ns, cudaStream_t st);
+// src [world][rows][row_floats] -> dst [rows][world][row_floats]; row_floats % 4 == 0, both
+// pointers 16-byte aligned.
+cudaError_t launch_interleave_heads(const float* src, float* dst, int world, int64_t rows, int64_t row_floats,
+                                    cudaStream_t st);
 cudaError_t launch_slot_mapping(const int32_t* table, int64_t table_len, const int64_t* positions,
                                 int64_t n, int bs, int64_t* slots, int32_t* err, cudaStream_t st);
 

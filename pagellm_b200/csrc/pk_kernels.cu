@@ -5,6 +5,8 @@
 
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "pk_device.cuh"
 #include "pk_internal.h"
 
@@ -130,6 +132,24 @@ __global__ void copy_blocks_kernel(uint8_t* __restrict__ k, uint8_t* __restrict_
     W* d = reinterpret_cast<W*>(base + dst * block_bytes);
     const int64_t words = block_bytes / static_cast<int64_t>(sizeof(W));
     for (int64_t i = threadIdx.x; i < words; i += blockDim.x) d[i] = s[i];
+}
+
+// ------------------------------------------------------------------ head-sharded output
+// src [world][rows][S] (an all-gather of every rank's [rows][H/world][D] slice, S floats per
+// row) -> dst [rows][world][S]: rank r's query heads land at [r*H/world, (r+1)*H/world).
+// One thread per 16 bytes; consecutive threads walk one destination row, so both the reads
+// (a run of S floats) and the writes are contiguous.
+__global__ void interleave_heads_kernel(const float4* __restrict__ src, float4* __restrict__ dst,
+                                        int world, int64_t rows, int64_t s4) {
+    const int64_t total = static_cast<int64_t>(world) * rows * s4;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t row = i / (world * s4);
+        const int64_t rem = i - row * world * s4;
+        const int64_t r = rem / s4;
+        const int64_t c = rem - r * s4;
+        dst[i] = src[(r * rows + row) * s4 + c];
+    }
 }
 
 // ------------------------------------------------------------------ generic attention
@@ -479,6 +499,18 @@ cudaError_t launch_copy_blocks(void* k, void* v, const int64_t* pairs, int64_t n
         copy_blocks_kernel<uint32_t><<<grid, 256, 0, st>>>(kb, vb, pairs, layer_bytes, block_bytes);
     else
         copy_blocks_kernel<uint16_t><<<grid, 256, 0, st>>>(kb, vb, pairs, layer_bytes, block_bytes);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_interleave_heads(const float* src, float* dst, int world, int64_t rows, int64_t row_floats,
+                                    cudaStream_t st) {
+    const int64_t s4 = row_floats / 4;
+    const int64_t total = static_cast<int64_t>(world) * rows * s4;
+    if (total <= 0) return cudaSuccess;
+    const int threads = 256;
+    const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 8);
+    interleave_heads_kernel<<<static_cast<int>(blocks), threads, 0, st>>>(
+        reinterpret_cast<const float4*>(src), reinterpret_cast<float4*>(dst), world, rows, s4);
     return cudaGetLastError();
 }
 

@@ -1,7 +1,7 @@
 // Decode attention that allocates nothing: the split-KV tensor-core attention of
 // pk_attn_tc.cu, with every piece of scratch it needs (the step's block tables and plan,
-// the per-CTA partial results of split sequences, the error word) held in one file-scope
-// device array instead of memory from cudaMalloc.
+// the per-CTA partial results of split sequences) held in one file-scope device array
+// instead of memory from cudaMalloc.
 //
 // Who needs this: a caller that runs under an allocator it does not own - a serving
 // framework that hands out every byte of HBM through its own caching allocator, or a
@@ -13,9 +13,11 @@
 // * The array is kStaticScratchBytes (16 MiB) on every GPU that loads the library, held
 //   until the process exits. A call whose plan does not fit is rejected with
 //   PK_ERR_INVALID_ARG before anything is launched (at most kStaticMaxSeqs sequences).
-// * Every call on a device uses the same array and leaves its contents behind; the error
-//   word is cleared at the start of each call. Calls whose work overlaps on the GPU (two
-//   streams, or two host threads) race on the array.
+// * Every call on a device uses the same array and leaves its contents behind. Calls whose
+//   work overlaps on the GPU (two streams, or two host threads) race on the array.
+// * A bounded device wait that gives up is reported through the caller's error word
+//   (err_dev, required): the array holds no error state that a later call would have to
+//   read back.
 // * The first call on a device looks the array's device address up
 //   (cudaGetSymbolAddress) with that device current and caches it; make that first call
 //   before any stream capture.
@@ -95,6 +97,7 @@ extern "C" PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, in
     if (nseq == 0) return PK_OK;
     if (!table_indptr || !table_ids || !ctx_lens || !q_dev || !out_dev)
         return sfail(PK_ERR_INVALID_ARG, "NULL pointer");
+    if (!err_dev) return sfail(PK_ERR_INVALID_ARG, "err_dev is NULL (a timed-out wait would go unreported)");
     if ((reinterpret_cast<uintptr_t>(q_dev) | reinterpret_cast<uintptr_t>(out_dev)) & 15u)
         return sfail(PK_ERR_INVALID_ARG, "q and out must be 16-byte aligned");
     const int bs = P.block_size;
@@ -148,8 +151,7 @@ extern "C" PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, in
     const size_t o_part = 0;
     const size_t n_part_o = segs * P.kvh * pk::kMaxCols * P.d;
     const size_t o_ml = up256(o_part + n_part_o * sizeof(float));
-    const size_t o_err = up256(o_ml + segs * P.kvh * pk::kMaxCols * 2 * sizeof(float));
-    const size_t o_ids = up256(o_err + sizeof(int32_t));
+    const size_t o_ids = up256(o_ml + segs * P.kvh * pk::kMaxCols * 2 * sizeof(float));
     const size_t o_meta = up256(o_ids + static_cast<size_t>(n_ids) * sizeof(int32_t));
     // meta = indptr | starts | offsets | useq | ut0 | un | ublk | su | sc0 | sc1
     int32_t pack[10 * (kStaticMaxSeqs + 1)];
@@ -194,10 +196,8 @@ extern "C" PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, in
     int rc = scratch_address(P.device, &base);
     if (rc != PK_OK) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemsetAsync(base + o_err, 0, sizeof(int32_t), st);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(base + o_ids, table_ids, static_cast<size_t>(n_ids) * sizeof(int32_t),
-                            cudaMemcpyHostToDevice, st);
+    cudaError_t e = cudaMemcpyAsync(base + o_ids, table_ids, static_cast<size_t>(n_ids) * sizeof(int32_t),
+                                    cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(base + o_meta, pack, m * sizeof(int32_t), cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return sfail(PK_ERR_CUDA, "scratch upload: %s", cudaGetErrorString(e));
@@ -208,7 +208,7 @@ extern "C" PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, in
     p.out = out_dev;
     p.part_o = reinterpret_cast<float*>(base + o_part);
     p.part_ml = reinterpret_cast<float*>(base + o_ml);
-    p.err = err_dev ? reinterpret_cast<int*>(err_dev) : reinterpret_cast<int*>(base + o_err);
+    p.err = reinterpret_cast<int*>(err_dev);
     p.indptr = meta + off[0];
     p.ids = reinterpret_cast<const int32_t*>(base + o_ids);
     p.starts = meta + off[1];

@@ -52,14 +52,43 @@ def head_slice(rank: int, world: int, n_kv_heads: int, n_heads: int) -> HeadSlic
     return HeadSlice(rank * per, (rank + 1) * per, rank * per * g, (rank + 1) * per * g)
 
 
-def gather_heads(out_slice, group=None):
-    """All-gather each rank's ``[rows, H/world, D]`` attention slice into ``[rows, H, D]``
-    (rank r's slice lands at query heads [r*H/world, (r+1)*H/world))."""
-    import torch
-    import torch.distributed as dist
+class HeadGather:
+    """All-gather of each rank's ``[rows, H/world, D]`` attention slice into ``[rows, H, D]``
+    (rank r's slice lands at query heads [r*H/world, (r+1)*H/world)), with reusable buffers.
 
-    world = dist.get_world_size(group)
-    rows, hs, d = out_slice.shape
-    buf = torch.empty((world * rows, hs, d), dtype=out_slice.dtype, device=out_slice.device)
-    dist.all_gather_into_tensor(buf, out_slice.contiguous(), group=group)
-    return buf.view(world, rows, hs, d).permute(1, 0, 2, 3).reshape(rows, world * hs, d)
+    CUDA tensors: ``all_gather_into_tensor`` (NCCL) into ``[world, rows, H/world, D]``, then
+    libpagekv's interleave kernel writes the ``[rows, H, D]`` result. CPU tensors (gloo, the
+    multi-process tests) interleave with a tensor permute."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self._buf = None
+        self._out = None
+
+    def __call__(self, out_slice):
+        import torch
+        import torch.distributed as dist
+
+        world = dist.get_world_size(self.group)
+        rows, hs, d = out_slice.shape
+        shape = (world * rows, hs, d)
+        if self._buf is None or self._buf.shape != shape or self._buf.device != out_slice.device \
+                or self._buf.dtype != out_slice.dtype:
+            self._buf = torch.empty(shape, dtype=out_slice.dtype, device=out_slice.device)
+            self._out = torch.empty((rows, world * hs, d), dtype=out_slice.dtype, device=out_slice.device)
+        dist.all_gather_into_tensor(self._buf, out_slice.contiguous(), group=self.group)
+        if not out_slice.is_cuda:
+            return self._buf.view(world, rows, hs, d).permute(1, 0, 2, 3).reshape(rows, world * hs, d)
+        if out_slice.dtype != torch.float32:
+            raise ValueError("head gather on the GPU takes float32 slices")
+        from . import _lib
+
+        st = torch.cuda.current_stream(out_slice.device).cuda_stream
+        _lib.check(_lib.load().pk_gather_interleave(self._buf.data_ptr(), self._out.data_ptr(), world, rows,
+                                                    hs * d, st))
+        return self._out
+
+
+def gather_heads(out_slice, group=None):
+    """One-off :class:`HeadGather` call (fresh buffers; the returned tensor is the caller's)."""
+    return HeadGather(group)(out_slice)

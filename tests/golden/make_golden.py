@@ -2,7 +2,8 @@
 
 Run with ``PAGELLM_SRC`` naming the ``src`` directory of a pagellm checkout:
 
-    PAGELLM_SRC=<pagellm checkout>/src python tests/golden/make_golden.py
+    PAGELLM_SRC=<pagellm checkout>/src python tests/golden/make_golden.py          # all
+    PAGELLM_SRC=<pagellm checkout>/src python tests/golden/make_golden.py engine   # engine_*.npz only
 
 Every fixture records seeded inputs together with the outputs of pagellm's own
 functions on them (``pagellm.cache.paged``, ``pagellm.model.transformer``). The tests
@@ -282,7 +283,135 @@ def allocator_trace(seed: int, num_blocks: int, bs: int, prefix_caching: bool, n
     return {"num_blocks": num_blocks, "block_size": bs, "prefix_caching": prefix_caching, "ops": ops}
 
 
-def main():
+ENGINE_SCENARIOS = {
+    # continuous batching with prefix-cache hits (requests sharing a system prompt arrive
+    # after its blocks are published) and parallel sampling n=3 (fork + copy-on-write)
+    "serve": dict(config=dict(num_blocks=96, block_size=8, max_num_seqs=8, max_num_batched_tokens=256),
+                  requests=[(0, "You are a helpful Shakespearean assistant.\nWho art thou?", 1, 14, 0.8, 1),
+                            (2, "You are a helpful Shakespearean assistant.\nWhat news?", 1, 12, 0.0, 2),
+                            (3, "ROMEO:\nBut soft", 3, 16, 1.0, 5),
+                            (5, "You are a helpful Shakespearean assistant.\nSpeak!", 1, 10, 0.7, 3)]),
+    # a pool too small for everyone: preemption frees blocks and recomputes prefills; the
+    # block-by-block ("paged") attention mode
+    "preempt": dict(config=dict(num_blocks=30, block_size=4, max_model_len=96, max_num_batched_tokens=96,
+                                max_num_seqs=8, attn="paged"),
+                    requests=[(0, "First Citizen:\nBefore we proceed", 1, 40, 0.8, 11),
+                              (0, "ROMEO:\nBut soft", 1, 40, 0.8, 12),
+                              (0, "To be, or not", 1, 28, 0.8, 13),
+                              (0, "KING RICHARD III:\nNow is the winter of our discontent", 1, 28, 0.8, 14),
+                              (0, "A", 1, 28, 0.8, 15),
+                              (0, "Speak, speak.", 1, 28, 0.8, 16)]),
+    # chunked prefill: long prompts split over steps beside running decodes
+    "chunked": dict(config=dict(num_blocks=64, block_size=16, max_num_seqs=4, max_num_batched_tokens=24,
+                                enable_chunked_prefill=True),
+                    requests=[(0, "First Citizen:\nBefore we proceed any further, hear me speak.\n"
+                                  "All:\nSpeak, speak.\nFirst Citizen:\nYou are all resolved rather", 1, 8, 0.0, 1),
+                              (1, "KING RICHARD III:\nNow is the winter of our discontent\nMade glorious summer", 1, 10,
+                               0.9, 2),
+                              (2, "abc", 1, 12, 0.0, 3)]),
+    # the step structure only (no tensors) of a run with 16-token blocks: forks sharing
+    # prompt blocks, prefix hits, chunked prefill and decodes, replayed on the GPU at a
+    # tensor-core shape (bf16, head_dim 128) against the oracle
+    "serve16": dict(config=dict(num_blocks=160, block_size=16, max_num_seqs=12, max_num_batched_tokens=96,
+                                enable_chunked_prefill=True),
+                    structure_only=True,
+                    requests=[(0, "You are a helpful Shakespearean assistant. Answer in verse.\n" * 2 + "Who art thou?",
+                               4, 20, 1.0, 7),
+                              (3, "You are a helpful Shakespearean assistant. Answer in verse.\n" * 2 + "What news?",
+                               1, 24, 0.8, 8),
+                              (4, "ROMEO:\nBut soft, what light through yonder window breaks?", 3, 18, 0.9, 9),
+                              (6, "You are a helpful Shakespearean assistant. Answer in verse.\n" * 2 + "Speak!",
+                               2, 16, 0.7, 10)]),
+}
+
+
+def engine_trace(name: str) -> dict:
+    """pagellm's own LLMEngine (bundled "target" model: 4 layers, H=4, KVH=2, d=32, fp32)
+    run on a scenario, with every PagedBatch it builds and every copy-on-write copy it makes
+    recorded: per step the copies applied before the batch, the block tables (CSR), starts,
+    n_new, attention mode, positions, slots and, per layer, the q / k / v the model handed to
+    write_and_attend and the output it returned (engine/llm_engine.py:201-255)."""
+    import pagellm.engine.llm_engine as le
+    from pagellm.engine import EngineConfig, LLMEngine, SamplingParams
+    from pagellm.model.weights import load_pretrained
+
+    sc = ENGINE_SCENARIOS[name]
+    model, tok = load_pretrained("target")
+    steps: list[dict] = []
+    pending: list[tuple[int, int]] = []
+
+    class RecordingBatch(PagedBatch):
+        def __init__(self, pool, block_tables, starts, n_new, attn="gather", batch_decode=True):
+            super().__init__(pool, block_tables, starts, n_new, attn, batch_decode)
+            self._rec = {"copies": list(pending), "tables": [list(map(int, t)) for t in block_tables],
+                         "starts": list(map(int, starts)), "n_new": list(map(int, n_new)), "attn": attn,
+                         "batch_decode": bool(batch_decode), "positions": self.positions.copy(),
+                         "slots": self.slots.copy(), "layers": []}
+            pending.clear()
+            steps.append(self._rec)
+
+        def write_and_attend(self, layer, q, k, v):
+            out = super().write_and_attend(layer, q, k, v)
+            self._rec["layers"].append((layer, q.copy(), k.copy(), v.copy(), out.copy()))
+            return out
+
+    saved = le.PagedBatch
+    le.PagedBatch = RecordingBatch
+    try:
+        eng = LLMEngine(model, tok, EngineConfig(**sc["config"]))
+        copy_block = eng.pool.copy_block
+
+        def recording_copy(src, dst):
+            pending.append((int(src), int(dst)))
+            copy_block(src, dst)
+
+        eng.pool.copy_block = recording_copy
+        todo = sorted(sc["requests"], key=lambda r: r[0])
+        step_no = 0
+        while todo or eng.has_unfinished():
+            while todo and todo[0][0] <= step_no:
+                _, prompt, n, max_tokens, temp, seed = todo.pop(0)
+                eng.add_request(prompt, SamplingParams(n=n, max_tokens=max_tokens, temperature=temp, seed=seed))
+            eng.step()
+            step_no += 1
+            assert step_no < 2000
+        stats = {"preemptions": eng.scheduler.num_preemptions, "cow_copies": eng.stats.cow_copies,
+                 "prefix_hits": eng.bm.alloc.prefix_hits, "cached_prompt_tokens": eng.stats.cached_prompt_tokens,
+                 "steps": eng.stats.steps}
+    finally:
+        le.PagedBatch = saved
+    cfg = model.cfg
+    out = {"dims": np.array([cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
+                             eng.config.num_blocks, eng.config.block_size], np.int64),
+           "nsteps": np.array(len(steps)), "stats": np.array(json.dumps(stats))}
+    for i, st in enumerate(steps):
+        lens = np.array([len(t) for t in st["tables"]], np.int64)
+        ip = np.zeros(len(lens) + 1, np.int64)
+        np.cumsum(lens, out=ip[1:])
+        out[f"s{i}_copies"] = np.array(st["copies"], np.int64).reshape(-1, 2)
+        out[f"s{i}_indptr"] = ip
+        out[f"s{i}_ids"] = np.array([b for t in st["tables"] for b in t], np.int64)
+        out[f"s{i}_starts"] = np.array(st["starts"], np.int64)
+        out[f"s{i}_n_new"] = np.array(st["n_new"], np.int64)
+        out[f"s{i}_mode"] = np.array([st["attn"] == "paged", st["batch_decode"]], np.int64)
+        out[f"s{i}_positions"] = st["positions"]
+        out[f"s{i}_slots"] = st["slots"]
+        assert [l_[0] for l_ in st["layers"]] == list(range(cfg.n_layers))
+        if sc.get("structure_only"):
+            continue
+        for key, j in (("q", 1), ("k", 2), ("v", 3), ("out", 4)):
+            out[f"s{i}_{key}"] = np.stack([l_[j] for l_ in st["layers"]]).astype(np.float32)
+    return out
+
+
+def main(only=None):
+    if only == "engine":
+        for name in ENGINE_SCENARIOS:
+            np.savez_compressed(HERE / f"engine_{name}.npz", **engine_trace(name))
+        print("wrote", sorted(p.name for p in HERE.iterdir() if p.name.startswith("engine_")))
+        return
+    for name in ENGINE_SCENARIOS:
+        np.savez_compressed(HERE / f"engine_{name}.npz", **engine_trace(name))
     np.savez_compressed(HERE / "paged_attention_cases.npz", **paged_attention_cases())
     np.savez_compressed(HERE / "batched_decode.npz", **batched_decode_case())
     for name, case in step_cases().items():
@@ -299,4 +428,4 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1] if len(sys.argv) > 1 else None)

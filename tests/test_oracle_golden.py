@@ -152,3 +152,34 @@ def _evictable(bm):
 @pytest.mark.parametrize("ti", [0, 1, 2])
 def test_oracle_block_manager_replays_pagellm(ti):
     _replay(load_traces()[ti], po.OracleBlockManager, po.OracleOutOfBlocks)
+
+
+@pytest.mark.parametrize("name", ["serve", "preempt", "chunked"])
+def test_oracle_replays_pagellm_engine(name):
+    """pagellm's own LLMEngine runs (tests/golden/engine_*.npz: 4 layers, prefix hits, an n=3
+    fork with copy-on-write, preemption with recompute, chunked prefill) replayed through the
+    oracle on a zero-filled multi-layer pool: every step's positions and slots bit-exact,
+    every layer's output within 1e-5 of its scale of pagellm's (float32 on both sides)."""
+    from engine_trace import OraclePool, Trace, assert_close_scaled
+
+    tr = Trace(name)
+    pool = OraclePool(tr.layers, tr.num_blocks, tr.bs, tr.KVH, tr.d)
+    for st in tr.steps:
+        meta = po.StepMeta(st.tables, st.starts, st.n_new, tr.bs, st.batch_decode, st.attn)
+        np.testing.assert_array_equal(meta.positions, st.positions)
+        np.testing.assert_array_equal(meta.slots, st.slots)
+        inputs = [(st.q[li], st.k[li], st.v[li]) for li in range(tr.layers)]
+        for li, out in pool.step(st, inputs):
+            assert_close_scaled(out, st.out[li])
+
+
+def test_engine_traces_cover_the_engine_paths():
+    """What the recorded runs exercise (so a regenerated fixture cannot silently lose it)."""
+    from engine_trace import Trace
+
+    serve, pre, chunk, s16 = (Trace(n) for n in ("serve", "preempt", "chunked", "serve16"))
+    assert serve.stats["cow_copies"] >= 2 and serve.stats["prefix_hits"] > 0
+    assert pre.stats["preemptions"] > 0 and any(s.attn == "paged" for s in pre.steps)
+    assert max(max(s.n_new) for s in chunk.steps) <= 24 < sum(s.rows for s in chunk.steps)
+    assert any(len(s.copies) for s in s16.steps) and max(max(s.n_new) for s in s16.steps) >= 16
+    assert all(t.layers == 4 and (t.H, t.KVH, t.d) == (4, 2, 32) for t in (serve, pre, chunk))
