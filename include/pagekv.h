@@ -188,6 +188,28 @@ PK_API int pk_plan_partition(const int64_t* unit_blocks, int64_t n_units, int ma
 PK_API int pk_gather_interleave(const float* src_dev, float* dst_dev, int world, int64_t rows,
                                 int64_t row_floats, void* stream);
 
+/* Head-sharded output exchange over peer memory (no counterpart in pagellm, which runs in one
+ * process). Each of `world` ranks (one process per GPU, GPUs with peer access over NVLink)
+ * creates one on its device with room for a [rows][H][head_dim] float32 result (`bytes`,
+ * a multiple of 16), passes the 64-byte IPC handle from pk_peer_gather_handle to every other
+ * rank (any host-side channel), and calls pk_peer_gather_open with all `world` handles in
+ * rank order. pk_peer_gather_heads then runs one launch per step: this rank's slice
+ * [rows][row_floats] (row_floats = H/world * head_dim, a multiple of 4) is stored into every
+ * rank's result buffer at head offset rank * H/world, and the launch completes once every
+ * rank's slice has landed here, so *result_dev ([rows][H][head_dim], the output of
+ * PagedBatch.write_and_attend, cache/paged.py:441-464) is complete in stream order. The two
+ * result buffers alternate by step; every rank calls it for every step, in the same order.
+ * A peer that does not signal within 1 s makes the launch record a timeout, reported by
+ * pk_peer_gather_check (which synchronises the stream). */
+typedef struct pk_peer_gather pk_peer_gather;
+PK_API int pk_peer_gather_create(int device, int world, int rank, int64_t bytes, pk_peer_gather** out);
+PK_API int pk_peer_gather_handle(const pk_peer_gather* gather, uint8_t* handle64);
+PK_API int pk_peer_gather_open(pk_peer_gather* gather, const uint8_t* handles);
+PK_API int pk_peer_gather_heads(pk_peer_gather* gather, const float* slice_dev, int64_t rows, int64_t row_floats,
+                                float** result_dev, void* stream);
+PK_API int pk_peer_gather_check(pk_peer_gather* gather, void* stream);
+PK_API int pk_peer_gather_destroy(pk_peer_gather* gather);
+
 /* Decode attention that allocates nothing. No counterpart in the reference: pagellm has no
  * device memory at all. For callers that cannot call cudaMalloc - a serving framework that
  * hands out all of HBM through its own caching allocator, or a plugin host that forbids

@@ -60,6 +60,12 @@ SIGNATURES: dict[str, tuple] = {
     "pk_batch_prefix_stats": (_i32, [_p, _pi64]),
     "pk_plan_partition": (_i32, [_pi64, _i64, _i32, _i32, _pi64, C.POINTER(_i32)]),
     "pk_gather_interleave": (_i32, [_p, _p, _i32, _i64, _i64, _p]),
+    "pk_peer_gather_create": (_i32, [_i32, _i32, _i32, _i64, C.POINTER(_p)]),
+    "pk_peer_gather_handle": (_i32, [_p, C.c_char_p]),
+    "pk_peer_gather_open": (_i32, [_p, C.c_char_p]),
+    "pk_peer_gather_heads": (_i32, [_p, _p, _i64, _i64, C.POINTER(_p), _p]),
+    "pk_peer_gather_check": (_i32, [_p, _p]),
+    "pk_peer_gather_destroy": (_i32, [_p]),
     "pk_decode_attend_static": (_i32, [_p, _i32, _i32, _i32, _pi64, _pi32, _pi64, _p, _p, _p, _p]),
     "pk_selftest_bounded_wait": (_i32, [_i32, _i64, C.POINTER(_i32)]),
     "pk_batch_profile": (_i32, [_p, _i32]),

@@ -21,7 +21,8 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libpagekv.so"
 
-SOURCES = ["pk_api.cu", "pk_kernels.cu", "pk_attn_tc.cu", "pk_attn_wide.cu", "pk_block_manager.cpp", "pk_static.cu"]
+SOURCES = ["pk_api.cu", "pk_kernels.cu", "pk_attn_tc.cu", "pk_attn_wide.cu", "pk_block_manager.cpp", "pk_static.cu",
+           "pk_peer.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1073,6 +1073,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
             m.g = g;
             m.H = H;
             m.D = P->d;
+            m.nt = B->nt;
             PK_CUDA(prof_begin(B, st));
             PK_CUDA(pk::launch_merge(m, B->nsplit, st));
             PK_CUDA(prof_end(B, kProfMerge, st));

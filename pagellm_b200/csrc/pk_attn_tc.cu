@@ -112,6 +112,10 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
     const int tile_bytes = p.bs * p.kvh * D * 2;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * 2 * tile_bytes);
     uint64_t* empty = full + p.stages;
+    // the consumers' end of work (one arrival per consumer warp), then one barrier per consumer
+    // warp for the bulk copies of its end-of-range merge
+    uint64_t* endbar = empty + p.stages;
+    uint64_t* mbar_m = endbar + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -122,6 +126,8 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], nwc);
         }
+        mbar_init(endbar, nwc);
+        for (int w = 0; w < nwc; ++w) mbar_init(&mbar_m[w], 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -136,6 +142,9 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
         if (lane == 0) {
             prefetch_tensormap(&tmk);
             prefetch_tensormap(&tmv);
+            // K/V blocks are read once per launch: first out of L2, so that what is read again
+            // (queries, block tables, the partials the merges fetch) stays there
+            const uint64_t evict_first = l2_policy_evict_first();
             int it = 0;
             bool ok = true;
             for (int j = lo, u = u_first; j < hi && ok; ++u) {
@@ -143,6 +152,9 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 const int seq = p.u_seq[u];
                 const int kb0 = p.u_kb0 != nullptr ? p.u_kb0[u] : 0;
                 const int tbase = p.indptr[seq] + kb0 - p.u_blk[u];
+                // the unit's query rows into L2 while its first blocks stream in
+                prefetch_l2_bulk(p.q + static_cast<size_t>(p.offsets[seq] + p.u_t0[u]) * p.H * D,
+                                 static_cast<uint32_t>(p.u_n[u]) * p.H * D * 4u);
                 for (; j < uend; ++j, ++it) {
                     const int s = it % p.stages;
                     const uint32_t k = static_cast<uint32_t>(it / p.stages);
@@ -157,13 +169,13 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                     uint8_t* vd = kd + tile_bytes;
                     mbar_arrive_expect_tx(&full[s], 2u * tile_bytes);
                     if (!p.per_head_layout) {
-                        tma_load_4d(kd, &tmk, 0, slot0, 0, 0, &full[s]);
-                        tma_load_4d(vd, &tmv, 0, slot0, 0, 0, &full[s]);
+                        tma_load_4d_hint(kd, &tmk, 0, slot0, 0, 0, &full[s], evict_first);
+                        tma_load_4d_hint(vd, &tmv, 0, slot0, 0, 0, &full[s], evict_first);
                     } else {
                         const int hb = p.bs * CH * 128;
                         for (int h = 0; h < p.kvh; ++h) {
-                            tma_load_4d(kd + h * hb, &tmk, 0, 0, h, slot0, &full[s]);
-                            tma_load_4d(vd + h * hb, &tmv, 0, 0, h, slot0, &full[s]);
+                            tma_load_4d_hint(kd + h * hb, &tmk, 0, 0, h, slot0, &full[s], evict_first);
+                            tma_load_4d_hint(vd + h * hb, &tmv, 0, 0, h, slot0, &full[s], evict_first);
                         }
                     }
                 }
@@ -249,7 +261,10 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             // before the .sync.aligned matrix instructions below.
             const bool got = mbar_wait_bounded(&full[s], static_cast<uint32_t>(it / p.stages) & 1u);
             if (!__all_sync(0xffffffffu, got)) {
-                if (lane == 0) atomicExch(p.err, kErrTimeout);
+                if (lane == 0) {
+                    atomicExch(p.err, kErrTimeout);
+                    mbar_arrive(endbar);  // the other warps' end-of-work wait does not hang on this one
+                }
                 alive = false;
                 break;
             }
@@ -414,33 +429,49 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 t += __shfl_xor_sync(0xffffffffu, t, 16);
                 l[nt][e] = t;
             }
+        // The last unit of the range: once every consumer warp of the CTA is here, no stage is
+        // read or filled any more, and the warps may use the stage ring to stage a merge.
+        bool at_end = false;
+        if (p.u_blk[u + 1] >= hi) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(endbar);
+            at_end = __all_sync(0xffffffffu, mbar_wait_bounded(endbar, 0u));
+        }
         const bool whole = ublk0 >= lo && p.u_blk[u + 1] <= hi;
         if (whole) {
             store_rows<D, NT>(p.out, acc, m, l, p.lse, nq, g, p.H, row0, h, quad, grp);
         } else {
+            // The partial of (unit u, CTA c, head h): (max, sum) per live column at
+            // part_ml[slot][h][col], and the un-normalised O in fragment order - lane L's
+            // KS * NT * 4 accumulator values contiguous at part_o[slot][h] + L * kFrag - so a
+            // partial leaves and comes back as kFrag / 4 coalesced 16-byte accesses per lane.
+            constexpr int kFrag = KS * NT * 4;
             const size_t seg = static_cast<size_t>(u) + c;
             const size_t base = (seg * p.kvh + h) * kMaxCols;
+            bool lane_live = false;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int col = nt * 8 + 2 * quad + e;
                     if (col / g >= nq) continue;
-                    float* po = p.part_o + (base + col) * D;
-#pragma unroll
-                    for (int mt = 0; mt < KS; ++mt) {
-                        po[mt * 16 + grp] = acc[mt][nt][e];
-                        po[mt * 16 + grp + 8] = acc[mt][nt][2 + e];
-                    }
+                    lane_live = true;
                     if (grp == 0) {
                         p.part_ml[(base + col) * 2] = m[nt][e];
                         p.part_ml[(base + col) * 2 + 1] = l[nt][e];
                     }
                 }
+            if (lane_live) {
+                float4* po = reinterpret_cast<float4*>(p.part_o + base * D + static_cast<size_t>(lane) * kFrag);
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+                        po[mt * NT + nt] = make_float4(acc[mt][nt][0], acc[mt][nt][1], acc[mt][nt][2], acc[mt][nt][3]);
+            }
             if (p.counters != nullptr) {
-                // The last of the unit's CTAs to finish head h merges: its own partial is
-                // still in registers, every other CTA's partial is fetched with one batch of
-                // independent loads per CTA. The counter is left at zero for the next launch.
+                // The last of the unit's CTAs to finish head h merges. The counter is left at
+                // zero for the next launch.
                 const int cf = cta_of_block(ublk0, p.total_blocks, p.ncta, p.cta_blk);
                 const int cl = cta_of_block(p.u_blk[u + 1] - 1, p.total_blocks, p.ncta, p.cta_blk);
                 __syncwarp();
@@ -454,10 +485,9 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 if (__shfl_sync(0xffffffffu, last, 0)) {
                     __threadfence();
                     // One pass in CTA order cf..cl with a running max (online softmax merge),
-                    // so the result does not depend on which CTA merges: this CTA's own
-                    // partial (bit-identical to what it stored) is taken from registers at
-                    // its place in the order. Each step's loads are independent of the
-                    // running values, so two CTAs' partials are in flight together.
+                    // so the result does not depend on which CTA merges; every partial is read
+                    // as stored (this CTA's own too), so both ways of fetching them below give
+                    // the same bits.
                     float mx[NT][2], den[NT][2];
                     float num[KS][NT][4];
 #pragma unroll
@@ -473,64 +503,96 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                             for (int i = 0; i < 4; ++i) num[mt][nt][i] = 0.f;
-                    // Where registers allow (one n8 tile, D <= 128), a step's loads go into
-                    // arrays and two steps are unrolled; elsewhere that spills, so the loads
-                    // are folded into the accumulation one step at a time.
-                    constexpr bool kArr = NT == 1 && D <= 128;
-                    auto merge_step = [&](int cc) {
-                        const size_t ob = ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols;
-                        const bool own = cc == c;
+                    // folds one partial: ml = its (max, sum) row, fr = this lane's fragment
+                    auto fold = [&](const float* ml, const float4* fr, bool from_global) {
+                        float a[NT][2], b[NT][2];
 #pragma unroll
                         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                             for (int e = 0; e < 2; ++e) {
                                 const int col = nt * 8 + 2 * quad + e;
-                                const float mc = own ? m[nt][e] : __ldcg(p.part_ml + (ob + col) * 2);
-                                const float lc = own ? l[nt][e] : __ldcg(p.part_ml + (ob + col) * 2 + 1);
-                                const float* po = p.part_o + (ob + col) * D;
-                                float o0[kArr ? KS : 1], o1[kArr ? KS : 1];
-                                if constexpr (kArr) {
-#pragma unroll
-                                    for (int mt = 0; mt < KS; ++mt) {
-                                        o0[mt] = own ? acc[mt][nt][e] : __ldcg(po + mt * 16 + grp);
-                                        o1[mt] = own ? acc[mt][nt][2 + e] : __ldcg(po + mt * 16 + grp + 8);
-                                    }
-                                }
+                                const bool live = col / g < nq;
+                                const float mc = live ? (from_global ? __ldcg(ml + 2 * col) : ml[2 * col]) : -INFINITY;
+                                const float lc = live ? (from_global ? __ldcg(ml + 2 * col + 1) : ml[2 * col + 1]) : 0.f;
                                 const float mn = fmaxf(mx[nt][e], mc);
-                                const float a = mx[nt][e] == -INFINITY ? 0.f : exp2f(mx[nt][e] - mn);
-                                const float b = mc == -INFINITY ? 0.f : exp2f(mc - mn);
+                                a[nt][e] = mx[nt][e] == -INFINITY ? 0.f : exp2f(mx[nt][e] - mn);
+                                b[nt][e] = mc == -INFINITY ? 0.f : exp2f(mc - mn);
                                 mx[nt][e] = mn;
-                                den[nt][e] = den[nt][e] * a + lc * b;
+                                den[nt][e] = den[nt][e] * a[nt][e] + lc * b[nt][e];
+                            }
 #pragma unroll
-                                for (int mt = 0; mt < KS; ++mt) {
-                                    float x0, x1;
-                                    if constexpr (kArr) {
-                                        x0 = o0[mt];
-                                        x1 = o1[mt];
-                                    } else {
-                                        x0 = own ? acc[mt][nt][e] : __ldcg(po + mt * 16 + grp);
-                                        x1 = own ? acc[mt][nt][2 + e] : __ldcg(po + mt * 16 + grp + 8);
-                                    }
-                                    num[mt][nt][e] = num[mt][nt][e] * a + x0 * b;
-                                    num[mt][nt][2 + e] = num[mt][nt][2 + e] * a + x1 * b;
-                                }
+                        for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt) {
+                                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                                if (lane_live) x = from_global ? __ldcg(fr + mt * NT + nt) : fr[mt * NT + nt];
+                                num[mt][nt][0] = num[mt][nt][0] * a[nt][0] + x.x * b[nt][0];
+                                num[mt][nt][1] = num[mt][nt][1] * a[nt][1] + x.y * b[nt][1];
+                                num[mt][nt][2] = num[mt][nt][2] * a[nt][0] + x.z * b[nt][0];
+                                num[mt][nt][3] = num[mt][nt][3] * a[nt][1] + x.w * b[nt][1];
                             }
                     };
-                    if constexpr (kArr) {
+                    auto ml_of = [&](int cc) {
+                        return p.part_ml + ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols * 2;
+                    };
+                    auto fr_of = [&](int cc) {
+                        return reinterpret_cast<const float4*>(
+                                   p.part_o + ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols * D) +
+                               lane * (kFrag / 4);
+                    };
+                    // At the end of the CTA's range the partials are staged in this warp's share
+                    // of the idle stage ring, several per bulk-copy round trip; a unit spread
+                    // over many CTAs (a long sequence) is merged by its slowest CTA at the end of
+                    // the launch, where two partials per round trip of register loads would
+                    // stretch the tail. Elsewhere (a merge mid-range, rare) registers are used.
+                    constexpr uint32_t kFragBytes = 32u * kFrag * 4u;  // all lanes' fragments
+                    constexpr uint32_t kMlBytes = kMaxCols * 2u * 4u;  // (max, sum) of every column
+                    constexpr uint32_t kPieceBytes = kFragBytes + kMlBytes;
+                    const uint32_t region_bytes = (static_cast<uint32_t>(p.stages) * 2u * tile_bytes / nwc) & ~127u;
+                    const int per_batch = static_cast<int>(region_bytes / kPieceBytes);
+                    bool merged = true;
+                    if (at_end && per_batch >= 2) {
+                        uint8_t* region = smem + static_cast<size_t>(h) * region_bytes;
+                        uint64_t* mb = &mbar_m[h];
+                        if (lane == 0) fence_proxy_async_global();
+                        int batch = 0;
+                        for (int c0 = cf; c0 <= cl && merged; c0 += per_batch, ++batch) {
+                            const int nb = min(per_batch, cl - c0 + 1);
+                            if (lane == 0) {
+                                mbar_arrive_expect_tx(mb, static_cast<uint32_t>(nb) * kPieceBytes);
+                                for (int i = 0; i < nb; ++i) {
+                                    const size_t sg2 = (static_cast<size_t>(u) + c0 + i) * p.kvh + h;
+                                    bulk_load(region + i * kPieceBytes, p.part_o + sg2 * kMaxCols * D, kFragBytes, mb);
+                                    bulk_load(region + i * kPieceBytes + kFragBytes, p.part_ml + sg2 * kMaxCols * 2,
+                                              kMlBytes, mb);
+                                }
+                            }
+                            if (!__all_sync(0xffffffffu, mbar_wait_bounded(mb, static_cast<uint32_t>(batch & 1)))) {
+                                if (lane == 0) atomicExch(p.err, kErrTimeout);
+                                merged = false;
+                                break;
+                            }
+                            for (int i = 0; i < nb; ++i)
+                                fold(reinterpret_cast<const float*>(region + i * kPieceBytes + kFragBytes),
+                                     reinterpret_cast<const float4*>(region + i * kPieceBytes) + lane * (kFrag / 4), false);
+                            __syncwarp();  // every lane is done with the batch before the next lands
+                        }
+                    } else if constexpr (NT == 1 && D <= 128) {
 #pragma unroll 2
-                        for (int cc = cf; cc <= cl; ++cc) merge_step(cc);
+                        for (int cc = cf; cc <= cl; ++cc) fold(ml_of(cc), fr_of(cc), true);
                     } else {
 #pragma unroll 1
-                        for (int cc = cf; cc <= cl; ++cc) merge_step(cc);
+                        for (int cc = cf; cc <= cl; ++cc) fold(ml_of(cc), fr_of(cc), true);
                     }
-                    store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp);
+                    if (merged) store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp);
                 }
             }
         }
     }
 }
 
-// One CTA per (split unit, KV head): combine the partials of every CTA that worked on it.
+// One CTA per (split unit, KV head): combine the partials of every CTA that worked on it
+// (the separate-launch merge; partials in tc_attn_kernel's fragment order).
 __global__ void merge_kernel(const MergeParams p) {
     const int e = blockIdx.x;
     const int h = blockIdx.y;
@@ -540,6 +602,7 @@ __global__ void merge_kernel(const MergeParams p) {
     const int seq = p.u_seq[u];
     const int row0 = p.offsets[seq] + p.u_t0[u];
     const int ncols = p.u_n[u] * p.g;
+    const int frag = (p.D / 16) * p.nt * 4;  // floats per lane of one partial
     for (int col = 0; col < ncols; ++col) {
         float mmax = -INFINITY;
         for (int c = c0; c <= c1; ++c) {
@@ -553,11 +616,17 @@ __global__ void merge_kernel(const MergeParams p) {
         }
         const float inv = 1.f / den;
         float* op = p.out + (static_cast<size_t>(row0 + col / p.g) * p.H + h * p.g + col % p.g) * p.D;
+        // column col, dim d: lane quad + 4 * grp, value (mt * NT + nt) * 4 + 2 * hi + e
+        const int nt = col / 8, quad = (col % 8) / 2, ce = col & 1;
         for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+            const int mt = d / 16, r = d % 16, grp = r & 7, hi = r >> 3;
+            const int lane = quad + 4 * grp;
+            const int vi = (mt * p.nt + nt) * 4 + 2 * hi + ce;
             float num = 0.f;
             for (int c = c0; c <= c1; ++c) {
-                const size_t idx = ((static_cast<size_t>(u) + c) * p.kvh + h) * kMaxCols + col;
-                num += exp2f(p.part_ml[idx * 2] - mmax) * p.part_o[idx * p.D + d];
+                const size_t sg = (static_cast<size_t>(u) + c) * p.kvh + h;
+                const size_t idx = sg * kMaxCols + col;
+                num += exp2f(p.part_ml[idx * 2] - mmax) * p.part_o[sg * kMaxCols * p.D + lane * frag + vi];
             }
             op[d] = num * inv;
         }
@@ -598,7 +667,10 @@ int tc_max_active_ctas(int D, int NT, int kvh, size_t smem) {
 }
 
 size_t tc_smem_bytes(int D, int bs, int kvh, int stages) {
-    return static_cast<size_t>(stages) * 2 * bs * kvh * D * 2 + 2 * stages * sizeof(uint64_t) + 1024;
+    // stages of K + V blocks, a full and an empty barrier per stage, the end-of-work barrier and
+    // one merge barrier per consumer warp, and the slack that aligns the base to 1024 bytes
+    return static_cast<size_t>(stages) * 2 * bs * kvh * D * 2 + 2 * stages * sizeof(uint64_t) +
+           (1 + kTcMaxKvHeads) * sizeof(uint64_t) + 1024;
 }
 
 cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUtensorMap* tmv,

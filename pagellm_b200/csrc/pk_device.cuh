@@ -34,6 +34,12 @@ __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Generic-proxy writes to global memory (made visible to this thread by an acquire) before
+// async-proxy (bulk copy) reads of them.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -96,6 +102,30 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
         "r"(smem_u32(bar))
         : "memory");
+}
+
+// The same with an L2 cache policy (from createpolicy) for the lines it reads.
+__device__ __forceinline__ void tma_load_4d_hint(void* smem_dst, const CUtensorMap* map, int c0, int c1,
+                                                 int c2, int c3, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+        "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// L2 cache policy: the lines of every access made with it are the first to be evicted.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// L2 prefetch of `bytes` (a multiple of 16, 16-byte aligned) of global memory.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* gptr, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gptr)), "r"(bytes)
+                 : "memory");
 }
 
 // Untiled bulk copy global -> shared (no multicast), completion as transaction bytes on

@@ -21,7 +21,9 @@ constexpr int kWideKeys = 128;  // keys per tile of the wide-tile kernel (a mult
 struct TcParams {
     const float* q;        // [rows][H][D]
     float* out;            // [rows][H][D]
-    float* part_o;         // [segments][kvh][kMaxCols][D]  un-normalised partial sums
+    // [segments][kvh] blocks of kMaxCols * D floats: un-normalised partial sums in fragment
+    // order (lane L's KS * NT * 4 accumulator values contiguous at L * KS * NT * 4)
+    float* part_o;
     float* part_ml;        // [segments][kvh][kMaxCols][2]  (running max, sum), log2 domain
     int* err;              // device error word
     const int32_t* indptr;  // [nseq+1] block-table CSR
@@ -77,6 +79,7 @@ struct MergeParams {
     int g;
     int H;
     int D;
+    int nt;  // n8 tiles of the attention launch that wrote the partials (fragment layout)
 };
 
 // CUDA-core attention for any pool dtype / head_dim (float32 pools, odd shapes).

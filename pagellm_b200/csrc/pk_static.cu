@@ -246,6 +246,7 @@ extern "C" PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, in
         mp.g = g;
         mp.H = n_heads;
         mp.D = P.d;
+        mp.nt = 1;
         e = pk::launch_merge(mp, nsplit, st);
         if (e != cudaSuccess) return sfail(PK_ERR_CUDA, "merge launch: %s", cudaGetErrorString(e));
     }

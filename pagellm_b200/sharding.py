@@ -89,6 +89,87 @@ class HeadGather:
         return self._out
 
 
+class PeerHeadGather:
+    """The head-sharded all-gather as one libpagekv launch per step over peer memory: every
+    rank stores its ``[rows, H/world, D]`` float32 slice straight into every rank's
+    ``[rows, H, D]`` result buffer (IPC-mapped over NVLink) and the launch completes once all
+    slices have landed. Buffers are created on the first call (a collective: every rank calls
+    with the same shape) and grown collectively when a larger result is needed. The returned
+    tensor is the library's buffer: it stays valid until the call after next."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self._g = None
+        self._bytes = 0
+
+    def _setup(self, nbytes: int, device):
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        lib = _lib.load()
+        self.close()
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        h = C.c_void_p()
+        _lib.check(lib.pk_peer_gather_create(device.index, world, rank, nbytes, C.byref(h)))
+        self._g = h.value
+        self._bytes = nbytes
+        mine = C.create_string_buffer(64)
+        _lib.check(lib.pk_peer_gather_handle(self._g, mine))
+        every = [None] * world
+        dist.all_gather_object(every, mine.raw, group=self.group)
+        _lib.check(lib.pk_peer_gather_open(self._g, b"".join(every)))
+
+    def __call__(self, out_slice):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if not out_slice.is_cuda or out_slice.dtype != torch.float32:
+            raise ValueError("peer head gather takes float32 CUDA slices")
+        world = dist.get_world_size(self.group)
+        rows, hs, d = out_slice.shape
+        nbytes = max(16, rows * world * hs * d * 4)
+        if self._g is None or nbytes > self._bytes:
+            self._setup(nbytes, out_slice.device)
+        src = out_slice if out_slice.is_contiguous() and out_slice.data_ptr() % 16 == 0 else out_slice.contiguous()
+        res = C.c_void_p()
+        st = torch.cuda.current_stream(out_slice.device).cuda_stream
+        _lib.check(_lib.load().pk_peer_gather_heads(self._g, src.data_ptr(), rows, hs * d, C.byref(res), st))
+        from .cache.paged import _CudaArray
+
+        return torch.as_tensor(_CudaArray(res.value, (rows, world * hs, d), "<f4", self), device=out_slice.device)
+
+    def check(self, stream=None) -> None:
+        """Synchronise and raise DeviceTimeout if a peer's slice did not arrive in time."""
+        import torch
+
+        from . import _lib
+
+        if self._g is not None:
+            st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+            _lib.check(_lib.load().pk_peer_gather_check(self._g, st))
+
+    def close(self) -> None:
+        if self._g is not None:
+            from . import _lib
+
+            _lib.load().pk_peer_gather_destroy(self._g)
+            self._g = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def gather_heads(out_slice, group=None):
     """One-off :class:`HeadGather` call (fresh buffers; the returned tensor is the caller's)."""
     return HeadGather(group)(out_slice)
