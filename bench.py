@@ -366,7 +366,7 @@ def attention_roofline(w, batch, prof_ms, prof_n, traffic=None):
 def measure_c5(ctx: Ctx, layout: str, steps: int, warmup: int) -> dict:
     """C5 (128 sequences) split over this run's ranks, one layout, strong scaling."""
     from pagellm_b200 import workloads
-    from pagellm_b200.sharding import HeadGather, shard_sequences
+    from pagellm_b200.sharding import HeadGather, PeerHeadGather, shard_sequences
 
     torch = ctx.torch
     L = workloads.c5_lengths(0)
@@ -377,7 +377,11 @@ def measure_c5(ctx: Ctx, layout: str, steps: int, warmup: int) -> dict:
     else:
         w = workloads.c5(0, lengths=L[shard_sequences(L, ctx.world)[ctx.rank]])
     job = Job(ctx, w, seed=ctx.rank)
-    gather = HeadGather() if (layout == "head" and ctx.world > 1) else None
+    sharded = layout == "head" and ctx.world > 1
+    # head-sharded exchange: one push launch over peer memory (the product path); the NCCL
+    # all-gather + interleave kernel is timed beside it for comparison
+    gather = PeerHeadGather() if sharded else None
+    nccl = HeadGather() if sharded else None
     full = {}
 
     def step():
@@ -387,21 +391,32 @@ def measure_c5(ctx: Ctx, layout: str, steps: int, warmup: int) -> dict:
 
     ms = ctx.timed(step, steps, warmup)
     us = ms / steps * 1e3
+    if sharded:
+        gather.check()
+        job.attend_layer()
+        same = bool(torch.equal(gather(job.out), nccl(job.out)))
+        ms_nccl = ctx.timed(lambda: (job.attend_layer(), nccl(job.out)), steps, warmup)
     prof_ms, prof_n = job.profile(job.attend_layer, steps)
     ctx.barrier()
     kernel_us = ctx.max_over_ranks(prof_ms[1] / max(1, prof_n[1]) * 1e3)
     res = {
-        "layout": ("head-sharded: 8/N KV heads of every sequence per GPU, NCCL all-gather of the "
-                   "[128, 64/N, 128] fp32 output slices + interleave kernel inside every step")
+        "layout": ("head-sharded: 8/N KV heads of every sequence per GPU; every step each GPU's "
+                   "[128, 64/N, 128] fp32 output slice is pushed into every GPU's [128, 64, 128] result "
+                   "over peer memory (one launch, epoch flag barrier)")
         if layout == "head" else "sequence-sharded: whole sequences per GPU (longest first), no collective",
         "steps": steps,
         "us_per_step": round(us, 2),
         "tokens_per_s": round(len(L) * steps / (ms / 1e3), 1),
         "attention_kernel_us": round(kernel_us, 2),
     }
-    if gather is not None:
+    if sharded:
         gms = ctx.timed(lambda: gather(job.out), steps, 3)
+        nms = ctx.timed(lambda: nccl(job.out), steps, 3)
         res["gather_us"] = round(gms / steps * 1e3, 2)
+        res["nccl_allgather_path"] = {"us_per_step": round(ms_nccl / steps * 1e3, 2),
+                                      "gather_us": round(nms / steps * 1e3, 2),
+                                      "result_equal_to_peer_path": same}
+        gather.close()
     kv = ctx.sum_over_ranks(float(w.kv_read_bytes()))
     hbm, src = peaks()
     per_gpu = kv / ctx.world / (us / 1e6) / 1e9

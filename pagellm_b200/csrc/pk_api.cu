@@ -833,7 +833,9 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         B->ws_part_o_floats = segs * P->kvh * pk::kMaxCols * P->d;
         const size_t ws_bytes = (B->ws_part_o_floats + segs * P->kvh * pk::kMaxCols * 2) * sizeof(float);
         PK_CUDA(B->ws.reserve(ws_bytes));
-        const size_t nctr = static_cast<size_t>(B->nu) * P->kvh;
+        // merge counters: per (partial slot, KV head) for the first level, then per (unit, KV
+        // head) for the second
+        const size_t nctr = (segs + static_cast<size_t>(B->nu)) * P->kvh;
         PK_CUDA(B->counters.reserve(nctr * sizeof(int)));
         PK_CUDA(cudaMemsetAsync(B->counters.ptr, 0, nctr * sizeof(int), st));
     }
@@ -1049,6 +1051,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
         p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
         p.counters = static_cast<int*>(B->counters.ptr);
+        p.unit_counters = p.counters + (static_cast<size_t>(B->nu) + B->ncta) * P->kvh;
         p.k_new = k_new;
         p.v_new = v_new;
         p.pool_k = reinterpret_cast<__nv_bfloat16*>(P->k_layer(layer));

@@ -100,6 +100,9 @@ __device__ __forceinline__ uint32_t tile_off(int chunk, int h, int t, int u16, i
     return static_cast<uint32_t>(row * 128 + ((u16 ^ (row & 7)) << 4));
 }
 
+// CTAs per first-level group of the two-level merge of a unit's partials.
+constexpr int kMergeGroup = 6;
+
 template <int D, int NT>
 __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
     tc_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -470,26 +473,33 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                         po[mt * NT + nt] = make_float4(acc[mt][nt][0], acc[mt][nt][1], acc[mt][nt][2], acc[mt][nt][3]);
             }
             if (p.counters != nullptr) {
-                // The last of the unit's CTAs to finish head h merges. The counter is left at
-                // zero for the next launch.
+                // Two-level merge in fixed order. The unit's CTAs cf..cl form groups of
+                // kMergeGroup consecutive CTAs; the last CTA of a group to finish head h merges
+                // the group's partials (in parallel with the other groups); with several
+                // groups it stores the group's partial in the slot of the group's first CTA,
+                // and the last group to finish merges the group partials. A unit spread over
+                // many CTAs (a long sequence) then costs two short merges at the end of the
+                // launch instead of one long one. Counters are left at zero for the next launch.
                 const int cf = cta_of_block(ublk0, p.total_blocks, p.ncta, p.cta_blk);
                 const int cl = cta_of_block(p.u_blk[u + 1] - 1, p.total_blocks, p.ncta, p.cta_blk);
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) {
-                    __threadfence();  // release the warp's partial (ordered by __syncwarp)
-                    int* ctr = p.counters + static_cast<size_t>(u) * p.kvh + h;
-                    last = atomicAdd(ctr, 1) == cl - cf;
-                    if (last) *ctr = 0;
-                }
-                if (__shfl_sync(0xffffffffu, last, 0)) {
-                    __threadfence();
-                    // One pass in CTA order cf..cl with a running max (online softmax merge),
-                    // so the result does not depend on which CTA merges; every partial is read
-                    // as stored (this CTA's own too), so both ways of fetching them below give
-                    // the same bits.
-                    float mx[NT][2], den[NT][2];
-                    float num[KS][NT][4];
+                const int ngr = (cl - cf + kMergeGroup) / kMergeGroup;
+                const int g0 = cf + (c - cf) / kMergeGroup * kMergeGroup;
+                const int g1 = min(cl, g0 + kMergeGroup - 1);
+                auto arrive_last = [&](int* ctr, int count) {
+                    __syncwarp();
+                    int last = 0;
+                    if (lane == 0) {
+                        __threadfence();  // release the warp's partial (ordered by __syncwarp)
+                        last = atomicAdd(ctr, 1) == count - 1;
+                        if (last) *ctr = 0;
+                    }
+                    last = __shfl_sync(0xffffffffu, last, 0);
+                    if (last) __threadfence();
+                    return last != 0;
+                };
+                float mx[NT][2], den[NT][2];
+                float num[KS][NT][4];
+                auto reset = [&]() {
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -503,88 +513,124 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                             for (int i = 0; i < 4; ++i) num[mt][nt][i] = 0.f;
-                    // folds one partial: ml = its (max, sum) row, fr = this lane's fragment
-                    auto fold = [&](const float* ml, const float4* fr, bool from_global) {
-                        float a[NT][2], b[NT][2];
+                };
+                // folds one partial into (mx, den, num): ml = its (max, sum) row, fr = this
+                // lane's fragment; an online softmax merge, so the order of folds fixes the bits
+                auto fold = [&](const float* ml, const float4* fr, bool from_global) {
+                    float a[NT][2], b[NT][2];
 #pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
+                    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                            for (int e = 0; e < 2; ++e) {
-                                const int col = nt * 8 + 2 * quad + e;
-                                const bool live = col / g < nq;
-                                const float mc = live ? (from_global ? __ldcg(ml + 2 * col) : ml[2 * col]) : -INFINITY;
-                                const float lc = live ? (from_global ? __ldcg(ml + 2 * col + 1) : ml[2 * col + 1]) : 0.f;
-                                const float mn = fmaxf(mx[nt][e], mc);
-                                a[nt][e] = mx[nt][e] == -INFINITY ? 0.f : exp2f(mx[nt][e] - mn);
-                                b[nt][e] = mc == -INFINITY ? 0.f : exp2f(mc - mn);
-                                mx[nt][e] = mn;
-                                den[nt][e] = den[nt][e] * a[nt][e] + lc * b[nt][e];
-                            }
+                        for (int e = 0; e < 2; ++e) {
+                            const int col = nt * 8 + 2 * quad + e;
+                            const bool live = col / g < nq;
+                            const float mc = live ? (from_global ? __ldcg(ml + 2 * col) : ml[2 * col]) : -INFINITY;
+                            const float lc = live ? (from_global ? __ldcg(ml + 2 * col + 1) : ml[2 * col + 1]) : 0.f;
+                            const float mn = fmaxf(mx[nt][e], mc);
+                            a[nt][e] = mx[nt][e] == -INFINITY ? 0.f : exp2f(mx[nt][e] - mn);
+                            b[nt][e] = mc == -INFINITY ? 0.f : exp2f(mc - mn);
+                            mx[nt][e] = mn;
+                            den[nt][e] = den[nt][e] * a[nt][e] + lc * b[nt][e];
+                        }
 #pragma unroll
-                        for (int mt = 0; mt < KS; ++mt)
+                    for (int mt = 0; mt < KS; ++mt)
 #pragma unroll
-                            for (int nt = 0; nt < NT; ++nt) {
-                                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-                                if (lane_live) x = from_global ? __ldcg(fr + mt * NT + nt) : fr[mt * NT + nt];
-                                num[mt][nt][0] = num[mt][nt][0] * a[nt][0] + x.x * b[nt][0];
-                                num[mt][nt][1] = num[mt][nt][1] * a[nt][1] + x.y * b[nt][1];
-                                num[mt][nt][2] = num[mt][nt][2] * a[nt][0] + x.z * b[nt][0];
-                                num[mt][nt][3] = num[mt][nt][3] * a[nt][1] + x.w * b[nt][1];
-                            }
-                    };
-                    auto ml_of = [&](int cc) {
-                        return p.part_ml + ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols * 2;
-                    };
-                    auto fr_of = [&](int cc) {
-                        return reinterpret_cast<const float4*>(
-                                   p.part_o + ((static_cast<size_t>(u) + cc) * p.kvh + h) * kMaxCols * D) +
-                               lane * (kFrag / 4);
-                    };
-                    // At the end of the CTA's range the partials are staged in this warp's share
-                    // of the idle stage ring, several per bulk-copy round trip; a unit spread
-                    // over many CTAs (a long sequence) is merged by its slowest CTA at the end of
-                    // the launch, where two partials per round trip of register loads would
-                    // stretch the tail. Elsewhere (a merge mid-range, rare) registers are used.
-                    constexpr uint32_t kFragBytes = 32u * kFrag * 4u;  // all lanes' fragments
-                    constexpr uint32_t kMlBytes = kMaxCols * 2u * 4u;  // (max, sum) of every column
-                    constexpr uint32_t kPieceBytes = kFragBytes + kMlBytes;
-                    const uint32_t region_bytes = (static_cast<uint32_t>(p.stages) * 2u * tile_bytes / nwc) & ~127u;
-                    const int per_batch = static_cast<int>(region_bytes / kPieceBytes);
-                    bool merged = true;
+                        for (int nt = 0; nt < NT; ++nt) {
+                            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (lane_live) x = from_global ? __ldcg(fr + mt * NT + nt) : fr[mt * NT + nt];
+                            num[mt][nt][0] = num[mt][nt][0] * a[nt][0] + x.x * b[nt][0];
+                            num[mt][nt][1] = num[mt][nt][1] * a[nt][1] + x.y * b[nt][1];
+                            num[mt][nt][2] = num[mt][nt][2] * a[nt][0] + x.z * b[nt][0];
+                            num[mt][nt][3] = num[mt][nt][3] * a[nt][1] + x.w * b[nt][1];
+                        }
+                };
+                // Merges the partials in the slots of CTAs first, first + stride, ... (count of
+                // them) into (mx, den, num), every one read as stored. At the end of the CTA's
+                // range they are staged in this warp's share of the idle stage ring, several per
+                // bulk-copy round trip; elsewhere (a merge mid-range, rare) register loads are
+                // used, two partials per round trip. Returns false if a wait timed out.
+                constexpr uint32_t kFragBytes = 32u * kFrag * 4u;  // all lanes' fragments
+                constexpr uint32_t kMlBytes = kMaxCols * 2u * 4u;  // (max, sum) of every column
+                constexpr uint32_t kPieceBytes = kFragBytes + kMlBytes;
+                const uint32_t region_bytes = (static_cast<uint32_t>(p.stages) * 2u * tile_bytes / nwc) & ~127u;
+                const int per_batch = static_cast<int>(region_bytes / kPieceBytes);
+                int batches = 0;  // this warp's merge barrier phases used so far
+                auto merge = [&](int first, int count, int stride) {
+                    reset();
+                    auto seg_of = [&](int i) { return (static_cast<size_t>(u) + first + i * stride) * p.kvh + h; };
                     if (at_end && per_batch >= 2) {
                         uint8_t* region = smem + static_cast<size_t>(h) * region_bytes;
                         uint64_t* mb = &mbar_m[h];
                         if (lane == 0) fence_proxy_async_global();
-                        int batch = 0;
-                        for (int c0 = cf; c0 <= cl && merged; c0 += per_batch, ++batch) {
-                            const int nb = min(per_batch, cl - c0 + 1);
+                        for (int i0 = 0; i0 < count; i0 += per_batch) {
+                            const int nb = min(per_batch, count - i0);
                             if (lane == 0) {
                                 mbar_arrive_expect_tx(mb, static_cast<uint32_t>(nb) * kPieceBytes);
                                 for (int i = 0; i < nb; ++i) {
-                                    const size_t sg2 = (static_cast<size_t>(u) + c0 + i) * p.kvh + h;
+                                    const size_t sg2 = seg_of(i0 + i);
                                     bulk_load(region + i * kPieceBytes, p.part_o + sg2 * kMaxCols * D, kFragBytes, mb);
                                     bulk_load(region + i * kPieceBytes + kFragBytes, p.part_ml + sg2 * kMaxCols * 2,
                                               kMlBytes, mb);
                                 }
                             }
-                            if (!__all_sync(0xffffffffu, mbar_wait_bounded(mb, static_cast<uint32_t>(batch & 1)))) {
+                            const bool got = mbar_wait_bounded(mb, static_cast<uint32_t>(batches & 1));
+                            ++batches;
+                            if (!__all_sync(0xffffffffu, got)) {
                                 if (lane == 0) atomicExch(p.err, kErrTimeout);
-                                merged = false;
-                                break;
+                                return false;
                             }
                             for (int i = 0; i < nb; ++i)
                                 fold(reinterpret_cast<const float*>(region + i * kPieceBytes + kFragBytes),
                                      reinterpret_cast<const float4*>(region + i * kPieceBytes) + lane * (kFrag / 4), false);
                             __syncwarp();  // every lane is done with the batch before the next lands
                         }
-                    } else if constexpr (NT == 1 && D <= 128) {
+                        return true;
+                    }
+                    auto fold_at = [&](int i) {
+                        const size_t sg2 = seg_of(i);
+                        fold(p.part_ml + sg2 * kMaxCols * 2,
+                             reinterpret_cast<const float4*>(p.part_o + sg2 * kMaxCols * D) + lane * (kFrag / 4), true);
+                    };
+                    if constexpr (NT == 1 && D <= 128) {
 #pragma unroll 2
-                        for (int cc = cf; cc <= cl; ++cc) fold(ml_of(cc), fr_of(cc), true);
+                        for (int i = 0; i < count; ++i) fold_at(i);
                     } else {
 #pragma unroll 1
-                        for (int cc = cf; cc <= cl; ++cc) fold(ml_of(cc), fr_of(cc), true);
+                        for (int i = 0; i < count; ++i) fold_at(i);
                     }
-                    if (merged) store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp);
+                    return true;
+                };
+                if (arrive_last(p.counters + (static_cast<size_t>(u) + g0) * p.kvh + h, g1 - g0 + 1) &&
+                    merge(g0, g1 - g0 + 1, 1)) {
+                    if (ngr == 1) {
+                        store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp);
+                    } else {
+                        // the group's partial, in the slot of its first CTA (whose partial the
+                        // merge has consumed)
+                        const size_t gb = ((static_cast<size_t>(u) + g0) * p.kvh + h) * kMaxCols;
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const int col = nt * 8 + 2 * quad + e;
+                                if (col / g < nq && grp == 0) {
+                                    p.part_ml[(gb + col) * 2] = mx[nt][e];
+                                    p.part_ml[(gb + col) * 2 + 1] = den[nt][e];
+                                }
+                            }
+                        if (lane_live) {
+                            float4* po = reinterpret_cast<float4*>(p.part_o + gb * D + static_cast<size_t>(lane) * kFrag);
+#pragma unroll
+                            for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+                                for (int nt = 0; nt < NT; ++nt)
+                                    po[mt * NT + nt] =
+                                        make_float4(num[mt][nt][0], num[mt][nt][1], num[mt][nt][2], num[mt][nt][3]);
+                        }
+                        if (arrive_last(p.unit_counters + static_cast<size_t>(u) * p.kvh + h, ngr) &&
+                            merge(cf, ngr, kMergeGroup))
+                            store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp);
+                    }
                 }
             }
         }

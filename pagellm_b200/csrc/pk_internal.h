@@ -53,9 +53,11 @@ struct TcParams {
     int per_head_layout;   // 0: one TMA box per K/V block, 1: one box per (block, head)
     int64_t layer_slot0;   // first slot of the layer in the flat [layers*num_blocks*bs] axis
     float qscale;          // log2(e) / sqrt(D)
-    // In-kernel merge: one zero-initialised counter per (unit, KV head); NULL = leave the
-    // partials to merge_kernel.
+    // In-kernel merge (NULL counters: leave the partials to merge_kernel): zero-initialised
+    // counters per (partial slot, KV head) for the first-level groups of a unit's CTAs, and per
+    // (unit, KV head) for the second level; both left at zero by the kernel.
     int* counters;
+    int* unit_counters;
     // Fused append: fp32 rows [rows][kvh][D] of this step and the layer's bf16 pool bases;
     // NULL k_new = attention only.
     const float* k_new;

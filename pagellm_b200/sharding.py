@@ -157,17 +157,30 @@ class PeerHeadGather:
             _lib.check(_lib.load().pk_peer_gather_check(self._g, st))
 
     def close(self) -> None:
+        """Collective (every rank calls it): waits until no rank's launch can still be storing
+        into this rank's buffers, then unmaps the peers' and frees this rank's."""
         if self._g is not None:
+            import torch
+            import torch.distributed as dist
+
             from . import _lib
 
+            torch.cuda.synchronize()
+            if dist.is_initialized():
+                dist.barrier(group=self.group)
             _lib.load().pk_peer_gather_destroy(self._g)
             self._g = None
 
     def __del__(self):
-        try:
-            self.close()
-        except Exception:
-            pass
+        # not collective: only frees what a missed close() left behind
+        if self._g is not None:
+            try:
+                from . import _lib
+
+                _lib.load().pk_peer_gather_destroy(self._g)
+            except Exception:
+                pass
+            self._g = None
 
 
 def gather_heads(out_slice, group=None):
