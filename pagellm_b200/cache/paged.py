@@ -20,7 +20,6 @@ from __future__ import annotations
 import ctypes as C
 import itertools
 import sys
-import weakref
 
 import numpy as np
 
@@ -157,6 +156,7 @@ class PagedKVPool:
         self.k_flat = self.k.view(flat)
         self.v_flat = self.v.view(flat)
         self._idle_batches: list[int] = []
+        self._batch_prefix_mode: dict[int, int] = {}  # handle -> prefix-sharing mode it holds
 
     # ------------------------------------------------------------------ pagellm API
     def copy_block(self, src: int, dst: int) -> None:
@@ -300,16 +300,15 @@ class PagedBatch:
         indptr, ids = _csr(block_tables)
         if len(indptr) - 1 != len(n_new_a):
             raise ValueError("block_tables and n_new differ in length")
-        self.offsets = np.zeros(len(n_new_a) + 1, dtype=np.int64)
-        np.cumsum(n_new_a, out=self.offsets[1:])
-        self.offsets = self.offsets.astype(int)
         self._starts_a, self._n_new_a = starts_a, n_new_a
+        self._offsets = None
         self._positions = None
         lib = _lib.load()
         self._lib = lib
         self._b = pool._acquire_batch()
-        self._fin = weakref.finalize(self, pool._release_batch, self._b)
-        _lib.check(lib.pk_batch_set_prefix_sharing(self._b, 1))  # recycled handles: default
+        if pool._batch_prefix_mode.get(self._b, 1) != 1:  # a recycled handle: back to the default
+            _lib.check(lib.pk_batch_set_prefix_sharing(self._b, 1))
+            pool._batch_prefix_mode[self._b] = 1
         self._prefix_sharing = "auto"
         rows = C.c_int64()
         _lib.check(lib.pk_batch_plan(self._b, len(n_new_a), _addr(indptr), _addr(ids), _addr(starts_a),
@@ -317,7 +316,26 @@ class PagedBatch:
         self.num_rows = rows.value
         self._slots = None
 
+    def __del__(self):
+        # the handle goes back to the pool for the next step's batch
+        b = getattr(self, "_b", None)
+        if b is not None:
+            try:
+                self.pool._release_batch(b)
+            except Exception:
+                pass
+            self._b = None
+
     # ------------------------------------------------------------------ step metadata
+    @property
+    def offsets(self) -> np.ndarray:
+        """First row of every sequence in the flat batch (paged.py:410), plus the total."""
+        if self._offsets is None:
+            off = np.zeros(len(self._n_new_a) + 1, dtype=np.int64)
+            np.cumsum(self._n_new_a, out=off[1:])
+            self._offsets = off.astype(int)
+        return self._offsets
+
     @property
     def positions(self) -> np.ndarray:
         """int64 absolute position of every new row (paged.py:412-414)."""
@@ -372,6 +390,7 @@ class PagedBatch:
             raise ValueError(f"prefix_sharing must be 'off', 'auto' or 'always', not {mode!r}")
         code = self._PREFIX_MODES[mode]
         _lib.check(self._lib.pk_batch_set_prefix_sharing(self._b, code))
+        self.pool._batch_prefix_mode[self._b] = code
         self._prefix_sharing = ("off", "auto", "always")[code]
 
     def prefix_stats(self) -> dict:

@@ -157,15 +157,15 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-PFN_cuPointerGetAttribute_v4000 pointer_attribute_fn() {
-    static PFN_cuPointerGetAttribute_v4000 fn = nullptr;
+PFN_cuPointerGetAttributes_v7000 pointer_attributes_fn() {
+    static PFN_cuPointerGetAttributes_v7000 fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuPointerGetAttribute", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        if (cudaGetDriverEntryPoint("cuPointerGetAttributes", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuPointerGetAttribute_v4000>(p);
+            fn = reinterpret_cast<PFN_cuPointerGetAttributes_v7000>(p);
     });
     return fn;
 }
@@ -175,19 +175,18 @@ PFN_cuPointerGetAttribute_v4000 pointer_attribute_fn() {
 // and cudaHostRegister ranges are mapped under unified addressing), else nullptr. The
 // allocation's extent comes from the driver, so a kernel never stores past the end of a
 // buffer shorter than `bytes`: such a buffer, and pageable memory, get nullptr.
-void* mapped_host_range(void* p, size_t bytes) {
-    PFN_cuPointerGetAttribute_v4000 fn = pointer_attribute_fn();
+void* mapped_host_range(const void* p, size_t bytes) {
+    PFN_cuPointerGetAttributes_v7000 fn = pointer_attributes_fn();
     if (!fn || !p || bytes == 0) return nullptr;
     const CUdeviceptr a = reinterpret_cast<CUdeviceptr>(p);
+    // one driver query for all four attributes (pageable memory reports no memory type)
     unsigned int mtype = 0;
     CUdeviceptr start = 0, dptr = 0;
     size_t size = 0;
-    if (fn(&mtype, CU_POINTER_ATTRIBUTE_MEMORY_TYPE, a) != CUDA_SUCCESS || mtype != CU_MEMORYTYPE_HOST)
-        return nullptr;
-    if (fn(&start, CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, a) != CUDA_SUCCESS ||
-        fn(&size, CU_POINTER_ATTRIBUTE_RANGE_SIZE, a) != CUDA_SUCCESS ||
-        fn(&dptr, CU_POINTER_ATTRIBUTE_DEVICE_POINTER, a) != CUDA_SUCCESS)
-        return nullptr;
+    CUpointer_attribute attrs[4] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE, CU_POINTER_ATTRIBUTE_RANGE_START_ADDR,
+                                    CU_POINTER_ATTRIBUTE_RANGE_SIZE, CU_POINTER_ATTRIBUTE_DEVICE_POINTER};
+    void* data[4] = {&mtype, &start, &size, &dptr};
+    if (fn(4, attrs, data, a) != CUDA_SUCCESS || mtype != CU_MEMORYTYPE_HOST) return nullptr;
     if (a < start || a - start > size || bytes > size - (a - start)) return nullptr;
     if (dptr == 0 || dptr % 16 != 0) return nullptr;
     return reinterpret_cast<void*>(dptr);
@@ -246,7 +245,9 @@ struct pk_batch {
     // positions / slots of the step's rows (rows buffer) not built yet; the plan's stream
     mutable bool rows_pending = false;
     cudaStream_t rows_stream = nullptr;
-    DevBuf counters;  // per (unit, KV head) merge counters, zero between launches
+    // merge counters, zero between launches: uploaded as zeros with every attention plan
+    // (plan part 22), left at zero by the kernel, reset by pk_batch_check after a timeout
+    std::vector<int32_t> ctr_zero;
     // Wide-tile work runs on a side stream, forked from and joined back into the caller's
     // stream with events, so it overlaps the split-KV kernel.
     cudaStream_t side = nullptr;
@@ -273,6 +274,8 @@ struct pk_batch {
     // wide-kernel schedule: per CTA a range of segments (pair, head, key tiles, slot, ph)
     std::vector<int32_t> pair_kend, cta_seg, seg, ph_info, split;
     int ncta_chunk = 0, ncta_prefix = 0, nslots = 0, nph = 0, nwsplit = 0;
+    int nwsplit_chunk = 0;  // the first nwsplit_chunk entries of split belong to chunk pairs
+    int tc_per_sm = 1;      // split-KV CTAs that share an SM in the current plan
     DevBuf wpart;  // partial O and (max, sum) of pair-heads cut between CTAs
     DevBuf qpk;    // packed bf16 query tiles of the wide-tile items (+1 zero tile)
     std::vector<int32_t> u_kb0;    // per unit: first block read (after a shared prefix)
@@ -594,11 +597,16 @@ void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>
     }
 }
 
-// Wide-kernel schedule. Chunk pairs: one CTA per (pair, KV head), whole key range. Prefix
-// pairs: the (pair-head, key tile) space, pair-heads in order, cut into G equal shares (G =
-// SMs, fewer when shares would be under kWideMinTilesPerCta tiles); a CTA's share is its
-// segment list; a pair-head met by several CTAs gets one partial slot per CTA.
-void build_wide_schedule(pk_batch* B) {
+// Wide-kernel schedule: the (pair-head, key tile) work of the chunk pairs, then of the
+// shared-prefix pairs, each cut over G CTAs with a makespan of ceil(W / G) tiles (W the
+// kind's tiles). Whole pair-heads first, longest first, each to the least-loaded CTA that
+// stays within the makespan (a whole pair-head needs no partial and no merge); the
+// pair-heads that fit nowhere are cut into pieces that fill the CTAs' spare capacity in CTA
+// order, so only those few leave partial slots (one per piece) for wide_merge_kernel.
+// Chunk pair-heads (run beside the split-KV kernel on a second stream) are never cut: one CTA
+// each. Shared-prefix work (after the split-KV kernel) gets all SMs, fewer when shares would
+// be under kWideMinTilesPerCta tiles.
+void build_wide_schedule(pk_batch* B, int64_t chunk_ctas) {
     pk_pool* P = B->pool;
     const int kvh = P->kvh;
     const int npairs = B->npair_chunk + B->npair_prefix;
@@ -611,35 +619,22 @@ void build_wide_schedule(pk_batch* B) {
     B->seg.clear();
     B->ph_info.clear();
     B->split.clear();
-    B->nslots = B->nwsplit = 0;
-    auto tiles = [&](int x) { return ceil_div(B->pair_kend[x], pk::kWideKeys); };
-    auto add_seg = [&](int x, int h, int t0, int t1, int slot, int ph) {
-        B->seg.insert(B->seg.end(), {x, h, t0, t1, slot, ph});
-    };
-    for (int x = 0; x < B->npair_chunk; ++x)
-        for (int h = 0; h < kvh; ++h) {
-            const int ph = static_cast<int>(B->ph_info.size() / 2);
-            B->ph_info.insert(B->ph_info.end(), {0, 1});
-            add_seg(x, h, 0, tiles(x), -1, ph);
-            B->cta_seg.push_back(static_cast<int32_t>(B->seg.size() / 6));
-        }
-    B->ncta_chunk = B->npair_chunk * kvh;
-    int64_t W = 0;
-    for (int x = B->npair_chunk; x < npairs; ++x) W += static_cast<int64_t>(tiles(x)) * kvh;
-    B->ncta_prefix = 0;
-    if (W > 0) {
-        const int64_t G = std::max<int64_t>(1, std::min<int64_t>(P->num_sms, W / kWideMinTilesPerCta));
-        const size_t seg0 = B->seg.size() / 6;
-        // Whole pair-heads first: longest first, each to the least-loaded CTA that stays
-        // within ceil(W / G) tiles (a whole pair-head needs no partial and no merge). The
-        // pair-heads that fit nowhere are cut into pieces that fill the CTAs' spare
-        // capacity in CTA order, so the makespan is the same ceil(W / G) as an even cut,
-        // while only those few pair-heads leave partials for the merge.
-        const int nphp = B->npair_prefix * kvh;
-        auto ph_tiles = [&](int q) { return static_cast<int64_t>(tiles(B->npair_chunk + q / kvh)); };
-        const int64_t target = (W + G - 1) / G;
-        std::vector<int> order(nphp);
-        for (int q = 0; q < nphp; ++q) order[q] = q;
+    B->nslots = B->nwsplit = B->nwsplit_chunk = 0;
+    auto tiles = [&](int x) { return static_cast<int64_t>(ceil_div(B->pair_kend[x], pk::kWideKeys)); };
+    // Schedules the pair-heads of pairs [x0, x1) over at most G CTAs; returns the CTAs used.
+    // whole_only: no pair-head is cut (the makespan is at least the longest pair-head).
+    auto stream_k = [&](int x0, int x1, int64_t G, bool whole_only) -> int {
+        const int nph = (x1 - x0) * kvh;
+        if (nph <= 0) return 0;
+        auto ph_tiles = [&](int q) { return tiles(x0 + q / kvh); };
+        int64_t W = 0;
+        for (int q = 0; q < nph; ++q) W += ph_tiles(q);
+        G = std::max<int64_t>(1, std::min(G, W));
+        int64_t longest = 0;
+        for (int q = 0; q < nph; ++q) longest = std::max(longest, ph_tiles(q));
+        const int64_t target = whole_only ? std::max((W + G - 1) / G, longest) : (W + G - 1) / G;
+        std::vector<int> order(nph);
+        for (int q = 0; q < nph; ++q) order[q] = q;
         std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return ph_tiles(a) > ph_tiles(b); });
         std::vector<int64_t> load(G, 0);
         std::vector<std::vector<std::array<int64_t, 3>>> segs_of(G);  // {q, t0, t1}
@@ -671,38 +666,45 @@ void build_wide_schedule(pk_batch* B) {
                 t += take;
             }
         }
-        for (int64_t cc = 0; cc < G; ++cc) {
-            for (const auto& sg : segs_of[cc]) {
-                const int q = static_cast<int>(sg[0]);
-                add_seg(B->npair_chunk + q / kvh, q % kvh, static_cast<int>(sg[1]), static_cast<int>(sg[2]), 0,
-                        B->ncta_chunk + q);
-            }
-            B->cta_seg.push_back(static_cast<int32_t>(B->seg.size() / 6));
-        }
-        B->ncta_prefix = static_cast<int>(G);
-        // slots: a pair-head with several segments gets one slot per segment
-        const int ph_base = static_cast<int>(B->ph_info.size() / 2);
-        const int nph_prefix = B->npair_prefix * kvh;
-        std::vector<int32_t> count(nph_prefix, 0);
-        const size_t nseg = B->seg.size() / 6;
-        for (size_t sidx = seg0; sidx < nseg; ++sidx) count[B->seg[6 * sidx + 5] - ph_base]++;
-        std::vector<int32_t> next(nph_prefix, -1);
-        for (int q = 0; q < nph_prefix; ++q) {
+        // a pair-head cut into several segments gets one partial slot per segment
+        std::vector<int32_t> count(nph, 0), next(nph, -1);
+        for (int64_t cc = 0; cc < G; ++cc)
+            for (const auto& sg : segs_of[cc]) count[sg[0]]++;
+        for (int q = 0; q < nph; ++q) {
             if (count[q] > 1) {
-                B->ph_info.insert(B->ph_info.end(), {B->nslots, count[q]});
-                B->split.insert(B->split.end(), {B->npair_chunk + q / kvh, q % kvh, B->nslots, count[q]});
+                B->split.insert(B->split.end(), {x0 + q / kvh, q % kvh, B->nslots, count[q]});
                 next[q] = B->nslots;
                 B->nslots += count[q];
-            } else {
-                B->ph_info.insert(B->ph_info.end(), {0, 1});
             }
         }
-        for (size_t sidx = seg0; sidx < nseg; ++sidx) {
-            const int q = B->seg[6 * sidx + 5] - ph_base;
-            B->seg[6 * sidx + 4] = next[q] >= 0 ? next[q]++ : -1;
+        int used = 0;
+        for (int64_t cc = 0; cc < G; ++cc) {
+            if (segs_of[cc].empty()) continue;
+            for (const auto& sg : segs_of[cc]) {
+                const int q = static_cast<int>(sg[0]);
+                const int slot = next[q] >= 0 ? next[q]++ : -1;
+                B->seg.insert(B->seg.end(), {x0 + q / kvh, q % kvh, static_cast<int32_t>(sg[1]),
+                                             static_cast<int32_t>(sg[2]), slot, 0});
+            }
+            B->cta_seg.push_back(static_cast<int32_t>(B->seg.size() / 6));
+            ++used;
         }
-    }
-    B->nph = static_cast<int>(B->ph_info.size() / 2);
+        return used;
+    };
+    int64_t Wc = 0, Wp = 0;
+    for (int x = 0; x < B->npair_chunk; ++x) Wc += tiles(x) * kvh;
+    for (int x = B->npair_chunk; x < npairs; ++x) Wp += tiles(x) * kvh;
+    const int64_t nph_chunk = static_cast<int64_t>(B->npair_chunk) * kvh;
+    // Chunk pair-heads stay whole, one per CTA: cut into pieces (measured on C3: 64 pair-heads
+    // of 9-12 tiles over the 76 SMs the split-KV kernel leaves), each piece's query-tile load,
+    // 128 KB partial and merge cost more than the balance gains.
+    (void)chunk_ctas;
+    (void)Wc;
+    B->ncta_chunk = stream_k(0, B->npair_chunk, nph_chunk, true);
+    B->nwsplit_chunk = static_cast<int>(B->split.size() / 4);
+    B->ncta_prefix = stream_k(B->npair_chunk, npairs,
+                              std::min<int64_t>(P->num_sms, std::max<int64_t>(1, Wp / kWideMinTilesPerCta)), false);
+    B->nph = 0;
     B->nwsplit = static_cast<int>(B->split.size() / 4);
 }
 
@@ -805,7 +807,6 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     };
     B->npair_chunk = make_pairs(0, B->nwide);
     B->npair_prefix = make_pairs(B->nwide, B->nwide + B->nprefix);
-    build_wide_schedule(B);
     B->nu = static_cast<int>(B->u_seq.size());
     B->ngeneric = static_cast<int>(B->gen_rows.size());
     if (B->nu > 0) {
@@ -816,6 +817,7 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         int& occ = P->tc_occ[std::min(B->nt, 2)];
         if (occ == 0) occ = pk::tc_max_active_ctas(P->d, B->nt, P->kvh, P->tc_smem);
         const int per_sm = std::max(1, std::min(P->tc_ctas_per_sm, occ));
+        B->tc_per_sm = per_sm;
         const int64_t nmax = split_kv_ctas(T, B->nu, static_cast<int64_t>(P->num_sms) * per_sm);
         B->ncta = partition_blocks(B->u_blk.data(), B->nu, nmax,
                                    unit_switch_blocks(P, static_cast<int64_t>(P->num_sms) * per_sm), B->cta_blk);
@@ -834,11 +836,12 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         const size_t ws_bytes = (B->ws_part_o_floats + segs * P->kvh * pk::kMaxCols * 2) * sizeof(float);
         PK_CUDA(B->ws.reserve(ws_bytes));
         // merge counters: per (partial slot, KV head) for the first level, then per (unit, KV
-        // head) for the second
-        const size_t nctr = (segs + static_cast<size_t>(B->nu)) * P->kvh;
-        PK_CUDA(B->counters.reserve(nctr * sizeof(int)));
-        PK_CUDA(cudaMemsetAsync(B->counters.ptr, 0, nctr * sizeof(int), st));
+        // head) for the second; they travel as zeros with the plan's upload
+        B->ctr_zero.assign((segs + static_cast<size_t>(B->nu)) * P->kvh, 0);
     }
+    // chunk work shares the GPU with the split-KV CTAs: it gets the SMs they leave free
+    build_wide_schedule(B, B->use_tc ? std::max<int64_t>(1, P->num_sms - ceil_div(B->ncta, B->tc_per_sm))
+                                     : P->num_sms);
     B->plan.begin();
     B->plan.add(B->u_seq.data(), B->u_seq.size() * 4);
     B->plan.add(B->u_t0.data(), B->u_t0.size() * 4);
@@ -862,6 +865,8 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan.add(B->seg.data(), B->seg.size() * 4);
     B->plan.add(B->split.data(), B->split.size() * 4);
     B->plan.add(B->cta_blk.data(), B->cta_blk.size() * 4);
+    if (!B->use_tc) B->ctr_zero.clear();
+    B->plan.add(B->ctr_zero.data(), B->ctr_zero.size() * 4);  // 22
     if (B->nslots > 0)
         PK_CUDA(B->wpart.reserve(static_cast<size_t>(B->nslots) * 2 * 128 * (128 + 2) * sizeof(float)));
     if (!B->w_seq.empty())
@@ -1018,8 +1023,12 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         const pk::WideParams w = wide_params(B, layer, H, q, out, 0, B->ncta_chunk, nullptr);
         PK_CUDA(prof_begin(B, ws));
         PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, ws));
-        PK_CUDA(prof_end(B, kProfWide, ws));
         B->launches++;
+        if (B->nwsplit_chunk > 0) {  // chunk pair-heads cut between CTAs: normalised merge
+            PK_CUDA(pk::launch_wide_merge(w, B->plan.at<int32_t>(20), B->nwsplit_chunk, ws));
+            B->launches++;
+        }
+        PK_CUDA(prof_end(B, kProfWide, ws));
     }
     if (B->use_tc) {
         pk::TcParams p{};
@@ -1050,7 +1059,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.per_head_layout = P->tc_per_head;
         p.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
         p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
-        p.counters = static_cast<int*>(B->counters.ptr);
+        p.counters = B->plan.at<int>(22);
         p.unit_counters = p.counters + (static_cast<size_t>(B->nu) + B->ncta) * P->kvh;
         p.k_new = k_new;
         p.v_new = v_new;
@@ -1090,8 +1099,9 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         if (pack_on_side) PK_CUDA(cudaStreamWaitEvent(st, B->ev_pack, 0));
         PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_wide_attention(&P->tmk1, &P->tmv1, w, st));
-        if (B->nwsplit > 0) {
-            PK_CUDA(pk::launch_wide_merge(w, B->plan.at<int32_t>(20), B->nwsplit, st));
+        if (B->nwsplit > B->nwsplit_chunk) {
+            PK_CUDA(pk::launch_wide_merge(w, B->plan.at<int32_t>(20) + 4 * B->nwsplit_chunk,
+                                          B->nwsplit - B->nwsplit_chunk, st));
             B->launches++;
         }
         PK_CUDA(prof_end(B, kProfWide, st));
@@ -1333,7 +1343,6 @@ int pk_batch_destroy(pk_batch* B) {
     B->rows.release();
     B->err.release();
     B->ws.release();
-    B->counters.release();
     B->io.release();
     B->lse.release();
     B->wpart.release();
@@ -1574,9 +1583,20 @@ int pk_batch_write_and_attend_host(pk_batch* B, int layer, int n_heads, const fl
     float* od = vd + up(kn);
     B->io_h2d = B->io_d2h = B->io_direct = 0;
     if (B->nrows > 0) {
-        PK_CUDA(cudaMemcpyAsync(qd, q_host, qn * sizeof(float), cudaMemcpyHostToDevice, st));
-        PK_CUDA(cudaMemcpyAsync(kd, k_host, kn * sizeof(float), cudaMemcpyHostToDevice, st));
-        PK_CUDA(cudaMemcpyAsync(vd, v_host, kn * sizeof(float), cudaMemcpyHostToDevice, st));
+        // Inputs in page-locked memory the device can address come over in one launch that
+        // reads all three (many reads in flight on the host link at once); other memory by the
+        // copy engine, one copy each.
+        const float* qm = static_cast<const float*>(mapped_host_range(q_host, qn * sizeof(float)));
+        const float* km = qm ? static_cast<const float*>(mapped_host_range(k_host, kn * sizeof(float))) : nullptr;
+        const float* vm = km ? static_cast<const float*>(mapped_host_range(v_host, kn * sizeof(float))) : nullptr;
+        if (vm && qn % 4 == 0 && kn % 4 == 0) {
+            PK_CUDA(pk::launch_h2d_gather(qm, qd, static_cast<int64_t>(qn), km, kd, static_cast<int64_t>(kn), vm, vd,
+                                          static_cast<int64_t>(kn), st));
+        } else {
+            PK_CUDA(cudaMemcpyAsync(qd, q_host, qn * sizeof(float), cudaMemcpyHostToDevice, st));
+            PK_CUDA(cudaMemcpyAsync(kd, k_host, kn * sizeof(float), cudaMemcpyHostToDevice, st));
+            PK_CUDA(cudaMemcpyAsync(vd, v_host, kn * sizeof(float), cudaMemcpyHostToDevice, st));
+        }
         B->io_h2d = static_cast<int64_t>(qn + 2 * kn) * sizeof(float);
         // the attention plan now, while the copies run (pk_batch_write_and_attend reuses it)
         if (layer >= 0 && layer < P->n_layers && B->plan_H != n_heads) {
@@ -1620,7 +1640,8 @@ int pk_batch_check(pk_batch* B, void* stream) {
     PK_CUDA(cudaMemcpy(&word, B->err.ptr, sizeof(int), cudaMemcpyDeviceToHost));
     if (word != 0) {
         PK_CUDA(cudaMemset(B->err.ptr, 0, sizeof(int)));
-        if (B->counters.ptr) PK_CUDA(cudaMemset(B->counters.ptr, 0, B->counters.cap));
+        if (B->plan_H >= 0 && !B->ctr_zero.empty())
+            PK_CUDA(cudaMemset(B->plan.at<int>(22), 0, B->ctr_zero.size() * sizeof(int)));
         return fail(PK_ERR_TIMEOUT, "a bounded device wait timed out (error word %d)", word);
     }
     return PK_OK;

@@ -210,6 +210,10 @@ cudaError_t launch_append_table(int dtype, void* pool_k_layer, void* pool_v_laye
 cudaError_t launch_copy_blocks(void* k, void* v, const int64_t* pairs, int64_t npairs, int layers,
                                int64_t layer_bytes, int64_t block_bytes, cudaStream_t st);
 cudaError_t launch_bounded_wait_selftest(int* err, unsigned long long limit_ns, cudaStream_t st);
+// Three device-addressable host arrays (float counts multiples of 4, 16-byte aligned) into
+// device buffers, one launch.
+cudaError_t launch_h2d_gather(const float* a_src, float* a_dst, int64_t a_floats, const float* b_src, float* b_dst,
+                              int64_t b_floats, const float* c_src, float* c_dst, int64_t c_floats, cudaStream_t st);
 // src [world][rows][row_floats] -> dst [rows][world][row_floats]; row_floats % 4 == 0, both
 // pointers 16-byte aligned.
 cudaError_t launch_interleave_heads(const float* src, float* dst, int world, int64_t rows, int64_t row_floats,

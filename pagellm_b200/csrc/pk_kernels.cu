@@ -152,6 +152,39 @@ __global__ void interleave_heads_kernel(const float4* __restrict__ src, float4* 
     }
 }
 
+// ------------------------------------------------------------------ host -> device gather
+// Up to three page-locked host arrays (device-addressable: mapped pinned memory) copied into
+// device buffers by one launch: each thread moves several independent 16-byte pieces, so many
+// reads are in flight over the host link at once.
+struct H2DPart {
+    const float4* src;
+    float4* dst;
+    int64_t n;  // 16-byte pieces
+};
+
+__global__ void __launch_bounds__(256) h2d_gather_kernel(H2DPart a, H2DPart b, H2DPart c) {
+    const int64_t total = a.n + b.n + c.n;
+    constexpr int kPer = 4;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i0 < total; i0 += stride * kPer) {
+        float4 v[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int64_t i = i0 + k * stride;
+            if (i < a.n) v[k] = a.src[i];
+            else if (i < a.n + b.n) v[k] = b.src[i - a.n];
+            else if (i < total) v[k] = c.src[i - a.n - b.n];
+        }
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int64_t i = i0 + k * stride;
+            if (i < a.n) a.dst[i] = v[k];
+            else if (i < a.n + b.n) b.dst[i - a.n] = v[k];
+            else if (i < total) c.dst[i - a.n - b.n] = v[k];
+        }
+    }
+}
+
 // ------------------------------------------------------------------ generic attention
 // One CTA (4 warps) per (row, query head). Keys are dealt to warps one at a time; each
 // warp keeps a running max / sum / output (the online softmax of cache/paged.py:309-352),
@@ -511,6 +544,18 @@ cudaError_t launch_interleave_heads(const float* src, float* dst, int world, int
     const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 8);
     interleave_heads_kernel<<<static_cast<int>(blocks), threads, 0, st>>>(
         reinterpret_cast<const float4*>(src), reinterpret_cast<float4*>(dst), world, rows, s4);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_h2d_gather(const float* a_src, float* a_dst, int64_t a_floats, const float* b_src, float* b_dst,
+                              int64_t b_floats, const float* c_src, float* c_dst, int64_t c_floats, cudaStream_t st) {
+    H2DPart a{reinterpret_cast<const float4*>(a_src), reinterpret_cast<float4*>(a_dst), a_floats / 4};
+    H2DPart b{reinterpret_cast<const float4*>(b_src), reinterpret_cast<float4*>(b_dst), b_floats / 4};
+    H2DPart c{reinterpret_cast<const float4*>(c_src), reinterpret_cast<float4*>(c_dst), c_floats / 4};
+    const int64_t total = a.n + b.n + c.n;
+    if (total <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((total + 4 * 256 - 1) / (4 * 256), 148 * 4);
+    h2d_gather_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(a, b, c);
     return cudaGetLastError();
 }
 

@@ -111,6 +111,14 @@ def test_host_buffer_result_paths():
     got = b.write_and_attend(0, qh, kh, vh)
     assert b.io_stats() == {"h2d": qh.nbytes + kh.nbytes + vh.nbytes, "d2h": 0, "direct": qh.nbytes}
     np.testing.assert_array_equal(got, ref)
+    # page-locked inputs travel by the one-launch gather instead of three copies: same bits
+    qp, kp, vp = (torch.empty(t.shape, dtype=torch.float32, pin_memory=True) for t in (q, k, v))
+    qp.copy_(q)
+    kp.copy_(k)
+    vp.copy_(v)
+    got_pinned = b.write_and_attend(0, qp.numpy(), kp.numpy(), vp.numpy())
+    assert b.io_stats()["h2d"] == qh.nbytes + kh.nbytes + vh.nbytes
+    np.testing.assert_array_equal(got_pinned, ref)
     out = np.full_like(qh, np.nan)  # pageable
     st = torch.cuda.current_stream().cuda_stream
     _lib.check(_lib.load().pk_batch_write_and_attend_host(b._b, 0, w.H, qh.ctypes.data, kh.ctypes.data,
