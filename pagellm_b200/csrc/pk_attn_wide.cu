@@ -30,12 +30,12 @@
 //   warp 1  TMEM owner (alloc/dealloc, 512 columns) and, on one lane, the MMA issuer:
 //           S_t = Q_t . K^T  (M=128, N=128, K=128; bf16 -> fp32 in TMEM)
 //           O_t += P_t . V   (M=128, N=128, K=128; P_t from TMEM, V MN-major from smem)
-//   warps 2-5 / 6-9  softmax of query tile 0 / 1: thread = row. Reads S_t from TMEM in two
-//           passes of 32 columns at a time (the masked row max, then P), so no more than 32
-//           scores are in registers and nothing spills to local memory; masks by absolute
-//           position; online max/sum in the exp2 domain (the base moves only when a tile's
-//           max exceeds it by 2^8, and only then is O_t in TMEM rescaled); writes P_t (bf16)
-//           over S_t's columns, and finally O_t / l to global.
+//   warps 2-5 / 6-9  softmax of query tile 0 / 1: thread = row. Loads all 128 scores of S_t
+//           from TMEM with one wait (a few registers spill; re-reading S in 32-column passes
+//           to avoid that serialises four TMEM round trips per pass and measured slower),
+//           masks by absolute position, online max/sum in the exp2 domain (the base moves only
+//           when a tile's max exceeds it by 2^8, and only then is O_t in TMEM rescaled),
+//           writes P_t (bf16) over S_t's first 64 columns, and finally O_t / l to global.
 // Q is rounded to bf16 once (scaled by log2(e)/sqrt(d)); P to bf16; accumulation is fp32.
 // Every wait is bounded; on a timeout the CTA records the error, unwinds and frees TMEM.
 
@@ -131,12 +131,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
         "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
         : "memory");
 }
-__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* v) {
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-            taddr),
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -453,54 +455,53 @@ __global__ void __launch_bounds__(kWThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                // Two passes over S in TMEM, 32 columns at a time, so that no more than one
-                // 32-column chunk is in registers (nothing spills): (1) the row max of the masked
-                // tile; (2) P = 2^(S - base) as bf16 pairs, chunk c written to columns
-                // [16c, 16c + 16) of S, all of which were read before (chunk c reads columns
-                // [32c, 32c + 32)). Masking by absolute position only on tiles that reach past
-                // this row's limit (earlier tiles are fully visible; dead rows mask everything).
+                // all 128 scores of the row, one TMEM wait; mask by absolute position only on
+                // tiles that reach past this row's limit (earlier tiles are fully visible; dead
+                // rows mask everything)
                 const bool masked = kbase + kWKeys - 1 > qlim;
-                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-                for (int c = 0; c < kWKeys / 32; ++c) {
-                    float sv[32];
-                    tmem_ld32(tS + c * 32, sv);
-                    tmem_wait_ld();
-                    if (masked) {
+                float sv[kWKeys];
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (kbase + c * 32 + i > qlim) sv[i] = -INFINITY;
-                    }
+                for (int c = 0; c < kWKeys / 32; ++c) tmem_ld32(tS + c * 32, sv + c * 32);
+                tmem_wait_ld();
+                if (masked) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], sv[i]);
+                    for (int i = 0; i < kWKeys; ++i)
+                        if (kbase + i > qlim) sv[i] = -INFINITY;
                 }
-                const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+                // row max as 8 independent chains
+                float mx8[8];
+#pragma unroll
+                for (int kq = 0; kq < 8; ++kq) {
+                    mx8[kq] = sv[kq];
+#pragma unroll
+                    for (int i = kq + 8; i < kWKeys; i += 8) mx8[kq] = fmaxf(mx8[kq], sv[i]);
+                }
+                const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
                 // Lazy rescale: keep the exponent base of earlier tiles unless this tile's max
                 // exceeds it by more than 8 (P stays <= 2^8 in bf16, l and O in fp32), so O in
                 // TMEM is rescaled only when the base actually moves.
                 const float mnew = (m == -INFINITY || mx > m + 8.f) ? mx : m;
                 const float base = mnew == -INFINITY ? 0.f : mnew;
                 const float corr = m == -INFINITY ? 0.f : ex2_approx(m - base);
-                float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-                for (int c = 0; c < kWKeys / 32; ++c) {
-                    float sv[32];
-                    tmem_ld32(tS + c * 32, sv);
-                    tmem_wait_ld();
-                    uint32_t pk[16];
+                // P = 2^(S - base) as bf16 pairs over S's first 64 columns, 64 keys at a time
+                float sum8[8];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const bool va = !masked || kbase + c * 32 + 2 * i <= qlim;
-                        const bool vb = !masked || kbase + c * 32 + 2 * i + 1 <= qlim;
-                        const float a = va ? ex2_approx(sv[2 * i] - base) : 0.f;
-                        const float b = vb ? ex2_approx(sv[2 * i + 1] - base) : 0.f;
-                        sum4[i & 3] += a + b;
+                for (int kq = 0; kq < 8; ++kq) sum8[kq] = 0.f;
+#pragma unroll
+                for (int half = 0; half < kWKeys / 64; ++half) {
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float a = ex2_approx(sv[half * 64 + 2 * i] - base);
+                        const float b = ex2_approx(sv[half * 64 + 2 * i + 1] - base);
+                        sum8[i & 7] += a + b;
                         pk[i] = pack_bf16(a, b);
                     }
-                    tmem_st16u(tS + c * 16, pk);
+                    tmem_st32u(tS + half * 32, pk);
                 }
                 tmem_wait_st();
-                l = l * corr + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+                l = l * corr + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
                 m = mnew;
                 // O is rescaled to the new base after P is written and before P.V of this tile
                 // may start (pfull below). O already holds P.V of the previous tile: that MMA
