@@ -279,12 +279,14 @@ struct pk_batch {
     DevBuf wpart;  // partial O and (max, sum) of pair-heads cut between CTAs
     DevBuf qpk;    // packed bf16 query tiles of the wide-tile items (+1 zero tile)
     std::vector<int32_t> u_kb0;    // per unit: first block read (after a shared prefix)
+    std::vector<int32_t> u_cta;    // per unit: first and last split-KV CTA of its blocks
     std::vector<int32_t> seq_kb0;  // scratch: per sequence
     int tc_max_new = 0;            // most new tokens of a sequence on the split-KV kernel
     DevBuf lse;                    // [rows][H] when shared-prefix items exist
     Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows 8 w_seq
                     // 9 w_tok0 10 w_rows 11 w_ntok 12 w_kend 13 tok_row 14 tok_pos 15 u_kb0
-                    // 16 w_pair 17 pair_kend 18 cta_seg 19 seg 20 split
+                    // 16 w_pair 17 pair_kend 18 cta_seg 19 seg 20 split 21 cta_blk
+                    // 22 merge counters (zeros) 23 u_cta
     DevBuf ws;
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
@@ -724,7 +726,7 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         if (P->d == 256) qmax = g <= 8 ? std::max(1, 8 / g) : 0;  // one n8 tile only at D=256
     }
     B->w_seq.clear(); B->w_tok0.clear(); B->w_ntok.clear(); B->w_kend.clear();
-    B->tok_row.clear(); B->tok_pos.clear(); B->w_rows.clear(); B->u_kb0.clear();
+    B->tok_row.clear(); B->tok_pos.clear(); B->w_rows.clear(); B->u_kb0.clear(); B->u_cta.clear();
     B->nwide = B->nprefix = B->nprefix_groups = 0;
     B->prefix_keys = B->prefix_token_keys = 0;
     B->seq_kb0.assign(B->nseq, 0);
@@ -821,9 +823,12 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         const int64_t nmax = split_kv_ctas(T, B->nu, static_cast<int64_t>(P->num_sms) * per_sm);
         B->ncta = partition_blocks(B->u_blk.data(), B->nu, nmax,
                                    unit_switch_blocks(P, static_cast<int64_t>(P->num_sms) * per_sm), B->cta_blk);
+        B->u_cta.resize(2 * static_cast<size_t>(B->nu));
         for (int u = 0; u < B->nu; ++u) {
             const int c0 = cta_of_block(B->cta_blk, B->u_blk[u]);
             const int c1 = cta_of_block(B->cta_blk, B->u_blk[u + 1] - 1);
+            B->u_cta[2 * u] = c0;
+            B->u_cta[2 * u + 1] = c1;
             if (c0 != c1) {
                 B->sp_u.push_back(u);
                 B->sp_c0.push_back(c0);
@@ -867,6 +872,8 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan.add(B->cta_blk.data(), B->cta_blk.size() * 4);
     if (!B->use_tc) B->ctr_zero.clear();
     B->plan.add(B->ctr_zero.data(), B->ctr_zero.size() * 4);  // 22
+    if (!B->use_tc) B->u_cta.clear();
+    B->plan.add(B->u_cta.data(), B->u_cta.size() * 4);  // 23
     if (B->nslots > 0)
         PK_CUDA(B->wpart.reserve(static_cast<size_t>(B->nslots) * 2 * 128 * (128 + 2) * sizeof(float)));
     if (!B->w_seq.empty())
@@ -1051,6 +1058,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.total_blocks = B->total_blocks;
         p.ncta = B->ncta;
         p.cta_blk = B->plan.at<int32_t>(21);
+        p.u_cta = B->plan.at<int32_t>(23);
         p.kvh = P->kvh;
         p.g = g;
         p.H = H;

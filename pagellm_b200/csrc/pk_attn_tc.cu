@@ -445,10 +445,11 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             store_rows<D, NT>(p.out, acc, m, l, p.lse, nq, g, p.H, row0, h, quad, grp);
         } else {
             // The partial of (unit u, CTA c, head h): (max, sum) per live column at
-            // part_ml[slot][h][col], and the un-normalised O in fragment order - lane L's
-            // KS * NT * 4 accumulator values contiguous at part_o[slot][h] + L * kFrag - so a
-            // partial leaves and comes back as kFrag / 4 coalesced 16-byte accesses per lane.
-            constexpr int kFrag = KS * NT * 4;
+            // part_ml[slot][h][col], and the un-normalised O in fragment order interleaved by
+            // lane - accumulator quad j = mt * NT + nt of lane L is float4 j * 32 + L of
+            // part_o[slot][h] - so each of the KS * NT 16-byte accesses of a warp covers 512
+            // contiguous bytes, in global memory and (conflict-free) in shared memory.
+            constexpr int kFrag = KS * NT * 4;  // floats per lane
             const size_t seg = static_cast<size_t>(u) + c;
             const size_t base = (seg * p.kvh + h) * kMaxCols;
             bool lane_live = false;
@@ -465,12 +466,12 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                     }
                 }
             if (lane_live) {
-                float4* po = reinterpret_cast<float4*>(p.part_o + base * D + static_cast<size_t>(lane) * kFrag);
+                float4* po = reinterpret_cast<float4*>(p.part_o + base * D) + lane;
 #pragma unroll
                 for (int mt = 0; mt < KS; ++mt)
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt)
-                        po[mt * NT + nt] = make_float4(acc[mt][nt][0], acc[mt][nt][1], acc[mt][nt][2], acc[mt][nt][3]);
+                        po[(mt * NT + nt) * 32] = make_float4(acc[mt][nt][0], acc[mt][nt][1], acc[mt][nt][2], acc[mt][nt][3]);
             }
             if (p.counters != nullptr) {
                 // Two-level merge in fixed order. The unit's CTAs cf..cl form groups of
@@ -480,8 +481,10 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 // and the last group to finish merges the group partials. A unit spread over
                 // many CTAs (a long sequence) then costs two short merges at the end of the
                 // launch instead of one long one. Counters are left at zero for the next launch.
-                const int cf = cta_of_block(ublk0, p.total_blocks, p.ncta, p.cta_blk);
-                const int cl = cta_of_block(p.u_blk[u + 1] - 1, p.total_blocks, p.ncta, p.cta_blk);
+                // the unit's first and last CTA, from the plan (one round trip, no search)
+                const int cf = p.u_cta != nullptr ? p.u_cta[2 * u] : cta_of_block(ublk0, p.total_blocks, p.ncta, p.cta_blk);
+                const int cl = p.u_cta != nullptr ? p.u_cta[2 * u + 1]
+                                                  : cta_of_block(p.u_blk[u + 1] - 1, p.total_blocks, p.ncta, p.cta_blk);
                 const int ngr = (cl - cf + kMergeGroup) / kMergeGroup;
                 const int g0 = cf + (c - cf) / kMergeGroup * kMergeGroup;
                 const int g1 = min(cl, g0 + kMergeGroup - 1);
@@ -514,8 +517,9 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
 #pragma unroll
                             for (int i = 0; i < 4; ++i) num[mt][nt][i] = 0.f;
                 };
-                // folds one partial into (mx, den, num): ml = its (max, sum) row, fr = this
-                // lane's fragment; an online softmax merge, so the order of folds fixes the bits
+                // folds one partial into (mx, den, num): ml = its (max, sum) row, fr = the
+                // partial's O plus this lane (quad j at fr[j * 32]); an online softmax merge, so
+                // the order of folds fixes the bits
                 auto fold = [&](const float* ml, const float4* fr, bool from_global) {
                     float a[NT][2], b[NT][2];
 #pragma unroll
@@ -537,7 +541,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
 #pragma unroll
                         for (int nt = 0; nt < NT; ++nt) {
                             float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-                            if (lane_live) x = from_global ? __ldcg(fr + mt * NT + nt) : fr[mt * NT + nt];
+                            if (lane_live) x = from_global ? __ldcg(fr + (mt * NT + nt) * 32) : fr[(mt * NT + nt) * 32];
                             num[mt][nt][0] = num[mt][nt][0] * a[nt][0] + x.x * b[nt][0];
                             num[mt][nt][1] = num[mt][nt][1] * a[nt][1] + x.y * b[nt][1];
                             num[mt][nt][2] = num[mt][nt][2] * a[nt][0] + x.z * b[nt][0];
@@ -581,7 +585,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                             }
                             for (int i = 0; i < nb; ++i)
                                 fold(reinterpret_cast<const float*>(region + i * kPieceBytes + kFragBytes),
-                                     reinterpret_cast<const float4*>(region + i * kPieceBytes) + lane * (kFrag / 4), false);
+                                     reinterpret_cast<const float4*>(region + i * kPieceBytes) + lane, false);
                             __syncwarp();  // every lane is done with the batch before the next lands
                         }
                         return true;
@@ -589,7 +593,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                     auto fold_at = [&](int i) {
                         const size_t sg2 = seg_of(i);
                         fold(p.part_ml + sg2 * kMaxCols * 2,
-                             reinterpret_cast<const float4*>(p.part_o + sg2 * kMaxCols * D) + lane * (kFrag / 4), true);
+                             reinterpret_cast<const float4*>(p.part_o + sg2 * kMaxCols * D) + lane, true);
                     };
                     if constexpr (NT == 1 && D <= 128) {
 #pragma unroll 2
@@ -619,12 +623,12 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                                 }
                             }
                         if (lane_live) {
-                            float4* po = reinterpret_cast<float4*>(p.part_o + gb * D + static_cast<size_t>(lane) * kFrag);
+                            float4* po = reinterpret_cast<float4*>(p.part_o + gb * D) + lane;
 #pragma unroll
                             for (int mt = 0; mt < KS; ++mt)
 #pragma unroll
                                 for (int nt = 0; nt < NT; ++nt)
-                                    po[mt * NT + nt] =
+                                    po[(mt * NT + nt) * 32] =
                                         make_float4(num[mt][nt][0], num[mt][nt][1], num[mt][nt][2], num[mt][nt][3]);
                         }
                         if (arrive_last(p.unit_counters + static_cast<size_t>(u) * p.kvh + h, ngr) &&
@@ -638,7 +642,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
 }
 
 // One CTA per (split unit, KV head): combine the partials of every CTA that worked on it
-// (the separate-launch merge; partials in tc_attn_kernel's fragment order).
+// (the separate-launch merge; partials in tc_attn_kernel's lane-interleaved fragment order).
 __global__ void merge_kernel(const MergeParams p) {
     const int e = blockIdx.x;
     const int h = blockIdx.y;
@@ -648,7 +652,6 @@ __global__ void merge_kernel(const MergeParams p) {
     const int seq = p.u_seq[u];
     const int row0 = p.offsets[seq] + p.u_t0[u];
     const int ncols = p.u_n[u] * p.g;
-    const int frag = (p.D / 16) * p.nt * 4;  // floats per lane of one partial
     for (int col = 0; col < ncols; ++col) {
         float mmax = -INFINITY;
         for (int c = c0; c <= c1; ++c) {
@@ -662,17 +665,18 @@ __global__ void merge_kernel(const MergeParams p) {
         }
         const float inv = 1.f / den;
         float* op = p.out + (static_cast<size_t>(row0 + col / p.g) * p.H + h * p.g + col % p.g) * p.D;
-        // column col, dim d: lane quad + 4 * grp, value (mt * NT + nt) * 4 + 2 * hi + e
+        // column col, dim d: lane quad + 4 * grp, quad j = mt * NT + nt, element 2 * hi + e,
+        // at float (j * 32 + lane) * 4 + element of the partial
         const int nt = col / 8, quad = (col % 8) / 2, ce = col & 1;
         for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
             const int mt = d / 16, r = d % 16, grp = r & 7, hi = r >> 3;
             const int lane = quad + 4 * grp;
-            const int vi = (mt * p.nt + nt) * 4 + 2 * hi + ce;
+            const int vi = ((mt * p.nt + nt) * 32 + lane) * 4 + 2 * hi + ce;
             float num = 0.f;
             for (int c = c0; c <= c1; ++c) {
                 const size_t sg = (static_cast<size_t>(u) + c) * p.kvh + h;
                 const size_t idx = sg * kMaxCols + col;
-                num += exp2f(p.part_ml[idx * 2] - mmax) * p.part_o[sg * kMaxCols * p.D + lane * frag + vi];
+                num += exp2f(p.part_ml[idx * 2] - mmax) * p.part_o[sg * kMaxCols * p.D + vi];
             }
             op[d] = num * inv;
         }

@@ -22,7 +22,8 @@ struct TcParams {
     const float* q;        // [rows][H][D]
     float* out;            // [rows][H][D]
     // [segments][kvh] blocks of kMaxCols * D floats: un-normalised partial sums in fragment
-    // order (lane L's KS * NT * 4 accumulator values contiguous at L * KS * NT * 4)
+    // order interleaved by lane (accumulator quad j = mt * NT + nt of lane L is float4
+    // j * 32 + L of the block)
     float* part_o;
     float* part_ml;        // [segments][kvh][kMaxCols][2]  (running max, sum), log2 domain
     int* err;              // device error word
@@ -42,6 +43,9 @@ struct TcParams {
     float* lse;
     // [ncta + 1] first block of each CTA's range; NULL = equal ranges [c*T/ncta, (c+1)*T/ncta)
     const int32_t* cta_blk;
+    // [nu][2] first and last CTA whose range holds blocks of each unit; NULL = searched in
+    // cta_blk (read only by the in-kernel merge)
+    const int32_t* u_cta;
     int nu;
     int total_blocks;
     int ncta;
