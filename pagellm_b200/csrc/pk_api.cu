@@ -212,8 +212,7 @@ struct pk_pool {
     int tc_per_head = 0;
     int tc_stages = 0;
     size_t tc_smem = 0;
-    int tc_ctas_per_sm = 1;  // split-KV CTAs meant to share an SM (few KV heads per pool)
-    int tc_occ[3] = {0, 0, 0};  // cached CTAs per SM that fit, per NT (1, 2)
+    int tc_virt = 1;  // virtual split-KV CTAs per CTA (8 / kvh for pools of few KV heads)
     std::string tc_why;
     CUtensorMap tmk{};
     CUtensorMap tmv{};
@@ -395,7 +394,7 @@ void setup_tc(pk_pool* P) {
     P->tc_ok = false;
     auto no = [&](const char* w) { P->tc_why = w; };
     if (P->dtype != PK_BF16) return no("pool is not bf16");
-    // only these head sizes have a compiled instance (launch_tc_attention, tc_max_active_ctas)
+    // only these head sizes have a compiled instance (launch_tc_attention)
     if (P->d != 64 && P->d != 128 && P->d != 256) return no("head_dim not in {64,128,256}");
     if (P->block_size % 16 != 0 || P->block_size > 256) return no("block_size not a multiple of 16 (<=256)");
     if (P->kvh > pk::kTcMaxKvHeads) return no("more than 8 KV heads");
@@ -404,20 +403,18 @@ void setup_tc(pk_pool* P) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, P->device);
     const size_t stage = static_cast<size_t>(2) * P->block_size * P->kvh * P->d * 2;
-    // A CTA has one consumer warp per KV head. With few KV heads (the head-sharded layout
-    // gives 1-4 per GPU) one CTA per SM would leave most of the SM idle, so 8 / kvh CTAs share
-    // an SM, each with its share of shared memory; stages: as many as fit (at most 8).
-    int per_sm = 0;
-    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, P->device);
-    // Several CTAs per SM only while each still gets >= 3 stages (else fewer CTAs per SM).
+    // A CTA has one consumer warp per KV head of each of its V virtual CTAs. With few KV heads
+    // (the head-sharded layout gives 1-4 per GPU) V = 8 / kvh virtual CTAs - each its own block
+    // range, stage ring and barriers - keep 8 consumer warps per SM under one producer warp
+    // (several 2-warp CTAs per SM would spend half the register file on producers). Stages: as
+    // many as fit (at most 8); V is lowered while fewer than 3 fit.
     int stages = 0;
-    for (int k = std::max(1, pk::kTcMaxKvHeads / P->kvh); k >= 1; --k) {
-        size_t budget = std::min<size_t>(static_cast<size_t>(optin), size_t(200) << 10);
-        if (k > 1 && per_sm > 0) budget = std::min<size_t>(budget, static_cast<size_t>(per_sm) / k - 1024);
+    for (int v = std::max(1, pk::kTcMaxKvHeads / P->kvh); v >= 1; --v) {
+        const size_t budget = std::min<size_t>(static_cast<size_t>(optin), size_t(200) << 10);
         stages = 8;
-        while (stages >= 2 && pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages) > budget) --stages;
-        P->tc_ctas_per_sm = k;
-        if (stages >= 3 || k == 1) break;
+        while (stages >= 2 && pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages, v) > budget) --stages;
+        P->tc_virt = v;
+        if (stages >= 3 || v == 1) break;
     }
     (void)stage;
     if (stages < 2) return no("K/V block too large for two shared-memory stages");
@@ -431,7 +428,7 @@ void setup_tc(pk_pool* P) {
         return;
     }
     P->tc_stages = stages;
-    P->tc_smem = pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages);
+    P->tc_smem = pk::tc_smem_bytes(P->d, P->block_size, P->kvh, stages, P->tc_virt);
     P->tc_ok = true;
     P->tc_why.clear();
     // wide tiles: head_dim 128, 128-key tiles made of whole blocks, the layout-0 view
@@ -816,9 +813,8 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         B->total_blocks = static_cast<int>(T);
         // On small steps more CTAs would cut every unit into many partials whose merge
         // outweighs the bandwidth the extra SMs add.
-        int& occ = P->tc_occ[std::min(B->nt, 2)];
-        if (occ == 0) occ = pk::tc_max_active_ctas(P->d, B->nt, P->kvh, P->tc_smem);
-        const int per_sm = std::max(1, std::min(P->tc_ctas_per_sm, occ));
+        // (virtual) split-KV CTAs per SM: one CTA (its shared memory fills the SM) of tc_virt
+        const int per_sm = P->tc_virt;
         B->tc_per_sm = per_sm;
         const int64_t nmax = split_kv_ctas(T, B->nu, static_cast<int64_t>(P->num_sms) * per_sm);
         B->ncta = partition_blocks(B->u_blk.data(), B->nu, nmax,
@@ -1064,6 +1060,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.H = H;
         p.bs = P->block_size;
         p.stages = P->tc_stages;
+        p.virt = P->tc_virt;
         p.per_head_layout = P->tc_per_head;
         p.layer_slot0 = static_cast<int64_t>(layer) * P->num_blocks * P->block_size;
         p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P->d)));
@@ -1167,6 +1164,7 @@ bool pk_pool_view(const pk_pool* P, pk::PoolView* v) {
     v->tc_ok = P->tc_ok;
     v->tc_per_head = P->tc_per_head;
     v->tc_stages = P->tc_stages;
+    v->tc_virt = P->tc_virt;
     v->tc_smem = P->tc_smem;
     v->tmk = &P->tmk;
     v->tmv = &P->tmv;

@@ -112,37 +112,56 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
+    // A CTA hosts V virtual CTAs (V > 1 for pools of few KV heads): each has its own block
+    // range (partition entry blockIdx.x * V + v), stage ring, barriers and kvh consumer warps,
+    // so that an SM runs up to 8 consumer warps under one producer warp whatever kvh is.
+    const int V = p.virt > 1 ? p.virt : 1;
     const int tile_bytes = p.bs * p.kvh * D * 2;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * 2 * tile_bytes);
-    uint64_t* empty = full + p.stages;
-    // the consumers' end of work (one arrival per consumer warp), then one barrier per consumer
-    // warp for the bulk copies of its end-of-range merge
-    uint64_t* endbar = empty + p.stages;
-    uint64_t* mbar_m = endbar + 1;
+    const int ring_bytes = p.stages * 2 * tile_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + V * ring_bytes);
+    uint64_t* empty = full + V * p.stages;
+    // each virtual CTA's end of work (one arrival per consumer warp of it), then one barrier
+    // per consumer warp for the bulk copies of its end-of-range merge
+    uint64_t* endbar = empty + V * p.stages;
+    uint64_t* mbar_m = endbar + V;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int nwc = p.kvh;
+    const int nwc = p.kvh * V;  // consumer warps
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < p.stages; ++s) {
+        for (int s = 0; s < V * p.stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], nwc);
+            mbar_init(&empty[s], p.kvh);
         }
-        mbar_init(endbar, nwc);
+        for (int v = 0; v < V; ++v) mbar_init(&endbar[v], p.kvh);
         for (int w = 0; w < nwc; ++w) mbar_init(&mbar_m[w], 1);
         fence_mbar_init();
     }
     __syncthreads();
 
-    const int c = blockIdx.x;
-    const int lo = p.cta_blk ? p.cta_blk[c] : static_cast<int>(static_cast<int64_t>(c) * p.total_blocks / p.ncta);
-    const int hi = p.cta_blk ? p.cta_blk[c + 1] : static_cast<int>(static_cast<int64_t>(c + 1) * p.total_blocks / p.ncta);
+    // block range [lo, hi) of virtual CTA cv (empty past the partition)
+    auto range_of = [&](int cv, int& lo_, int& hi_) {
+        if (cv >= p.ncta) {
+            lo_ = hi_ = p.total_blocks;
+            return;
+        }
+        lo_ = p.cta_blk ? p.cta_blk[cv] : static_cast<int>(static_cast<int64_t>(cv) * p.total_blocks / p.ncta);
+        hi_ = p.cta_blk ? p.cta_blk[cv + 1] : static_cast<int>(static_cast<int64_t>(cv + 1) * p.total_blocks / p.ncta);
+    };
+    const int vme = warp < nwc ? warp / p.kvh : 0;  // this warp's virtual CTA (the producer: 0)
+    const int c = blockIdx.x * V + vme;             // its partition entry
+    int lo, hi;
+    range_of(c, lo, hi);
     const int u_first = upper_bound_i32(p.u_blk, p.nu + 1, lo) - 1;
+    uint8_t* ring = smem + vme * ring_bytes;
+    uint64_t* vfull = full + vme * p.stages;
+    uint64_t* vempty = empty + vme * p.stages;
+    uint64_t* vend = endbar + vme;
 
     if (warp == nwc) {
         // ------------------------------------------------------------ producer
-        if (lane == 0) {
+        if (lane == 0 && V == 1) {
             prefetch_tensormap(&tmk);
             prefetch_tensormap(&tmv);
             // K/V blocks are read once per launch: first out of L2, so that what is read again
@@ -161,38 +180,108 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 for (; j < uend; ++j, ++it) {
                     const int s = it % p.stages;
                     const uint32_t k = static_cast<uint32_t>(it / p.stages);
-                    if (!mbar_wait_bounded(&empty[s], (k & 1u) ^ 1u)) {
+                    if (!mbar_wait_bounded(&vempty[s], (k & 1u) ^ 1u)) {
                         atomicExch(p.err, kErrTimeout);
                         ok = false;
                         break;
                     }
                     const int phys = p.ids[tbase + j];
                     const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(phys) * p.bs);
-                    uint8_t* kd = smem + s * 2 * tile_bytes;
+                    uint8_t* kd = ring + s * 2 * tile_bytes;
                     uint8_t* vd = kd + tile_bytes;
-                    mbar_arrive_expect_tx(&full[s], 2u * tile_bytes);
+                    mbar_arrive_expect_tx(&vfull[s], 2u * tile_bytes);
                     if (!p.per_head_layout) {
-                        tma_load_4d_hint(kd, &tmk, 0, slot0, 0, 0, &full[s], evict_first);
-                        tma_load_4d_hint(vd, &tmv, 0, slot0, 0, 0, &full[s], evict_first);
+                        tma_load_4d_hint(kd, &tmk, 0, slot0, 0, 0, &vfull[s], evict_first);
+                        tma_load_4d_hint(vd, &tmv, 0, slot0, 0, 0, &vfull[s], evict_first);
                     } else {
                         const int hb = p.bs * CH * 128;
                         for (int h = 0; h < p.kvh; ++h) {
-                            tma_load_4d_hint(kd + h * hb, &tmk, 0, 0, h, slot0, &full[s], evict_first);
-                            tma_load_4d_hint(vd + h * hb, &tmv, 0, 0, h, slot0, &full[s], evict_first);
+                            tma_load_4d_hint(kd + h * hb, &tmk, 0, 0, h, slot0, &vfull[s], evict_first);
+                            tma_load_4d_hint(vd + h * hb, &tmv, 0, 0, h, slot0, &vfull[s], evict_first);
                         }
                     }
                 }
             }
             // Never leave the CTA with copies still landing in its shared memory.
             for (int t = max(0, it - p.stages); t < it; ++t) {
-                mbar_wait_bounded(&full[t % p.stages], static_cast<uint32_t>(t / p.stages) & 1u);
+                mbar_wait_bounded(&vfull[t % p.stages], static_cast<uint32_t>(t / p.stages) & 1u);
             }
+        } else if (V > 1) {
+            // Lane v feeds virtual CTA v. The lanes advance in warp-uniform rounds: each issues
+            // its next block once that stage of its ring is free (non-blocking test), and the
+            // warp gives up after kWaitLimitNs without any lane making progress.
+            const bool has = lane < V;
+            int vlo = 0, vhi = 0;
+            if (has) range_of(blockIdx.x * V + lane, vlo, vhi);
+            uint8_t* vr = smem + (has ? lane : 0) * ring_bytes;
+            uint64_t* pf = full + (has ? lane : 0) * p.stages;
+            uint64_t* pe = empty + (has ? lane : 0) * p.stages;
+            if (lane == 0) {
+                prefetch_tensormap(&tmk);
+                prefetch_tensormap(&tmv);
+            }
+            const uint64_t evict_first = l2_policy_evict_first();
+            int j = vlo, it = 0, uend = 0, tbase = 0;
+            int u = has ? upper_bound_i32(p.u_blk, p.nu + 1, vlo) - 1 : 0;
+            bool active = has && j < vhi, fresh = true;
+            unsigned long long t_last = global_ns();
+            while (__any_sync(0xffffffffu, active)) {
+                bool issued = false;
+                if (active) {
+                    if (fresh) {
+                        uend = min(vhi, p.u_blk[u + 1]);
+                        const int seq = p.u_seq[u];
+                        const int kb0 = p.u_kb0 != nullptr ? p.u_kb0[u] : 0;
+                        tbase = p.indptr[seq] + kb0 - p.u_blk[u];
+                        prefetch_l2_bulk(p.q + static_cast<size_t>(p.offsets[seq] + p.u_t0[u]) * p.H * D,
+                                         static_cast<uint32_t>(p.u_n[u]) * p.H * D * 4u);
+                        fresh = false;
+                    }
+                    const int s = it % p.stages;
+                    const uint32_t k = static_cast<uint32_t>(it / p.stages);
+                    if (mbar_test_wait(&pe[s], (k & 1u) ^ 1u)) {
+                        const int phys = p.ids[tbase + j];
+                        const int slot0 = static_cast<int>(p.layer_slot0 + static_cast<int64_t>(phys) * p.bs);
+                        uint8_t* kd = vr + s * 2 * tile_bytes;
+                        uint8_t* vd = kd + tile_bytes;
+                        mbar_arrive_expect_tx(&pf[s], 2u * tile_bytes);
+                        if (!p.per_head_layout) {
+                            tma_load_4d_hint(kd, &tmk, 0, slot0, 0, 0, &pf[s], evict_first);
+                            tma_load_4d_hint(vd, &tmv, 0, slot0, 0, 0, &pf[s], evict_first);
+                        } else {
+                            const int hb = p.bs * CH * 128;
+                            for (int h = 0; h < p.kvh; ++h) {
+                                tma_load_4d_hint(kd + h * hb, &tmk, 0, 0, h, slot0, &pf[s], evict_first);
+                                tma_load_4d_hint(vd + h * hb, &tmv, 0, 0, h, slot0, &pf[s], evict_first);
+                            }
+                        }
+                        ++j;
+                        ++it;
+                        issued = true;
+                        if (j >= uend) {
+                            ++u;
+                            fresh = true;
+                        }
+                        active = j < vhi;
+                    }
+                }
+                if (__any_sync(0xffffffffu, issued)) {
+                    t_last = global_ns();
+                } else if (global_ns() - t_last > kWaitLimitNs) {
+                    if (lane == 0) atomicExch(p.err, kErrTimeout);
+                    break;
+                }
+            }
+            // Never leave the CTA with copies still landing in its shared memory.
+            if (has)
+                for (int t = max(0, it - p.stages); t < it; ++t)
+                    mbar_wait_bounded(&pf[t % p.stages], static_cast<uint32_t>(t / p.stages) & 1u);
         }
         return;
     }
 
     // ---------------------------------------------------------------- consumers
-    const int h = warp;
+    const int h = warp - vme * p.kvh;  // KV head within virtual CTA vme
     const int g = p.g;
     const int quad = lane & 3;   // column pair within an n8 tile
     const int grp = lane >> 2;   // row within an 8-row group
@@ -262,23 +351,23 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             const int s = it % p.stages;
             // Every lane waits; the verdict is made warp-uniform (and the warp reconverged)
             // before the .sync.aligned matrix instructions below.
-            const bool got = mbar_wait_bounded(&full[s], static_cast<uint32_t>(it / p.stages) & 1u);
+            const bool got = mbar_wait_bounded(&vfull[s], static_cast<uint32_t>(it / p.stages) & 1u);
             if (!__all_sync(0xffffffffu, got)) {
                 if (lane == 0) {
                     atomicExch(p.err, kErrTimeout);
-                    mbar_arrive(endbar);  // the other warps' end-of-work wait does not hang on this one
+                    mbar_arrive(vend);  // the other warps' end-of-work wait does not hang on this one
                 }
                 alive = false;
                 break;
             }
-            const uint32_t kst = smem_u32(smem + s * 2 * tile_bytes);
+            const uint32_t kst = smem_u32(ring + s * 2 * tile_bytes);
             const uint32_t vst = kst + tile_bytes;
             const int kpos0 = (j - ublk0 + kb0) * p.bs;
             const int nvalid = min(p.bs, uctx - kpos0);
             if (nvalid < p.bs) {
                 // Slots past the context may hold anything; zero this head's V rows there so
                 // that 0 * V stays 0 in the P.V product.
-                uint8_t* vgen = smem + s * 2 * tile_bytes + tile_bytes;
+                uint8_t* vgen = ring + s * 2 * tile_bytes + tile_bytes;
                 const int units = (p.bs - nvalid) * CH * 8;
                 for (int x = lane; x < units; x += 32) {
                     const int t = nvalid + x / (CH * 8);
@@ -300,7 +389,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 const int hi_pos = min(kpos0 + p.bs, uctx);
                 if (lo_pos < hi_pos) {
                     patched = true;
-                    uint8_t* kgen = smem + s * 2 * tile_bytes;
+                    uint8_t* kgen = ring + s * 2 * tile_bytes;
                     uint8_t* vgen = kgen + tile_bytes;
                     const int phys = p.ids[p.indptr[seq] + kb0 + (j - ublk0)];
                     const int row_base = p.offsets[seq] - s_start;
@@ -417,7 +506,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             // Generic-proxy writes into the stage must be ordered before the next TMA fill.
             if (nvalid < p.bs || patched) fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+            if (lane == 0) mbar_arrive(&vempty[s]);
         }
         if (!alive) break;
 
@@ -432,13 +521,13 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 t += __shfl_xor_sync(0xffffffffu, t, 16);
                 l[nt][e] = t;
             }
-        // The last unit of the range: once every consumer warp of the CTA is here, no stage is
-        // read or filled any more, and the warps may use the stage ring to stage a merge.
+        // The last unit of the range: once every consumer warp of the (virtual) CTA is here, no
+        // stage of its ring is read or filled any more, and its warps may stage a merge there.
         bool at_end = false;
         if (p.u_blk[u + 1] >= hi) {
             __syncwarp();
-            if (lane == 0) mbar_arrive(endbar);
-            at_end = __all_sync(0xffffffffu, mbar_wait_bounded(endbar, 0u));
+            if (lane == 0) mbar_arrive(vend);
+            at_end = __all_sync(0xffffffffu, mbar_wait_bounded(vend, 0u));
         }
         const bool whole = ublk0 >= lo && p.u_blk[u + 1] <= hi;
         if (whole) {
@@ -556,15 +645,15 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 constexpr uint32_t kFragBytes = 32u * kFrag * 4u;  // all lanes' fragments
                 constexpr uint32_t kMlBytes = kMaxCols * 2u * 4u;  // (max, sum) of every column
                 constexpr uint32_t kPieceBytes = kFragBytes + kMlBytes;
-                const uint32_t region_bytes = (static_cast<uint32_t>(p.stages) * 2u * tile_bytes / nwc) & ~127u;
+                const uint32_t region_bytes = (static_cast<uint32_t>(p.stages) * 2u * tile_bytes / p.kvh) & ~127u;
                 const int per_batch = static_cast<int>(region_bytes / kPieceBytes);
                 int batches = 0;  // this warp's merge barrier phases used so far
                 auto merge = [&](int first, int count, int stride) {
                     reset();
                     auto seg_of = [&](int i) { return (static_cast<size_t>(u) + first + i * stride) * p.kvh + h; };
                     if (at_end && per_batch >= 2) {
-                        uint8_t* region = smem + static_cast<size_t>(h) * region_bytes;
-                        uint64_t* mb = &mbar_m[h];
+                        uint8_t* region = ring + static_cast<size_t>(h) * region_bytes;
+                        uint64_t* mb = &mbar_m[warp];
                         if (lane == 0) fence_proxy_async_global();
                         for (int i0 = 0; i0 < count; i0 += per_batch) {
                             const int nb = min(per_batch, count - i0);
@@ -690,37 +779,20 @@ cudaError_t launch_tc_t(const CUtensorMap* tmk, const CUtensorMap* tmv, const Tc
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    kern<<<p.ncta, (p.kvh + 1) * 32, smem, st>>>(*tmk, *tmv, p);
+    const int V = p.virt > 1 ? p.virt : 1;
+    kern<<<(p.ncta + V - 1) / V, (p.kvh * V + 1) * 32, smem, st>>>(*tmk, *tmv, p);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-template <int D, int NT>
-int max_active_t(int kvh, size_t smem) {
-    int n = 0;
-    if (cudaFuncSetAttribute(tc_attn_kernel<D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-        return 1;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, tc_attn_kernel<D, NT>, (kvh + 1) * 32, smem) != cudaSuccess)
-        return 1;
-    return n;
-}
-
-int tc_max_active_ctas(int D, int NT, int kvh, size_t smem) {
-    if (D == 64 && NT == 1) return max_active_t<64, 1>(kvh, smem);
-    if (D == 64 && NT == 2) return max_active_t<64, 2>(kvh, smem);
-    if (D == 128 && NT == 1) return max_active_t<128, 1>(kvh, smem);
-    if (D == 128 && NT == 2) return max_active_t<128, 2>(kvh, smem);
-    if (D == 256 && NT == 1) return max_active_t<256, 1>(kvh, smem);
-    return 1;
-}
-
-size_t tc_smem_bytes(int D, int bs, int kvh, int stages) {
-    // stages of K + V blocks, a full and an empty barrier per stage, the end-of-work barrier and
-    // one merge barrier per consumer warp, and the slack that aligns the base to 1024 bytes
-    return static_cast<size_t>(stages) * 2 * bs * kvh * D * 2 + 2 * stages * sizeof(uint64_t) +
-           (1 + kTcMaxKvHeads) * sizeof(uint64_t) + 1024;
+size_t tc_smem_bytes(int D, int bs, int kvh, int stages, int virt) {
+    // per virtual CTA: stages of K + V blocks, a full and an empty barrier per stage and the
+    // end-of-work barrier; one merge barrier per consumer warp; the slack that aligns the base
+    // to 1024 bytes
+    return static_cast<size_t>(virt) * (static_cast<size_t>(stages) * 2 * bs * kvh * D * 2 +
+                                         (2 * stages + 1) * sizeof(uint64_t)) +
+           kTcMaxKvHeads * sizeof(uint64_t) + 1024;
 }
 
 cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUtensorMap* tmv,

@@ -54,6 +54,7 @@ struct TcParams {
     int H;
     int bs;
     int stages;
+    int virt;              // virtual CTAs per CTA (0 or 1: one); kvh * virt <= kTcMaxKvHeads
     int per_head_layout;   // 0: one TMA box per K/V block, 1: one box per (block, head)
     int64_t layer_slot0;   // first slot of the layer in the flat [layers*num_blocks*bs] axis
     float qscale;          // log2(e) / sqrt(D)
@@ -162,6 +163,7 @@ struct PoolView {
     bool tc_ok;
     int tc_per_head;
     int tc_stages;
+    int tc_virt;
     size_t tc_smem;
     const CUtensorMap* tmk;
     const CUtensorMap* tmv;
@@ -169,9 +171,7 @@ struct PoolView {
 
 cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUtensorMap* tmv,
                                 const TcParams& p, size_t smem, cudaStream_t st);
-size_t tc_smem_bytes(int D, int bs, int kvh, int stages);
-// How many split-KV CTAs of this shape fit on one SM (registers, shared memory, threads).
-int tc_max_active_ctas(int D, int NT, int kvh, size_t smem);
+size_t tc_smem_bytes(int D, int bs, int kvh, int stages, int virt);
 cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st);
 size_t wide_smem_bytes();
 cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tmv1, const WideParams& p,

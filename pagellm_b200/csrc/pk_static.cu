@@ -134,7 +134,8 @@ extern "C" PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, in
     }
     indptr[nseq] = static_cast<int32_t>(n_ids);
     if (T >= (int64_t(1) << 31)) return sfail(PK_ERR_UNSUPPORTED, "too many blocks");
-    const int ncta = static_cast<int>(T < P.num_sms ? T : P.num_sms);
+    const int64_t nv = static_cast<int64_t>(P.num_sms) * (P.tc_virt > 1 ? P.tc_virt : 1);  // (virtual) CTAs
+    const int ncta = static_cast<int>(T < nv ? T : nv);
     int nsplit = 0;
     for (int u = 0; u < nseq; ++u) {
         const int c0 = cta_of(ublk[u], T, ncta), c1 = cta_of(ublk[u + 1] - 1, T, ncta);
@@ -225,6 +226,7 @@ extern "C" PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, in
     p.H = n_heads;
     p.bs = bs;
     p.stages = P.tc_stages;
+    p.virt = P.tc_virt;
     p.per_head_layout = P.tc_per_head;
     p.layer_slot0 = static_cast<int64_t>(layer) * P.num_blocks * bs;
     p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(P.d)));
