@@ -380,31 +380,35 @@ def measure_c5(ctx: Ctx, layout: str, steps: int, warmup: int) -> dict:
         w = workloads.c5(0, lengths=L[shard_sequences(L, ctx.world)[ctx.rank]])
     job = Job(ctx, w, seed=ctx.rank)
     sharded = layout == "head" and ctx.world > 1
-    # head-sharded exchange: one push launch over peer memory (the product path); the NCCL
-    # all-gather + interleave kernel is timed beside it for comparison
+    # head-sharded exchange fused into the attention launch over peer memory (the product
+    # path); attention + a separate push launch, and attention + the NCCL all-gather and
+    # interleave kernel, are timed beside it for comparison
     gather = PeerHeadGather() if sharded else None
     nccl = HeadGather() if sharded else None
     full = {}
 
     def step():
-        job.attend_layer()
         if gather is not None:
-            full["out"] = gather(job.out)
+            full["out"] = gather.write_and_attend(job.batch, 0, job.q, job.k, job.v)
+        else:
+            job.attend_layer()
 
     ms = ctx.timed(step, steps, warmup)
     us = ms / steps * 1e3
     if sharded:
         gather.check()
+        fused_out = full["out"].clone()
         job.attend_layer()
-        same = bool(torch.equal(gather(job.out), nccl(job.out)))
+        same = bool(torch.equal(gather(job.out), nccl(job.out))) and bool(torch.equal(fused_out, gather(job.out)))
+        ms_push = ctx.timed(lambda: (job.attend_layer(), gather(job.out)), steps, warmup)
         ms_nccl = ctx.timed(lambda: (job.attend_layer(), nccl(job.out)), steps, warmup)
     prof_ms, prof_n = job.profile(job.attend_layer, steps)
     ctx.barrier()
     kernel_us = ctx.max_over_ranks(prof_ms[1] / max(1, prof_n[1]) * 1e3)
     res = {
-        "layout": ("head-sharded: 8/N KV heads of every sequence per GPU; every step each GPU's "
-                   "[128, 64/N, 128] fp32 output slice is pushed into every GPU's [128, 64, 128] result "
-                   "over peer memory (one launch, epoch flag barrier)")
+        "layout": ("head-sharded: 8/N KV heads of every sequence per GPU; the attention kernel stores "
+                   "every [64/N, 128] output row into every GPU's [128, 64, 128] result over peer memory "
+                   "and exchanges epoch flags at its end (one launch per step)")
         if layout == "head" else "sequence-sharded: whole sequences per GPU (longest first), no collective",
         "steps": steps,
         "us_per_step": round(us, 2),
@@ -414,10 +418,11 @@ def measure_c5(ctx: Ctx, layout: str, steps: int, warmup: int) -> dict:
     if sharded:
         gms = ctx.timed(lambda: gather(job.out), steps, 3)
         nms = ctx.timed(lambda: nccl(job.out), steps, 3)
-        res["gather_us"] = round(gms / steps * 1e3, 2)
+        res["separate_push_path"] = {"us_per_step": round(ms_push / steps * 1e3, 2),
+                                     "push_us": round(gms / steps * 1e3, 2)}
         res["nccl_allgather_path"] = {"us_per_step": round(ms_nccl / steps * 1e3, 2),
                                       "gather_us": round(nms / steps * 1e3, 2),
-                                      "result_equal_to_peer_path": same}
+                                      "result_equal_to_fused_path": same}
         gather.close()
     kv = ctx.sum_over_ranks(float(w.kv_read_bytes()))
     hbm, src = peaks()
@@ -429,7 +434,7 @@ def measure_c5(ctx: Ctx, layout: str, steps: int, warmup: int) -> dict:
         "peak_source": src,
         "context_tokens_per_gpu_max": int(ctx.max_over_ranks(float(w.ctx_lens.sum()))),
         "context_tokens_all_gpus": int(L.sum()),
-        "launches_per_step": job.launches_per_step() + (1 if gather is not None else 0),
+        "launches_per_step": job.launches_per_step(),
     })
     assert torch.isfinite(job.out).all()
     job.close()

@@ -209,6 +209,18 @@ PK_API int pk_peer_gather_heads(pk_peer_gather* gather, const float* slice_dev, 
                                 float** result_dev, void* stream);
 PK_API int pk_peer_gather_check(pk_peer_gather* gather, void* stream);
 PK_API int pk_peer_gather_destroy(pk_peer_gather* gather);
+/* The head-sharded step with the exchange fused into the attention: this rank's
+ * pk_batch_write_and_attend (PagedBatch.write_and_attend, cache/paged.py:441-464, over the
+ * rank's n_heads = H/world query heads) whose kernel stores every output row straight into
+ * every rank's result buffer at head offset rank * n_heads and, once all its rows are stored,
+ * exchanges the step's completion flags with the other ranks - one launch per step instead of
+ * attention + pk_peer_gather_heads. A step the split-KV kernel does not compute alone (chunks,
+ * shared prefixes, fp32 pools) computes the slice into batch scratch and then exchanges it with
+ * pk_peer_gather_heads. *result_dev, the timeout report and the calling rules are those of
+ * pk_peer_gather_heads; at most 8 ranks. */
+PK_API int pk_peer_gather_write_and_attend(pk_peer_gather* gather, pk_batch* batch, int layer, int n_heads,
+                                           const float* q_dev, const float* k_dev, const float* v_dev,
+                                           float** result_dev, void* stream);
 
 /* Decode attention that allocates nothing. No counterpart in the reference: pagellm has no
  * device memory at all. For callers that cannot call cudaMalloc - a serving framework that

@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple] = {
     "pk_peer_gather_handle": (_i32, [_p, C.c_char_p]),
     "pk_peer_gather_open": (_i32, [_p, C.c_char_p]),
     "pk_peer_gather_heads": (_i32, [_p, _p, _i64, _i64, C.POINTER(_p), _p]),
+    "pk_peer_gather_write_and_attend": (_i32, [_p, _p, _i32, _i32, _p, _p, _p, C.POINTER(_p), _p]),
     "pk_peer_gather_check": (_i32, [_p, _p]),
     "pk_peer_gather_destroy": (_i32, [_p]),
     "pk_decode_attend_static": (_i32, [_p, _i32, _i32, _i32, _pi64, _pi32, _pi64, _p, _p, _p, _p]),

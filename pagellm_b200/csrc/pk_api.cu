@@ -289,6 +289,10 @@ struct pk_batch {
     DevBuf ws;
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
+    // Head-sharded exchange fused into the split-KV launch of the current call (n == 0: off),
+    // and the slice the exchange sends when the step cannot fuse it
+    pk::PeerOut peer_out{};
+    DevBuf peer_slice;
     int launches = 0;
     // bytes the last pk_batch_write_and_attend_host moved: host to device, device to host
     // by a copy after the kernels, stored by the kernels straight into the caller's
@@ -1070,6 +1074,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.v_new = v_new;
         p.pool_k = reinterpret_cast<__nv_bfloat16*>(P->k_layer(layer));
         p.pool_v = reinterpret_cast<__nv_bfloat16*>(P->v_layer(layer));
+        p.peer = B->peer_out;
         PK_CUDA(prof_begin(B, st));
         PK_CUDA(pk::launch_tc_attention(P->d, B->nt, &P->tmk, &P->tmv, p, P->tc_smem, st));
         PK_CUDA(prof_end(B, kProfTc, st));
@@ -1566,6 +1571,47 @@ int pk_batch_write_and_attend(pk_batch* B, int layer, int n_heads, const float* 
         B->launches++;
     }
     return attend_impl(B, layer, n_heads, q_dev, out_dev, st);
+}
+
+int pk_peer_gather_write_and_attend(pk_peer_gather* g, pk_batch* B, int layer, int n_heads,
+                                    const float* q_dev, const float* k_dev, const float* v_dev,
+                                    float** result_dev, void* stream) {
+    if (!g || !B || !result_dev) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    int rc = check_heads(B, n_heads);
+    if (rc != PK_OK) return rc;
+    pk_pool* P = B->pool;
+    if (layer < 0 || layer >= P->n_layers) return fail(PK_ERR_OUT_OF_RANGE, "layer %d", layer);
+    if (B->nrows > 0 && (!q_dev || !k_dev || !v_dev)) return fail(PK_ERR_INVALID_ARG, "NULL pointer");
+    if ((rc = check_aligned(q_dev, "q")) || (rc = check_aligned(k_dev, "k")) || (rc = check_aligned(v_dev, "v")))
+        return rc;
+    DeviceScope ds(P->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (B->plan_H != n_heads) {
+        rc = build_attention_plan(B, n_heads, st);
+        if (rc != PK_OK) return rc;
+    }
+    const int64_t row_floats = static_cast<int64_t>(n_heads) * P->d;
+    // One split-KV launch writes every output row of such a step: the exchange rides on it.
+    if (B->nrows > 0 && B->use_tc && B->nwide == 0 && B->nprefix == 0 && B->ngeneric == 0) {
+        float* res = nullptr;
+        rc = pk_peer_gather_step(g, B->nrows, row_floats, P->d, &B->peer_out, &res);
+        if (rc != PK_OK) return rc;
+        rc = pk_batch_write_and_attend(B, layer, n_heads, q_dev, k_dev, v_dev, res, stream);
+        B->peer_out = pk::PeerOut{};
+        if (rc != PK_OK) return rc;
+        *result_dev = res;
+        return PK_OK;
+    }
+    // Otherwise the attention writes this rank's slice, and one push launch exchanges it.
+    const float* slice = nullptr;
+    if (B->nrows > 0) {
+        PK_CUDA(B->peer_slice.reserve(static_cast<size_t>(B->nrows) * row_floats * sizeof(float)));
+        rc = pk_batch_write_and_attend(B, layer, n_heads, q_dev, k_dev, v_dev, static_cast<float*>(B->peer_slice.ptr),
+                                       stream);
+        if (rc != PK_OK) return rc;
+        slice = static_cast<const float*>(B->peer_slice.ptr);
+    }
+    return pk_peer_gather_heads(g, slice, B->nrows, row_floats, result_dev, stream);
 }
 
 int pk_batch_write_and_attend_host(pk_batch* B, int layer, int n_heads, const float* q_host,

@@ -62,12 +62,13 @@ __device__ __forceinline__ int cta_of_block(int j, int T, int n, const int32_t* 
 
 // Normalised output of the columns a lane holds (C-fragment layout of O^T: dims
 // mt*16 + grp (+8), columns nt*8 + 2*quad + e) for the live query tokens of a unit.
-// With `lse` set, also the row's log2-domain log-sum-exp m + log2(l) ([rows][H]).
+// With `lse` set, also the row's log2-domain log-sum-exp m + log2(l) ([rows][H]). With the
+// fused head exchange on (po.n > 0) every row goes to each rank's result buffer instead.
 template <int D, int NT>
 __device__ __forceinline__ void store_rows(float* out, const float (&acc)[D / 16][NT][4],
                                            const float (&m)[NT][2], const float (&l)[NT][2],
                                            float* lse, int nq, int g, int H, int row0, int h,
-                                           int quad, int grp) {
+                                           int quad, int grp, const PeerOut& po) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -76,13 +77,25 @@ __device__ __forceinline__ void store_rows(float* out, const float (&acc)[D / 16
             const int tq = col / g;
             if (tq >= nq) continue;
             const float inv = 1.f / l[nt][e];
-            const size_t orow = static_cast<size_t>(row0 + tq) * H + h * g + col % g;
-            if (lse != nullptr && grp == 0) lse[orow] = m[nt][e] + log2f(l[nt][e]);
-            float* op = out + orow * D;
+            if (po.n == 0) {
+                const size_t orow = static_cast<size_t>(row0 + tq) * H + h * g + col % g;
+                if (lse != nullptr && grp == 0) lse[orow] = m[nt][e] + log2f(l[nt][e]);
+                float* op = out + orow * D;
 #pragma unroll
-            for (int mt = 0; mt < D / 16; ++mt) {
-                op[mt * 16 + grp] = acc[mt][nt][e] * inv;
-                op[mt * 16 + grp + 8] = acc[mt][nt][2 + e] * inv;
+                for (int mt = 0; mt < D / 16; ++mt) {
+                    op[mt * 16 + grp] = acc[mt][nt][e] * inv;
+                    op[mt * 16 + grp + 8] = acc[mt][nt][2 + e] * inv;
+                }
+            } else {
+                const size_t orow = static_cast<size_t>(row0 + tq) * po.out_H + h * g + col % g;
+                for (int r = 0; r < po.n; ++r) {
+                    float* op = po.out[r] + orow * D;
+#pragma unroll
+                    for (int mt = 0; mt < D / 16; ++mt) {
+                        op[mt * 16 + grp] = acc[mt][nt][e] * inv;
+                        op[mt * 16 + grp + 8] = acc[mt][nt][2 + e] * inv;
+                    }
+                }
             }
         }
 }
@@ -106,7 +119,7 @@ constexpr int kMergeGroup = 6;
 template <int D, int NT>
 __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
     tc_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                   const TcParams p) {
+                   const __grid_constant__ TcParams p) {
     constexpr int KS = D / 16;  // k-steps over the head dim / m-tiles of O^T
     constexpr int CH = TileGeom<D>::kChunks;
     extern __shared__ uint8_t smem_raw[];
@@ -531,7 +544,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
         }
         const bool whole = ublk0 >= lo && p.u_blk[u + 1] <= hi;
         if (whole) {
-            store_rows<D, NT>(p.out, acc, m, l, p.lse, nq, g, p.H, row0, h, quad, grp);
+            store_rows<D, NT>(p.out, acc, m, l, p.lse, nq, g, p.H, row0, h, quad, grp, p.peer);
         } else {
             // The partial of (unit u, CTA c, head h): (max, sum) per live column at
             // part_ml[slot][h][col], and the un-normalised O in fragment order interleaved by
@@ -696,7 +709,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 if (arrive_last(p.counters + (static_cast<size_t>(u) + g0) * p.kvh + h, g1 - g0 + 1) &&
                     merge(g0, g1 - g0 + 1, 1)) {
                     if (ngr == 1) {
-                        store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp);
+                        store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp, p.peer);
                     } else {
                         // the group's partial, in the slot of its first CTA (whose partial the
                         // merge has consumed)
@@ -722,8 +735,39 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                         }
                         if (arrive_last(p.unit_counters + static_cast<size_t>(u) * p.kvh + h, ngr) &&
                             merge(cf, ngr, kMergeGroup))
-                            store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp);
+                            store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp, p.peer);
                     }
+                }
+            }
+        }
+    }
+    if (p.peer.n > 0) {
+        // Fused head exchange: every consumer warp (with work or not, timed out or not) counts
+        // itself done after a system-scope fence over its rows' stores; the last of the launch
+        // publishes the step's epoch to every rank, one lane per rank, and waits until every
+        // rank's epoch has arrived here (one lane per sender), for at most kWaitLimitNs.
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_system();
+            last = atomicAdd(p.peer.done, 1u) == gridDim.x * static_cast<unsigned int>(nwc) - 1u;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            if (lane == 0) {
+                *p.peer.done = 0;
+                __threadfence_system();
+            }
+            __syncwarp();
+            if (lane < p.peer.n) st_release_sys(p.peer.flag_of[lane] + p.peer.rank, p.peer.epoch);
+            const unsigned long long t0 = global_ns();
+            for (;;) {
+                const bool arrived =
+                    lane >= p.peer.n || static_cast<int>(ld_acquire_sys(p.peer.flags + lane) - p.peer.epoch) >= 0;
+                if (__all_sync(0xffffffffu, arrived)) break;
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    if (lane == 0) atomicExch(p.peer.err, kErrTimeout);
+                    break;
                 }
             }
         }

@@ -15,6 +15,25 @@ constexpr int kTcMaxKvHeads = 8;
 constexpr int kWideKeys = 128;  // keys per tile of the wide-tile kernel (a multiple of block_size)
 
 // Parameters of the split-KV tensor-core attention kernel (bf16 pool).
+// Head-sharded output exchange fused into the split-KV kernel (n > 0): every output row goes
+// to out[0..n) - each rank's result buffer, already offset to this rank's first query head,
+// rows out_H heads apart - and when every consumer warp of the launch has stored its rows
+// (a system-scope fence, then a count in `done`), the last one writes `epoch` into flag word
+// `rank` of every rank (flag_of) and waits, for at most the wait limit, until every rank's
+// flag word here (flags) holds it; a timeout sets *err.
+constexpr int kMaxOutPeers = 8;
+struct PeerOut {
+    int n;
+    int out_H;
+    int rank;
+    unsigned int epoch;
+    float* out[kMaxOutPeers];
+    unsigned int* flag_of[kMaxOutPeers];
+    unsigned int* flags;
+    unsigned int* done;  // zero between launches; the last warp resets it
+    int* err;
+};
+
 // A "unit" is a window of at most kMaxCols / g query tokens of one sequence; every unit
 // reads the blocks holding positions 0 .. unit_ctx-1 of its sequence. Units' blocks are
 // laid end to end and cut into ncta equal ranges, one per CTA.
@@ -69,6 +88,7 @@ struct TcParams {
     const float* v_new;
     __nv_bfloat16* pool_k;
     __nv_bfloat16* pool_v;
+    PeerOut peer;  // n == 0: rows go to `out` (H heads per row)
 };
 
 struct MergeParams {
@@ -230,5 +250,11 @@ cudaError_t launch_slot_mapping(const int32_t* table, int64_t table_len, const i
 struct pk_pool;
 // Fills *out from `pool`; false if pool is NULL.
 bool pk_pool_view(const pk_pool* pool, pk::PoolView* out);
+struct pk_peer_gather;
+// The exchange of the next step of `g` for slices of [rows][row_floats] floats (row_floats =
+// heads x d of one rank): bumps the step epoch and fills *po (d: floats per head); *result is
+// this rank's [rows][world * row_floats] result buffer of that step. PK_OK or an error code.
+int pk_peer_gather_step(pk_peer_gather* g, int64_t rows, int64_t row_floats, int d, pk::PeerOut* po,
+                        float** result);
 // Sets the message pk_last_error() returns on this thread.
 void pk_set_last_error(const char* msg);

@@ -7,9 +7,10 @@
 // step s) and a flag word per sender. One launch per step:
 //   * every thread stores 16-byte pieces of this rank's slice into every rank's current result
 //     buffer, at this rank's head offset (plain peer stores, no multicast);
-//   * each CTA fences at system scope and counts itself done; the last CTA writes the step's
-//     epoch into this rank's flag word in every rank's allocation (release, system scope), then
-//     waits until every rank's flag word here holds the epoch (acquire), for at most 1 s of
+//   * each CTA fences at system scope and counts itself done; the last CTA fences once more
+//     and writes the step's epoch into this rank's flag word in every rank's allocation
+//     (release, system scope, one lane per destination), then waits until every rank's flag
+//     word here holds the epoch (acquire, one lane per sender), for at most 1 s of
 //     %globaltimer - after that it records a timeout in the error word and returns.
 // When the launch completes, the local result buffer holds every rank's slice.
 
@@ -40,15 +41,6 @@ struct PeerParams {
     unsigned int epoch;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __global__ void __launch_bounds__(256) peer_push_kernel(const PeerParams p) {
     const int64_t total = p.rows * p.s4;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -57,24 +49,44 @@ __global__ void __launch_bounds__(256) peer_push_kernel(const PeerParams p) {
         const int64_t c = i - row * p.s4;
         const float4 v = p.src[i];
         const int64_t o = (row * p.world + p.rank) * p.s4 + c;
-        for (int r = 0; r < p.world; ++r) p.dst[r][o] = v;
+        // every rank starts with a different destination, so the senders spread over the
+        // switch ports instead of all storing into the same peer first
+        for (int k = 0; k < p.world; ++k) {
+            int r = p.rank + k;
+            if (r >= p.world) r -= p.world;
+            p.dst[r][o] = v;
+        }
+    }
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();  // this CTA's stores before its count
+        last = atomicAdd(p.done, 1u) == gridDim.x - 1;
     }
     __syncthreads();
-    if (threadIdx.x != 0) return;
-    __threadfence_system();  // this CTA's stores before its count
-    if (atomicAdd(p.done, 1u) != gridDim.x - 1) return;
-    // the last CTA: every CTA's stores are ordered before its count, so before these flags
-    *p.done = 0;
-    __threadfence_system();
-    for (int r = 0; r < p.world; ++r) st_release_sys(p.flag_of[r] + p.rank, p.epoch);
+    if (!last || threadIdx.x >= 32) return;
+    // The last CTA's first warp. Every CTA's stores are ordered before its count, so before
+    // the flags: one system-scope fence, then one release store per destination, each on its
+    // own lane (one instruction, not a fence per flag).
+    const int lane = threadIdx.x;
+    if (lane == 0) {
+        *p.done = 0;
+        __threadfence_system();
+    }
+    __syncwarp();
+    for (int r = lane; r < p.world; r += 32) pk::st_release_sys(p.flag_of[r] + p.rank, p.epoch);
+    // Lane r watches sender r's flag word here; the warp leaves once all have the epoch, or
+    // records a timeout after kWaitLimitNs.
     const unsigned long long t0 = pk::global_ns();
-    for (int r = 0; r < p.world; ++r) {
-        while (static_cast<int>(ld_acquire_sys(p.flags + r) - p.epoch) < 0) {
+    for (int r0 = 0; r0 < p.world; r0 += 32) {
+        const int r = r0 + lane;
+        for (;;) {
+            const bool arrived = r >= p.world || static_cast<int>(pk::ld_acquire_sys(p.flags + r) - p.epoch) >= 0;
+            if (__all_sync(0xffffffffu, arrived)) break;
             if (pk::global_ns() - t0 > pk::kWaitLimitNs) {
-                atomicExch(p.err, pk::kErrTimeout);
+                if (lane == 0) atomicExch(p.err, pk::kErrTimeout);
                 return;
             }
-            __nanosleep(200);
         }
     }
 }
@@ -96,6 +108,33 @@ struct pk_peer_gather {
     unsigned int epoch = 0;
     bool open = false;
 };
+
+int pk_peer_gather_step(pk_peer_gather* g, int64_t rows, int64_t row_floats, int d, pk::PeerOut* po,
+                        float** result) {
+    if (!g || !po || !result) return pfail(PK_ERR_INVALID_ARG, "NULL pointer");
+    if (!g->open) return pfail(PK_ERR_INVALID_ARG, "peer gather not opened (pk_peer_gather_open)");
+    if (g->world > pk::kMaxOutPeers) return pfail(PK_ERR_UNSUPPORTED, "fused exchange: at most 8 ranks");
+    if (rows < 0 || d <= 0 || row_floats <= 0 || row_floats % d)
+        return pfail(PK_ERR_INVALID_ARG, "rows >= 0 and row_floats a positive multiple of d");
+    if (rows * row_floats * g->world * 4 > g->bytes)
+        return pfail(PK_ERR_INVALID_ARG, "result larger than the peer gather's buffers");
+    const unsigned int epoch = ++g->epoch;
+    const int64_t buf = (epoch & 1u) * g->bytes;
+    *po = pk::PeerOut{};
+    po->n = g->world;
+    po->out_H = static_cast<int>(row_floats / d) * g->world;
+    po->rank = g->rank;
+    po->epoch = epoch;
+    for (int r = 0; r < g->world; ++r) {
+        po->out[r] = reinterpret_cast<float*>(g->peer_base[r] + buf) + g->rank * row_floats;
+        po->flag_of[r] = reinterpret_cast<unsigned int*>(g->peer_base[r] + 2 * g->bytes);
+    }
+    po->flags = reinterpret_cast<unsigned int*>(g->base + 2 * g->bytes);
+    po->done = g->done;
+    po->err = g->err;
+    *result = reinterpret_cast<float*>(g->base + buf);
+    return PK_OK;
+}
 
 extern "C" {
 

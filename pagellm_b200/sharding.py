@@ -146,6 +146,37 @@ class PeerHeadGather:
 
         return torch.as_tensor(_CudaArray(res.value, (rows, world * hs, d), "<f4", self), device=out_slice.device)
 
+    def write_and_attend(self, batch, layer: int, q, k, v):
+        """The head-sharded step in one launch: ``batch.write_and_attend(layer, q, k, v)`` over
+        this rank's heads (``q`` [rows, H/world, D], ``k``/``v`` [rows, KVH/world, D], float32
+        CUDA tensors), whose kernel stores every output row into every rank's result and
+        exchanges the completion flags with the other ranks. Returns the [rows, H, D] result
+        (the library's buffer, valid until the call after next). Collective: every rank calls
+        it for the same step, with the same rows."""
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        for t in (q, k, v):
+            if not t.is_cuda or t.dtype != torch.float32:
+                raise ValueError("write_and_attend takes float32 CUDA tensors")
+        world = dist.get_world_size(self.group)
+        rows, hs, d = q.shape
+        nbytes = max(16, rows * world * hs * d * 4)
+        if self._g is None or nbytes > self._bytes:
+            self._setup(nbytes, q.device)
+        q, k, v = (t if t.is_contiguous() else t.contiguous() for t in (q, k, v))
+        res = C.c_void_p()
+        st = torch.cuda.current_stream(q.device).cuda_stream
+        _lib.check(_lib.load().pk_peer_gather_write_and_attend(self._g, batch._b, layer, hs, q.data_ptr(),
+                                                               k.data_ptr(), v.data_ptr(), C.byref(res), st))
+        from .cache.paged import _CudaArray
+
+        return torch.as_tensor(_CudaArray(res.value, (rows, world * hs, d), "<f4", self), device=q.device)
+
     def check(self, stream=None) -> None:
         """Synchronise and raise DeviceTimeout if a peer's slice did not arrive in time."""
         import torch
