@@ -464,10 +464,13 @@ constexpr int64_t kWideMinRows = 64;
 // Time a split-KV CTA loses per unit boundary inside its block range (B200, C2 decode
 // shape): it reloads queries, publishes a partial for the unit it leaves, and the unit it
 // ends in it usually finishes last of that unit's CTAs, so it merges the unit's partials at
-// the end of its run. Per-CTA globaltimer traces showed ~9.5 us (112 us against 102.6 us at
-// equal block counts); a sweep of the cost (5 / 9 / 14 / 20 / 28 us) put the fastest C2 step
-// at 14 us (602k against 596k tok/s at 9), the long-sequence C5 step being indifferent.
-constexpr double kUnitSwitchUs = 14.0;
+// the end of its run. Per-CTA globaltimer traces first showed ~9.5 us (112 us against 102.6 us
+// at equal block counts). Sweeps of the cost (6 / 9 / 11 / 14 / 18 us, three C2 batches and
+// the C5 8- and 4-way shards) put the fastest steps at 11 us once merges had become cheap
+// (C2 98.3 against 99.8 us at 14); pools split into virtual CTAs (few KV heads) were fastest
+// at 14 us (the 8-way head shard of C5: 125.2 against 129.3 us at 11).
+constexpr double kUnitSwitchUs = 11.0;
+constexpr double kUnitSwitchUsVirtual = 14.0;
 
 // The units' blocks (in unit order, prefix sums ub[0..nu]) cut into contiguous CTA ranges,
 // at most n of them. A range costs its blocks plus `switch_cost` blocks per unit boundary
@@ -528,12 +531,14 @@ constexpr double kWideFixedUs = 5.0;          // launch, Q load, epilogue
 constexpr int64_t kWideMinTilesPerCta = 4;    // stream-K shares smaller than this cost more than they save
 constexpr double kSplitKvBytesPerUs = 6.0e6;  // split-KV streaming rate (HBM / L2)
 
-// Unit-boundary cost in blocks for a pool: kUnitSwitchUs of one CTA's share of the
-// split-KV streaming rate (`ctas` CTAs sharing it), over the K+V bytes of one block.
+// Unit-boundary cost in blocks for a pool: kUnitSwitchUs (kUnitSwitchUsVirtual for pools in
+// virtual CTAs) of one CTA's share of the split-KV streaming rate (`ctas` CTAs sharing it),
+// over the K+V bytes of one block.
 int64_t unit_switch_blocks(const pk_pool* P, int64_t ctas) {
     const double cta_rate = kSplitKvBytesPerUs / static_cast<double>(std::max<int64_t>(1, ctas));
     const double blk = static_cast<double>(P->block_bytes()) * 2.0;
-    return std::max<int64_t>(0, std::llround(kUnitSwitchUs * cta_rate / blk));
+    const double us = P->tc_virt > 1 ? kUnitSwitchUsVirtual : kUnitSwitchUs;
+    return std::max<int64_t>(0, std::llround(us * cta_rate / blk));
 }
 
 void plan_shared_prefixes(pk_batch* B, int qmax, int tpt, const std::vector<int>& tc_seqs) {

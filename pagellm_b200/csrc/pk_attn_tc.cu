@@ -542,9 +542,45 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             if (lane == 0) mbar_arrive(vend);
             at_end = __all_sync(0xffffffffu, mbar_wait_bounded(vend, 0u));
         }
+        // The unit's output rows. With the fused head exchange at the end of the range they go
+        // through this warp's share of the idle stage ring, so that every rank receives them as
+        // 16-byte stores in 512-byte runs (rows of a token's g heads are contiguous there);
+        // elsewhere store_rows.
+        auto store_out = [&](const float (&o)[KS][NT][4], const float (&mm)[NT][2], const float (&ll)[NT][2]) {
+            constexpr int Dp = D + 4;  // padded row: a warp's 4 column groups hit different banks
+            const uint32_t share = (static_cast<uint32_t>(p.stages) * 2u * tile_bytes / p.kvh) & ~127u;
+            if (p.peer.n == 0 || !at_end || share < static_cast<uint32_t>(NT * 8 * Dp * 4)) {
+                store_rows<D, NT>(p.out, o, mm, ll, p.lse, nq, g, p.H, row0, h, quad, grp, p.peer);
+                return;
+            }
+            float* tile = reinterpret_cast<float*>(ring + static_cast<size_t>(h) * share);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int col = nt * 8 + 2 * quad + e;
+                    if (col / g >= nq) continue;
+                    const float inv = 1.f / ll[nt][e];
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        tile[col * Dp + mt * 16 + grp] = o[mt][nt][e] * inv;
+                        tile[col * Dp + mt * 16 + grp + 8] = o[mt][nt][2 + e] * inv;
+                    }
+                }
+            __syncwarp();
+            const int n4 = nq * g * (D / 4);
+            for (int i = lane; i < n4; i += 32) {
+                const int col = i / (D / 4);
+                const int d4 = i - col * (D / 4);
+                const float4 v = *reinterpret_cast<const float4*>(tile + col * Dp + d4 * 4);
+                const size_t orow = static_cast<size_t>(row0 + col / g) * p.peer.out_H + h * g + col % g;
+                for (int r = 0; r < p.peer.n; ++r) reinterpret_cast<float4*>(p.peer.out[r] + orow * D)[d4] = v;
+            }
+            __syncwarp();
+        };
         const bool whole = ublk0 >= lo && p.u_blk[u + 1] <= hi;
         if (whole) {
-            store_rows<D, NT>(p.out, acc, m, l, p.lse, nq, g, p.H, row0, h, quad, grp, p.peer);
+            store_out(acc, m, l);
         } else {
             // The partial of (unit u, CTA c, head h): (max, sum) per live column at
             // part_ml[slot][h][col], and the un-normalised O in fragment order interleaved by
@@ -709,7 +745,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 if (arrive_last(p.counters + (static_cast<size_t>(u) + g0) * p.kvh + h, g1 - g0 + 1) &&
                     merge(g0, g1 - g0 + 1, 1)) {
                     if (ngr == 1) {
-                        store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp, p.peer);
+                        store_out(num, mx, den);
                     } else {
                         // the group's partial, in the slot of its first CTA (whose partial the
                         // merge has consumed)
@@ -735,7 +771,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                         }
                         if (arrive_last(p.unit_counters + static_cast<size_t>(u) * p.kvh + h, ngr) &&
                             merge(cf, ngr, kMergeGroup))
-                            store_rows<D, NT>(p.out, num, mx, den, p.lse, nq, g, p.H, row0, h, quad, grp, p.peer);
+                            store_out(num, mx, den);
                     }
                 }
             }
@@ -743,21 +779,18 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
     }
     if (p.peer.n > 0) {
         // Fused head exchange: every consumer warp (with work or not, timed out or not) counts
-        // itself done after a system-scope fence over its rows' stores; the last of the launch
-        // publishes the step's epoch to every rank, one lane per rank, and waits until every
-        // rank's epoch has arrived here (one lane per sender), for at most kWaitLimitNs.
+        // itself done with an acquire-release increment at system scope, which orders its rows'
+        // stores before the count; the last of the launch, which has acquired every other
+        // warp's, publishes the step's epoch to every rank (release stores, one lane per rank)
+        // and waits until every rank's epoch has arrived here (one lane per sender), for at
+        // most kWaitLimitNs.
         __syncwarp();
         int last = 0;
-        if (lane == 0) {
-            __threadfence_system();
-            last = atomicAdd(p.peer.done, 1u) == gridDim.x * static_cast<unsigned int>(nwc) - 1u;
-        }
+        if (lane == 0)
+            last = atom_add_acq_rel_sys(p.peer.done, 1u) == gridDim.x * static_cast<unsigned int>(nwc) - 1u;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-            if (lane == 0) {
-                *p.peer.done = 0;
-                __threadfence_system();
-            }
+            if (lane == 0) *p.peer.done = 0;
             __syncwarp();
             if (lane < p.peer.n) st_release_sys(p.peer.flag_of[lane] + p.peer.rank, p.peer.epoch);
             const unsigned long long t0 = global_ns();

@@ -103,6 +103,15 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
     return v;
 }
 
+// Counter increment with acquire-release semantics at system scope: the caller's earlier
+// stores (to any GPU's memory) are ordered before it, and the stores that other threads
+// ordered before their increments are visible to the caller after it. Returns the old value.
+__device__ __forceinline__ unsigned int atom_add_acq_rel_sys(unsigned int* p, unsigned int v) {
+    unsigned int old;
+    asm volatile("atom.add.acq_rel.sys.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // ---------------------------------------------------------------- TMA (no multicast)
 // 4-D tiled bulk tensor load global -> shared, completion on an mbarrier (tx bytes).
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, int c0, int c1,

@@ -7,11 +7,11 @@
 // step s) and a flag word per sender. One launch per step:
 //   * every thread stores 16-byte pieces of this rank's slice into every rank's current result
 //     buffer, at this rank's head offset (plain peer stores, no multicast);
-//   * each CTA fences at system scope and counts itself done; the last CTA fences once more
-//     and writes the step's epoch into this rank's flag word in every rank's allocation
-//     (release, system scope, one lane per destination), then waits until every rank's flag
-//     word here holds the epoch (acquire, one lane per sender), for at most 1 s of
-//     %globaltimer - after that it records a timeout in the error word and returns.
+//   * each CTA counts itself done (acquire-release increment, system scope); the last CTA
+//     writes the step's epoch into this rank's flag word in every rank's allocation (release,
+//     system scope, one lane per destination), then waits until every rank's flag word here
+//     holds the epoch (acquire, one lane per sender), for at most 1 s of %globaltimer - after
+//     that it records a timeout in the error word and returns.
 // When the launch completes, the local result buffer holds every rank's slice.
 
 #include <algorithm>
@@ -59,20 +59,15 @@ __global__ void __launch_bounds__(256) peer_push_kernel(const PeerParams p) {
     }
     __shared__ int last;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();  // this CTA's stores before its count
-        last = atomicAdd(p.done, 1u) == gridDim.x - 1;
-    }
+    if (threadIdx.x == 0)  // this CTA's stores before its count (acquire-release, system scope)
+        last = pk::atom_add_acq_rel_sys(p.done, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!last || threadIdx.x >= 32) return;
-    // The last CTA's first warp. Every CTA's stores are ordered before its count, so before
-    // the flags: one system-scope fence, then one release store per destination, each on its
-    // own lane (one instruction, not a fence per flag).
+    // The last CTA's first warp: every CTA's stores are ordered before its count, which this
+    // CTA has acquired, so before the flags - one release store per destination, each on its
+    // own lane.
     const int lane = threadIdx.x;
-    if (lane == 0) {
-        *p.done = 0;
-        __threadfence_system();
-    }
+    if (lane == 0) *p.done = 0;
     __syncwarp();
     for (int r = lane; r < p.world; r += 32) pk::st_release_sys(p.flag_of[r] + p.rank, p.epoch);
     // Lane r watches sender r's flag word here; the warp leaves once all have the epoch, or
