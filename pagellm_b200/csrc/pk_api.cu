@@ -279,13 +279,14 @@ struct pk_batch {
     DevBuf qpk;    // packed bf16 query tiles of the wide-tile items (+1 zero tile)
     std::vector<int32_t> u_kb0;    // per unit: first block read (after a shared prefix)
     std::vector<int32_t> u_cta;    // per unit: first and last split-KV CTA of its blocks
+    std::vector<int32_t> u_meta;   // per unit: packed record (TcParams::u_meta)
     std::vector<int32_t> seq_kb0;  // scratch: per sequence
     int tc_max_new = 0;            // most new tokens of a sequence on the split-KV kernel
     DevBuf lse;                    // [rows][H] when shared-prefix items exist
     Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows 8 w_seq
                     // 9 w_tok0 10 w_rows 11 w_ntok 12 w_kend 13 tok_row 14 tok_pos 15 u_kb0
                     // 16 w_pair 17 pair_kend 18 cta_seg 19 seg 20 split 21 cta_blk
-                    // 22 merge counters (zeros) 23 u_cta
+                    // 22 merge counters (zeros) 23 u_cta 24 u_meta
     DevBuf ws;
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
@@ -879,6 +880,21 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
     B->plan.add(B->ctr_zero.data(), B->ctr_zero.size() * 4);  // 22
     if (!B->use_tc) B->u_cta.clear();
     B->plan.add(B->u_cta.data(), B->u_cta.size() * 4);  // 23
+    // packed unit records: {t0, n, kb0, row0}, {qpos0, blk0, blk1, tbase}
+    B->u_meta.resize(8 * static_cast<size_t>(B->nu));
+    for (int u = 0; u < B->nu; ++u) {
+        const int i = B->u_seq[u];
+        int32_t* r = B->u_meta.data() + 8 * static_cast<size_t>(u);
+        r[0] = B->u_t0[u];
+        r[1] = B->u_n[u];
+        r[2] = B->u_kb0[u];
+        r[3] = B->offsets[i] + B->u_t0[u];
+        r[4] = B->starts[i] + B->u_t0[u];
+        r[5] = B->u_blk[u];
+        r[6] = B->u_blk[u + 1];
+        r[7] = B->indptr[i] + B->u_kb0[u] - B->u_blk[u];
+    }
+    B->plan.add(B->u_meta.data(), B->u_meta.size() * 4);  // 24
     if (B->nslots > 0)
         PK_CUDA(B->wpart.reserve(static_cast<size_t>(B->nslots) * 2 * 128 * (128 + 2) * sizeof(float)));
     if (!B->w_seq.empty())
@@ -1064,6 +1080,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.ncta = B->ncta;
         p.cta_blk = B->plan.at<int32_t>(21);
         p.u_cta = B->plan.at<int32_t>(23);
+        p.u_meta = B->nu > 0 ? B->plan.at<int4>(24) : nullptr;
         p.kvh = P->kvh;
         p.g = g;
         p.H = H;

@@ -113,6 +113,39 @@ __device__ __forceinline__ uint32_t tile_off(int chunk, int h, int t, int u16, i
     return static_cast<uint32_t>(row * 128 + ((u16 ^ (row & 7)) << 4));
 }
 
+// One unit's metadata: the plan's packed record (two 16-byte loads, one round trip) when
+// present, else gathered from the per-unit and per-sequence arrays (a chain of dependent
+// loads: unit -> sequence -> its start, row offset and table).
+struct UnitInfo {
+    int t0, n, kb0, row0, qpos0, blk0, blk1, tbase;
+};
+__device__ __forceinline__ UnitInfo load_unit(const TcParams& p, int u) {
+    UnitInfo x;
+    if (p.u_meta != nullptr) {
+        const int4 a = __ldg(p.u_meta + 2 * u);
+        const int4 b = __ldg(p.u_meta + 2 * u + 1);
+        x.t0 = a.x;
+        x.n = a.y;
+        x.kb0 = a.z;
+        x.row0 = a.w;
+        x.qpos0 = b.x;
+        x.blk0 = b.y;
+        x.blk1 = b.z;
+        x.tbase = b.w;
+        return x;
+    }
+    const int seq = p.u_seq[u];
+    x.t0 = p.u_t0[u];
+    x.n = p.u_n[u];
+    x.kb0 = p.u_kb0 != nullptr ? p.u_kb0[u] : 0;
+    x.row0 = p.offsets[seq] + x.t0;
+    x.qpos0 = p.starts[seq] + x.t0;
+    x.blk0 = p.u_blk[u];
+    x.blk1 = p.u_blk[u + 1];
+    x.tbase = p.indptr[seq] + x.kb0 - x.blk0;
+    return x;
+}
+
 // CTAs per first-level group of the two-level merge of a unit's partials.
 constexpr int kMergeGroup = 6;
 
@@ -183,13 +216,12 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             int it = 0;
             bool ok = true;
             for (int j = lo, u = u_first; j < hi && ok; ++u) {
-                const int uend = min(hi, p.u_blk[u + 1]);
-                const int seq = p.u_seq[u];
-                const int kb0 = p.u_kb0 != nullptr ? p.u_kb0[u] : 0;
-                const int tbase = p.indptr[seq] + kb0 - p.u_blk[u];
+                const UnitInfo ui = load_unit(p, u);
+                const int uend = min(hi, ui.blk1);
+                const int tbase = ui.tbase;
                 // the unit's query rows into L2 while its first blocks stream in
-                prefetch_l2_bulk(p.q + static_cast<size_t>(p.offsets[seq] + p.u_t0[u]) * p.H * D,
-                                 static_cast<uint32_t>(p.u_n[u]) * p.H * D * 4u);
+                prefetch_l2_bulk(p.q + static_cast<size_t>(ui.row0) * p.H * D,
+                                 static_cast<uint32_t>(ui.n) * p.H * D * 4u);
                 for (; j < uend; ++j, ++it) {
                     const int s = it % p.stages;
                     const uint32_t k = static_cast<uint32_t>(it / p.stages);
@@ -242,12 +274,11 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 bool issued = false;
                 if (active) {
                     if (fresh) {
-                        uend = min(vhi, p.u_blk[u + 1]);
-                        const int seq = p.u_seq[u];
-                        const int kb0 = p.u_kb0 != nullptr ? p.u_kb0[u] : 0;
-                        tbase = p.indptr[seq] + kb0 - p.u_blk[u];
-                        prefetch_l2_bulk(p.q + static_cast<size_t>(p.offsets[seq] + p.u_t0[u]) * p.H * D,
-                                         static_cast<uint32_t>(p.u_n[u]) * p.H * D * 4u);
+                        const UnitInfo ui = load_unit(p, u);
+                        uend = min(vhi, ui.blk1);
+                        tbase = ui.tbase;
+                        prefetch_l2_bulk(p.q + static_cast<size_t>(ui.row0) * p.H * D,
+                                         static_cast<uint32_t>(ui.n) * p.H * D * 4u);
                         fresh = false;
                     }
                     const int s = it % p.stages;
@@ -301,15 +332,16 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
     int it = 0;
     bool alive = true;
     for (int j = lo, u = u_first; j < hi && alive; ++u) {
-        const int uend = min(hi, p.u_blk[u + 1]);
-        const int ublk0 = p.u_blk[u];
-        const int seq = p.u_seq[u];
-        const int t0 = p.u_t0[u];
-        const int nq = p.u_n[u];
-        const int qpos0 = p.starts[seq] + t0;  // absolute position of the unit's first query
+        const UnitInfo ui = load_unit(p, u);
+        const int ublk1 = ui.blk1;             // the unit's blocks end here (this range may end first)
+        const int uend = min(hi, ublk1);
+        const int ublk0 = ui.blk0;
+        const int t0 = ui.t0;
+        const int nq = ui.n;
+        const int qpos0 = ui.qpos0;            // absolute position of the unit's first query
         const int uctx = qpos0 + nq;           // keys kb0*bs..uctx-1 are read
-        const int kb0 = p.u_kb0 != nullptr ? p.u_kb0[u] : 0;
-        const int row0 = p.offsets[seq] + t0;
+        const int kb0 = ui.kb0;
+        const int row0 = ui.row0;
 
         // Q^T as the B operand: column n = lane/4 of each n8 tile, dims 2*quad(+1), +8.
         // Q's low half (q - bf16(q)) only where registers allow it: with two n8 tiles or
@@ -397,15 +429,15 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             // query rows they are also stores them to the pool (the fused append).
             bool patched = false;
             if (p.k_new != nullptr) {
-                const int s_start = p.starts[seq];
+                const int s_start = qpos0 - t0;  // the sequence's first new position
                 const int lo_pos = max(kpos0, s_start);
                 const int hi_pos = min(kpos0 + p.bs, uctx);
                 if (lo_pos < hi_pos) {
                     patched = true;
                     uint8_t* kgen = ring + s * 2 * tile_bytes;
                     uint8_t* vgen = kgen + tile_bytes;
-                    const int phys = p.ids[p.indptr[seq] + kb0 + (j - ublk0)];
-                    const int row_base = p.offsets[seq] - s_start;
+                    const int phys = p.ids[ui.tbase + j];
+                    const int row_base = row0 - qpos0;  // row of position pos: row_base + pos
                     // (position, 4-dim) items, lane-strided; each batch issues all its loads
                     // (read-only inputs) before any store, so the rows' latencies overlap.
                     constexpr int kPerRow = D / 4;
@@ -537,7 +569,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
         // The last unit of the range: once every consumer warp of the (virtual) CTA is here, no
         // stage of its ring is read or filled any more, and its warps may stage a merge there.
         bool at_end = false;
-        if (p.u_blk[u + 1] >= hi) {
+        if (ublk1 >= hi) {
             __syncwarp();
             if (lane == 0) mbar_arrive(vend);
             at_end = __all_sync(0xffffffffu, mbar_wait_bounded(vend, 0u));
@@ -578,7 +610,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
             }
             __syncwarp();
         };
-        const bool whole = ublk0 >= lo && p.u_blk[u + 1] <= hi;
+        const bool whole = ublk0 >= lo && ublk1 <= hi;
         if (whole) {
             store_out(acc, m, l);
         } else {
@@ -622,7 +654,7 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
                 // the unit's first and last CTA, from the plan (one round trip, no search)
                 const int cf = p.u_cta != nullptr ? p.u_cta[2 * u] : cta_of_block(ublk0, p.total_blocks, p.ncta, p.cta_blk);
                 const int cl = p.u_cta != nullptr ? p.u_cta[2 * u + 1]
-                                                  : cta_of_block(p.u_blk[u + 1] - 1, p.total_blocks, p.ncta, p.cta_blk);
+                                                  : cta_of_block(ublk1 - 1, p.total_blocks, p.ncta, p.cta_blk);
                 const int ngr = (cl - cf + kMergeGroup) / kMergeGroup;
                 const int g0 = cf + (c - cf) / kMergeGroup * kMergeGroup;
                 const int g1 = min(cl, g0 + kMergeGroup - 1);

@@ -65,6 +65,11 @@ struct TcParams {
     // [nu][2] first and last CTA whose range holds blocks of each unit; NULL = searched in
     // cta_blk (read only by the in-kernel merge)
     const int32_t* u_cta;
+    // [nu] packed unit records, two int4 each: {t0, n, kb0, row0}, {qpos0, blk0, blk1, tbase}
+    // (row0 = offsets[seq] + t0, qpos0 = starts[seq] + t0, blk0/blk1 = u_blk[u]/u_blk[u + 1],
+    // tbase = indptr[seq] + kb0 - blk0, so that block j's id is ids[tbase + j]); NULL =
+    // gathered from the arrays above
+    const int4* u_meta;
     int nu;
     int total_blocks;
     int ncta;
