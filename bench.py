@@ -363,7 +363,10 @@ def attention_roofline(w, batch, prof_ms, prof_n, traffic=None):
     """Roofline object for the dominant attention kernel of a step of ``w``."""
     uniq = w.unique_kv_bytes()
     alg = (uniq + w.rows * w.H * w.D * 8 + int(sum(-(-int(L) // w.bs) for L in w.ctx_lens)) * 4 + w.nseq * 12)
-    kind = max((1, 3, 4), key=lambda i: prof_ms[i])
+    # the wide-tile (tensor) kernel whenever the step has one (its split-KV kernel can take as
+    # long on C3, and the line should not flip between HBM and tensor rooflines run to run),
+    # else the longest of the others
+    kind = 4 if prof_n[4] else max((1, 3), key=lambda i: prof_ms[i])
     avg_ms = prof_ms[kind] / max(1, prof_n[kind])
     hbm, hbm_src = peaks()
     achieved = alg / (avg_ms / 1e3) / 1e9
