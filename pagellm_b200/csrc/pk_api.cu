@@ -280,13 +280,14 @@ struct pk_batch {
     std::vector<int32_t> u_kb0;    // per unit: first block read (after a shared prefix)
     std::vector<int32_t> u_cta;    // per unit: first and last split-KV CTA of its blocks
     std::vector<int32_t> u_meta;   // per unit: packed record (TcParams::u_meta)
+    std::vector<int64_t> w_slots;  // per wide-item row (w_rows): its pool slot
     std::vector<int32_t> seq_kb0;  // scratch: per sequence
     int tc_max_new = 0;            // most new tokens of a sequence on the split-KV kernel
     DevBuf lse;                    // [rows][H] when shared-prefix items exist
     Uploader plan;  // 0 u_seq 1 u_t0 2 u_n 3 u_blk 4 sp_u 5 sp_c0 6 sp_c1 7 gen_rows 8 w_seq
                     // 9 w_tok0 10 w_rows 11 w_ntok 12 w_kend 13 tok_row 14 tok_pos 15 u_kb0
                     // 16 w_pair 17 pair_kend 18 cta_seg 19 seg 20 split 21 cta_blk
-                    // 22 merge counters (zeros) 23 u_cta 24 u_meta
+                    // 22 merge counters (zeros) 23 u_cta 24 u_meta 25 w_slots
     DevBuf ws;
     size_t ws_part_o_floats = 0;
     DevBuf io;  // q | k | v | out for the host-buffer entry point
@@ -895,6 +896,16 @@ int build_attention_plan(pk_batch* B, int H, cudaStream_t st) {
         r[7] = B->indptr[i] + B->u_kb0[u] - B->u_blk[u];
     }
     B->plan.add(B->u_meta.data(), B->u_meta.size() * 4);  // 24
+    // pool slots of the wide-item rows, for their append
+    B->w_slots.resize(B->w_rows.size());
+    for (size_t x = 0; x < B->w_rows.size(); ++x) {
+        const int r = B->w_rows[x];
+        const int i = B->row_seq[r];
+        const int64_t pos = static_cast<int64_t>(B->starts[i]) + (r - B->offsets[i]);
+        const int64_t blk = pos / P->block_size;
+        B->w_slots[x] = static_cast<int64_t>(B->ids[B->indptr[i] + blk]) * P->block_size + (pos - blk * P->block_size);
+    }
+    B->plan.add(B->w_slots.data(), B->w_slots.size() * 8);  // 25
     if (B->nslots > 0)
         PK_CUDA(B->wpart.reserve(static_cast<size_t>(B->nslots) * 2 * 128 * (128 + 2) * sizeof(float)));
     if (!B->w_seq.empty())
@@ -1036,6 +1047,7 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
             a.indptr = B->meta.at<int32_t>(0);
             a.ids = B->meta.at<int32_t>(1);
             a.rows = B->plan.at<int32_t>(10);
+            a.slots = B->plan.at<int64_t>(25);
             a.n = static_cast<int64_t>(B->w_rows.size());
             a.rowlen = P->kvh * P->d;
             a.bs = P->block_size;

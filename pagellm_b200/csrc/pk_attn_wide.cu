@@ -803,10 +803,15 @@ __global__ void __launch_bounds__(128) wide_prep_kernel(const WideParams p, int 
         const int64_t r = a.rows[ri];
         const float4 kx = *reinterpret_cast<const float4*>(a.k + r * a.rowlen + c);
         const float4 vx = *reinterpret_cast<const float4*>(a.v + r * a.rowlen + c);
-        const int sq = a.row_seq[r];
-        const int64_t pos = static_cast<int64_t>(a.starts[sq]) + (r - a.offsets[sq]);
-        const int64_t blk = pos / a.bs;
-        const int64_t slot = static_cast<int64_t>(a.ids[a.indptr[sq] + blk]) * a.bs + (pos - blk * a.bs);
+        int64_t slot;
+        if (a.slots != nullptr) {
+            slot = a.slots[ri];  // from the plan: one load instead of a chain of five
+        } else {
+            const int sq = a.row_seq[r];
+            const int64_t pos = static_cast<int64_t>(a.starts[sq]) + (r - a.offsets[sq]);
+            const int64_t blk = pos / a.bs;
+            slot = static_cast<int64_t>(a.ids[a.indptr[sq] + blk]) * a.bs + (pos - blk * a.bs);
+        }
         const int64_t dst = slot * a.rowlen + c;
         *reinterpret_cast<uint2*>(a.pool_k + dst) = make_uint2(pack_bf16(kx.x, kx.y), pack_bf16(kx.z, kx.w));
         *reinterpret_cast<uint2*>(a.pool_v + dst) = make_uint2(pack_bf16(vx.x, vx.y), pack_bf16(vx.z, vx.w));

@@ -214,6 +214,7 @@ struct WideAppend {
     const float* v;
     const int32_t *row_seq, *offsets, *starts, *indptr, *ids;
     const int32_t* rows;  // [n] the step rows to append
+    const int64_t* slots; // [n] their pool slots (layer 0); NULL = looked up from the tables
     int64_t n;
     int rowlen;           // kvh * head_dim
     int bs;
