@@ -146,13 +146,17 @@ class PeerHeadGather:
 
         return torch.as_tensor(_CudaArray(res.value, (rows, world * hs, d), "<f4", self), device=out_slice.device)
 
-    def write_and_attend(self, batch, layer: int, q, k, v):
-        """The head-sharded step in one launch: ``batch.write_and_attend(layer, q, k, v)`` over
-        this rank's heads (``q`` [rows, H/world, D], ``k``/``v`` [rows, KVH/world, D], float32
-        CUDA tensors), whose kernel stores every output row into every rank's result and
-        exchanges the completion flags with the other ranks. Returns the [rows, H, D] result
-        (the library's buffer, valid until the call after next). Collective: every rank calls
-        it for the same step, with the same rows."""
+    def write_and_attend(self, batch, layer: int, q, k, v, fused=None):
+        """The head-sharded step: ``batch.write_and_attend(layer, q, k, v)`` over this rank's
+        heads (``q`` [rows, H/world, D], ``k``/``v`` [rows, KVH/world, D], float32 CUDA
+        tensors) and the exchange of the output slices. ``fused=True``: one launch, the
+        attention kernel stores every output row into every rank's result and exchanges the
+        flags at its end; ``fused=False``: the attention, then one push launch. ``None`` picks
+        by world size from B200 measurements of C5's head-sharded step: fused at 2 ranks
+        (438.6 against 450.9 us), push beyond (8 ranks: 145.4 against 155.8 us, since only the
+        few merging warps issue the fused kernel's tail stores to 8 ranks). Returns the
+        [rows, H, D] result (the library's buffer, valid until the call after next).
+        Collective: every rank calls it for the same step, with the same rows."""
         import ctypes as C
 
         import torch
@@ -164,6 +168,10 @@ class PeerHeadGather:
             if not t.is_cuda or t.dtype != torch.float32:
                 raise ValueError("write_and_attend takes float32 CUDA tensors")
         world = dist.get_world_size(self.group)
+        if fused is None:
+            fused = world <= 2
+        if not fused:
+            return self(batch.write_and_attend(layer, q, k, v))
         rows, hs, d = q.shape
         nbytes = max(16, rows * world * hs * d * 4)
         if self._g is None or nbytes > self._bytes:

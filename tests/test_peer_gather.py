@@ -115,12 +115,15 @@ def _fused_steps(rank, world, dev, pg):
         q = torch.randn((rows, hs, D), generator=gq, device=dev)
         k = torch.randn((rows, kvh, D), generator=gq, device=dev)
         v = torch.randn((rows, kvh, D), generator=gq, device=dev)
-        fused = pg.write_and_attend(batch, layer, q, k, v).clone()
+        fused = pg.write_and_attend(batch, layer, q, k, v, fused=True).clone()
         pg.check()
         slice_ = batch.write_and_attend(layer, q, k, v)  # the same rows appended again: same pool
         sep = pg(slice_).clone()
         pg.check()
         assert torch.equal(fused, sep), (rank, seed)
+        dflt = pg.write_and_attend(batch, layer, q, k, v, fused=False).clone()  # attention + push launch
+        pg.check()
+        assert torch.equal(dflt, sep), (rank, seed)
         assert torch.equal(fused[:, sl.q0:sl.q1], slice_), (rank, seed)
         assert torch.isfinite(fused).all()
         st = batch.stats()
