@@ -234,8 +234,9 @@ PK_API int pk_peer_gather_write_and_attend(pk_peer_gather* gather, pk_batch* bat
  * loading this library holds until exit; a call that needs more, or has more than 512
  * sequences, fails with PK_ERR_INVALID_ARG before launching anything. Every call on a device
  * shares that array and leaves it dirty (the error word is cleared per call): calls that
- * overlap on the GPU race. The first call on a device looks the array's address up - make it
- * before any stream capture. err_dev (required, a device int the caller owns and clears):
+ * overlap on the GPU race. The call uploads from host memory of the call itself, so it cannot be
+ * captured into a CUDA graph: on a capturing stream it returns PK_ERR_UNSUPPORTED before doing
+ * anything. err_dev (required, a device int the caller owns and clears):
  * set to 1 if a bounded device wait gave up, so a timeout is never lost.
  * Pageable table_ids / ctx arrays are copied before return; pinned ones must stay valid until
  * the stream has run the call. */

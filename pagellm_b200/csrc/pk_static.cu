@@ -100,6 +100,15 @@ extern "C" PK_API int pk_decode_attend_static(const pk_pool* pool, int layer, in
     if (!err_dev) return sfail(PK_ERR_INVALID_ARG, "err_dev is NULL (a timed-out wait would go unreported)");
     if ((reinterpret_cast<uintptr_t>(q_dev) | reinterpret_cast<uintptr_t>(out_dev)) & 15u)
         return sfail(PK_ERR_INVALID_ARG, "q and out must be 16-byte aligned");
+    {
+        // its uploads read host memory of this call (the plan is on the stack), which a
+        // captured graph would read again at replay, after it is gone
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cs) != cudaSuccess)
+            return sfail(PK_ERR_CUDA, "cudaStreamIsCapturing failed");
+        if (cs != cudaStreamCaptureStatusNone)
+            return sfail(PK_ERR_UNSUPPORTED, "pk_decode_attend_static cannot be captured into a CUDA graph");
+    }
     const int bs = P.block_size;
 
     // Host-side plan in fixed-size stack arrays: one unit (= one decode row) per sequence.

@@ -165,3 +165,36 @@ def test_static_entry_rejects_oversize_and_missing_error_word_before_launch():
     torch.cuda.synchronize()
     assert float(ob.abs().max()) == 0.0 and float(o4.abs().max()) == 0.0  # nothing was launched
     assert int(err.item()) == 0
+
+
+def test_static_entry_refuses_stream_capture():
+    """The call uploads from its own host memory, which a graph replay would read after it is
+    gone: on a capturing stream it returns PK_ERR_UNSUPPORTED and enqueues nothing."""
+    import torch
+
+    from pagellm_b200 import _lib, workloads
+
+    lib = _lib.load()
+    w = workloads.c2(13, batch=4)
+    pool = _filled_pool(_Shape(1, w.KVH, w.D), w.num_blocks, w.bs, 13)
+    q = torch.randn((w.nseq, w.H, w.D), device="cuda")
+    out = torch.zeros_like(q)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert _static_call(lib, pool, w.H, w.tables, w.ctx_lens, 0, q, out, err) == 0  # eager: fine
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    rc = None
+    with torch.cuda.stream(side):
+        graph.capture_begin()
+        try:
+            rc = _static_call(lib, pool, w.H, w.tables, w.ctx_lens, 0, q, out, err)
+            marker = out.sum()  # something for the graph to hold
+        finally:
+            graph.capture_end()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    assert rc == _lib.PK_ERR_UNSUPPORTED
+    assert "graph" in _lib.last_error()
+    del marker, graph
