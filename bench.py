@@ -50,9 +50,9 @@ METRIC = "decode-attn tokens/s & achieved HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1400.0  # sustained under the power cap
 # dram__bytes_read.sum + dram__bytes_write.sum of one tc_attn_kernel launch on the default
-# C2 workload (620,217,856 + 4,190,464), from an ncu --set full capture of this kernel (one
+# C2 workload (620,258,304 + 6,978,304), from an ncu --set full capture of this kernel (one
 # launch, cold L2); every rank runs the same batch, so it holds at every N
-TC_C2_NCU_TRAFFIC = 624_408_320
+TC_C2_NCU_TRAFFIC = 627_236_608
 TC_C2_NCU_SOURCE = "ncu capture of one tc_attn_kernel launch on this workload (cold L2): dram read + write bytes"
 C5_MIN_STEPS = 200
 RESULT_OUT = sys.stdout
