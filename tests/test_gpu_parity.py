@@ -271,6 +271,25 @@ def test_c5_full_batch_and_head_shards():
         torch.cuda.empty_cache()
 
 
+@pytest.mark.parametrize("D,KVH,g", [(64, 1, 8), (64, 2, 8), (256, 1, 4), (256, 2, 4)])
+def test_few_kv_heads_virtual_ctas(D, KVH, g):
+    """Pools of 1-2 KV heads (head-sharded shards) run V = 8/kvh virtual CTAs per CTA, each with
+    its own block range and stage ring (fewer at head_dim 256, where shared memory runs out):
+    a decode step of 24 long sequences, every row against the oracle, append bit-exact."""
+    from pagellm_b200 import workloads
+
+    rng = np.random.default_rng(D * 10 + KVH)
+    L = rng.integers(200, 3000, size=24).astype(np.int64)
+    need = int(sum(-(-int(x) // 16) for x in L))
+    nb = int(np.ceil(1.25 * need))
+    tables = workloads._scatter_tables(rng, L, 16, nb)
+    w = workloads.Workload("fewkv", g * KVH, KVH, D, 16, "bf16", nb, tables, (L - 1).astype(np.int64),
+                           np.ones(len(L), np.int64))
+    pool, batch, _ = _run_config(w, range(w.nseq))
+    assert pool.tensor_core_path[0], pool.tensor_core_path[1]
+    assert batch.stats()["split_units"] > 0
+
+
 # ----------------------------------------------------------------------------- bit-exact ops
 def test_copy_blocks_bit_exact_and_ordered():
     torch = torch_cuda()
