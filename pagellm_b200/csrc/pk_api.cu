@@ -213,6 +213,7 @@ struct pk_pool {
     int tc_stages = 0;
     size_t tc_smem = 0;
     int tc_virt = 1;  // virtual split-KV CTAs per CTA (8 / kvh for pools of few KV heads)
+    int smem_optin = 0;  // largest dynamic shared memory a CTA may opt in to
     std::string tc_why;
     CUtensorMap tmk{};
     CUtensorMap tmv{};
@@ -408,6 +409,7 @@ void setup_tc(pk_pool* P) {
     if (slots >= (int64_t(1) << 31)) return no("pool has 2^31 slots or more");
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, P->device);
+    P->smem_optin = optin;
     const size_t stage = static_cast<size_t>(2) * P->block_size * P->kvh * P->d * 2;
     // A CTA has one consumer warp per KV head of each of its V virtual CTAs. With few KV heads
     // (the head-sharded layout gives 1-4 per GPU) V = 8 / kvh virtual CTAs - each its own block
@@ -1109,8 +1111,9 @@ int attend_impl(pk_batch* B, int layer, int H, const float* q, float* out, cudaS
         p.pool_k = reinterpret_cast<__nv_bfloat16*>(P->k_layer(layer));
         p.pool_v = reinterpret_cast<__nv_bfloat16*>(P->v_layer(layer));
         p.peer = B->peer_out;
+        const size_t smem = P->tc_smem + (p.peer.n > 0 ? pk::tc_peer_stage_bytes(P->d) : 0);
         PK_CUDA(prof_begin(B, st));
-        PK_CUDA(pk::launch_tc_attention(P->d, B->nt, &P->tmk, &P->tmv, p, P->tc_smem, st));
+        PK_CUDA(pk::launch_tc_attention(P->d, B->nt, &P->tmk, &P->tmv, p, smem, st));
         PK_CUDA(prof_end(B, kProfTc, st));
         B->launches++;
         if (B->nsplit > 0 && p.counters == nullptr) {
@@ -1625,8 +1628,10 @@ int pk_peer_gather_write_and_attend(pk_peer_gather* g, pk_batch* B, int layer, i
         if (rc != PK_OK) return rc;
     }
     const int64_t row_floats = static_cast<int64_t>(n_heads) * P->d;
-    // One split-KV launch writes every output row of such a step: the exchange rides on it.
-    if (B->nrows > 0 && B->use_tc && B->nwide == 0 && B->nprefix == 0 && B->ngeneric == 0) {
+    // One split-KV launch writes every output row of such a step: the exchange rides on it
+    // (if the launch's shared memory has room for the rows' staging).
+    if (B->nrows > 0 && B->use_tc && B->nwide == 0 && B->nprefix == 0 && B->ngeneric == 0 &&
+        P->tc_smem + pk::tc_peer_stage_bytes(P->d) <= static_cast<size_t>(P->smem_optin)) {
         float* res = nullptr;
         rc = pk_peer_gather_step(g, B->nrows, row_floats, P->d, &B->peer_out, &res);
         if (rc != PK_OK) return rc;

@@ -170,6 +170,10 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
     // per consumer warp for the bulk copies of its end-of-range merge
     uint64_t* endbar = empty + V * p.stages;
     uint64_t* mbar_m = endbar + V;
+    // with the fused head exchange on: each consumer warp's 4-row staging area for the rows it
+    // stores to every rank (tc_peer_stage_bytes beyond the pool's usual shared memory)
+    float* peer_stage = reinterpret_cast<float*>(
+        (reinterpret_cast<uintptr_t>(mbar_m + kTcMaxKvHeads) + 15) & ~uintptr_t(15));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -579,36 +583,42 @@ __global__ void __launch_bounds__((kTcMaxKvHeads + 1) * 32, 1)
         // 16-byte stores in 512-byte runs (rows of a token's g heads are contiguous there);
         // elsewhere store_rows.
         auto store_out = [&](const float (&o)[KS][NT][4], const float (&mm)[NT][2], const float (&ll)[NT][2]) {
-            constexpr int Dp = D + 4;  // padded row: a warp's 4 column groups hit different banks
-            const uint32_t share = (static_cast<uint32_t>(p.stages) * 2u * tile_bytes / p.kvh) & ~127u;
-            if (p.peer.n == 0 || !at_end || share < static_cast<uint32_t>(NT * 8 * Dp * 4)) {
+            if (p.peer.n == 0) {
                 store_rows<D, NT>(p.out, o, mm, ll, p.lse, nq, g, p.H, row0, h, quad, grp, p.peer);
                 return;
             }
-            float* tile = reinterpret_cast<float*>(ring + static_cast<size_t>(h) * share);
+            // Every rank receives the rows as whole 512-byte runs of 16-byte stores: 4 rows at a
+            // time go through this warp's staging area (rows padded to D + 4 floats, so that a
+            // warp's column groups hit different banks), then each row leaves contiguously.
+            constexpr int Dp = D + 4;
+            float* tile = peer_stage + static_cast<size_t>(warp) * 4 * Dp;
+            const int ncol = nq * g;
+            for (int c0 = 0; c0 < ncol; c0 += 4) {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
+                for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int col = nt * 8 + 2 * quad + e;
-                    if (col / g >= nq) continue;
-                    const float inv = 1.f / ll[nt][e];
+                    for (int e = 0; e < 2; ++e) {
+                        const int col = nt * 8 + 2 * quad + e;
+                        if (col < c0 || col >= c0 + 4 || col >= ncol) continue;
+                        const float inv = 1.f / ll[nt][e];
 #pragma unroll
-                    for (int mt = 0; mt < KS; ++mt) {
-                        tile[col * Dp + mt * 16 + grp] = o[mt][nt][e] * inv;
-                        tile[col * Dp + mt * 16 + grp + 8] = o[mt][nt][2 + e] * inv;
+                        for (int mt = 0; mt < KS; ++mt) {
+                            tile[(col - c0) * Dp + mt * 16 + grp] = o[mt][nt][e] * inv;
+                            tile[(col - c0) * Dp + mt * 16 + grp + 8] = o[mt][nt][2 + e] * inv;
+                        }
                     }
+                __syncwarp();
+                const int n4 = min(4, ncol - c0) * (D / 4);
+                for (int i = lane; i < n4; i += 32) {
+                    const int lc = i / (D / 4);
+                    const int d4 = i - lc * (D / 4);
+                    const int col = c0 + lc;
+                    const float4 v = *reinterpret_cast<const float4*>(tile + lc * Dp + d4 * 4);
+                    const size_t orow = static_cast<size_t>(row0 + col / g) * p.peer.out_H + h * g + col % g;
+                    for (int r = 0; r < p.peer.n; ++r) reinterpret_cast<float4*>(p.peer.out[r] + orow * D)[d4] = v;
                 }
-            __syncwarp();
-            const int n4 = nq * g * (D / 4);
-            for (int i = lane; i < n4; i += 32) {
-                const int col = i / (D / 4);
-                const int d4 = i - col * (D / 4);
-                const float4 v = *reinterpret_cast<const float4*>(tile + col * Dp + d4 * 4);
-                const size_t orow = static_cast<size_t>(row0 + col / g) * p.peer.out_H + h * g + col % g;
-                for (int r = 0; r < p.peer.n; ++r) reinterpret_cast<float4*>(p.peer.out[r] + orow * D)[d4] = v;
+                __syncwarp();
             }
-            __syncwarp();
         };
         const bool whole = ublk0 >= lo && ublk1 <= hi;
         if (whole) {
@@ -894,6 +904,10 @@ cudaError_t launch_tc_t(const CUtensorMap* tmk, const CUtensorMap* tmv, const Tc
 }
 
 }  // namespace
+
+size_t tc_peer_stage_bytes(int D) {
+    return 16 + static_cast<size_t>(kTcMaxKvHeads) * 4 * (D + 4) * sizeof(float);
+}
 
 size_t tc_smem_bytes(int D, int bs, int kvh, int stages, int virt) {
     // per virtual CTA: stages of K + V blocks, a full and an empty barrier per stage and the

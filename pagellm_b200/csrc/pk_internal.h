@@ -197,6 +197,9 @@ struct PoolView {
 cudaError_t launch_tc_attention(int D, int NT, const CUtensorMap* tmk, const CUtensorMap* tmv,
                                 const TcParams& p, size_t smem, cudaStream_t st);
 size_t tc_smem_bytes(int D, int bs, int kvh, int stages, int virt);
+// Shared memory a launch with the fused head exchange needs beyond tc_smem_bytes (each consumer
+// warp's staging of 4 output rows, and alignment slack).
+size_t tc_peer_stage_bytes(int D);
 cudaError_t launch_merge(const MergeParams& p, int nsplit, cudaStream_t st);
 size_t wide_smem_bytes();
 cudaError_t launch_wide_attention(const CUtensorMap* tmk1, const CUtensorMap* tmv1, const WideParams& p,

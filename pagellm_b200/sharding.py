@@ -153,7 +153,7 @@ class PeerHeadGather:
         attention kernel stores every output row into every rank's result and exchanges the
         flags at its end; ``fused=False``: the attention, then one push launch. ``None`` picks
         by world size from B200 measurements of C5's head-sharded step: fused at 2 ranks
-        (438.6 against 450.9 us), push beyond (8 ranks: 145.4 against 155.8 us, since only the
+        (439.5 against 444.9 us), push beyond (8 ranks: 145.4 against 159.0 us, since only the
         few merging warps issue the fused kernel's tail stores to 8 ranks). Returns the
         [rows, H, D] result (the library's buffer, valid until the call after next).
         Collective: every rank calls it for the same step, with the same rows."""
